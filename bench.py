@@ -1,0 +1,495 @@
+#!/usr/bin/env python
+"""Grouped NVFP4 GEMM benchmark on B200.
+
+Default workload = the headline config (8 groups, M_g ~ U[64, 1024] seeded,
+N=4096, K=7168, NVFP4 x NVFP4 -> bf16).  Other configs: --config dense
+(8192^3) and --config decode (256 groups, M_g ~ U[1, 16], N=7168, K=2048).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line on rank 0.  Under torchrun every rank runs its own
+instance of the workload (weak scaling; no collective on the data path),
+timed between barriers, max over ranks.
+
+  value       TFLOP/s of the public operator call (prepare + GEMM kernels)
+              with inputs resident in HBM, K steps back to back; R rotating
+              input sets whose total exceeds the 126 MB L2 (config.l2)
+  e2e         the same call fed from pinned host buffers: per step H2D of the
+              activation codes + scales, the call, D2H of every output
+  roofline    the GEMM kernel alone (CUDA events around K launches on the
+              launching stream) against 4 x the measured dense bf16 peak
+              (B200's dense FP4 rate is 4x its bf16 rate), or against the
+              measured HBM copy bandwidth for the decode config
+  cpu_baseline  the CPU oracle (dequantise + fp32 matmul, all host threads)
+              on a bounded sample of the same workload, rank 0, N=1
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+L2_BYTES = 126 * 1024 * 1024
+
+
+# ------------------------------------------------------------------ workloads
+def workload(name: str, seed: int = 0) -> dict:
+    rng = np.random.default_rng(seed)
+    if name == "grouped":
+        ms = [int(v) for v in rng.integers(64, 1025, size=8)]
+        return dict(name="grouped", desc="8 groups, M_g~U[64,1024] seed 0, N=4096, K=7168",
+                    m=ms, n=4096, k=7168, w_std=1.0, bound="tensor")
+    if name == "dense":
+        return dict(name="dense", desc="single group M=N=K=8192", m=[8192], n=8192, k=8192,
+                    w_std=1.0, bound="tensor")
+    if name == "decode":
+        ms = [int(v) for v in rng.integers(1, 17, size=256)]
+        return dict(name="decode", desc="256 groups, M_g~U[1,16] seed 0, N=7168, K=2048",
+                    m=ms, n=7168, k=2048, w_std=0.02, bound="hbm")
+    raise SystemExit(f"unknown config {name}")
+
+
+def flops(wl) -> float:
+    return 2.0 * sum(wl["m"]) * wl["n"] * wl["k"]
+
+
+def alg_bytes(wl) -> float:
+    """Algorithmic HBM bytes of one call: read A codes+scales, B codes+scales,
+    write C (bf16)."""
+    n, k, G = wl["n"], wl["k"], len(wl["m"])
+    sm = sum(wl["m"])
+    return sm * (k / 2 + k / 16) + G * n * (k / 2 + k / 16) + sm * n * 2
+
+
+def set_bytes(wl) -> float:
+    return alg_bytes(wl)
+
+
+# ------------------------------------------------------------------ helpers
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16": float(d["bf16_tflops"]), "bf16_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "hbm": float(d["hbm_gbs"]), "src": "measured"}
+    return {"bf16": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def max_over_ranks(x: float, ws: int, dev) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws: int):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ inputs
+def make_set(wl, seed: int, dev):
+    """One input set on the device: N(0,1) activations and N(0, w_std) weights,
+    each quantised to NVFP4 with its own global scale by the device quantiser."""
+    import ratchet_b200 as rb
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    n, k = wl["n"], wl["k"]
+    A, ASF, B, BSF, alpha = [], [], [], [], []
+    for m in wl["m"]:
+        x = torch.randn((m, k), generator=gen, device=dev, dtype=torch.float32)
+        w = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32) * wl["w_std"]
+        qa, sa, ga = rb.quantize_nvfp4(x)
+        qb, sb, gb = rb.quantize_nvfp4(w)
+        del x, w
+        A.append(qa)
+        ASF.append(sa)
+        B.append(qb)
+        BSF.append(sb)
+        alpha.append(ga * gb)
+    return dict(a=A, a_sf=ASF, b=B, b_sf=BSF, alpha=torch.stack(alpha).float(),
+                sizes=[(m, n, k) for m in wl["m"]])
+
+
+def time_value(sets, steps, warmup, dev, ws):
+    import ratchet_b200 as rb
+
+    R = len(sets)
+    call = lambda s: rb.nvfp4_grouped_gemm(s["a"], s["a_sf"], s["b"], s["b_sf"], s["sizes"],
+                                           s["alpha"])
+    for i in range(warmup):
+        call(sets[i % R])
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        call(sets[i % R])
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    rb.last_status()
+    return e0.elapsed_time(e1) / steps
+
+
+def time_kernel_only(sets, steps, dev):
+    """Average duration of the GEMM kernel alone: each set prepared once, then
+    K launches of the GEMM half on rotating sets, events on the launch stream."""
+    import ratchet_b200 as rb
+    from ratchet_b200 import _lib, ops
+
+    L = _lib.lib()
+    st = torch.cuda.current_stream()
+    handles = []
+    for s in sets:
+        pack = rb.pack_weights(s["b"], s["b_sf"])
+        G = len(s["a"])
+        n, k = pack.n, pack.k
+        ms = [int(t.shape[0]) for t in s["a"]]
+        out = torch.empty((sum(ms), n), dtype=torch.bfloat16, device=dev)
+        m_arr = np.asarray(ms, dtype=np.int32)
+        pa = ops._ptr_array([t.view(torch.uint8) for t in s["a"]])
+        psf = ops._ptr_array([t.view(torch.uint8) for t in s["a_sf"]])
+        prob = _lib.FggNvfp4Problem(G, n, k, m_arr.ctypes.data, pa.ctypes.data, psf.ctypes.data,
+                                    s["alpha"].data_ptr(), out.data_ptr())
+        nbytes = int(L.fgg_nvfp4_workspace_bytes(prob))
+        wsb = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        _lib.check(L.fgg_nvfp4_prepare(prob, wsb.data_ptr(), nbytes, st.cuda_stream), "prepare")
+        handles.append((prob, pack, wsb, nbytes, out, m_arr, pa, psf))
+    for i in range(3):
+        prob, pack, wsb, nb = handles[i % len(handles)][:4]
+        _lib.check(L.fgg_nvfp4_gemm(prob, pack.buf.data_ptr(), wsb.data_ptr(), nb, st.cuda_stream), "gemm")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        prob, pack, wsb, nb = handles[i % len(handles)][:4]
+        _lib.check(L.fgg_nvfp4_gemm(prob, pack.buf.data_ptr(), wsb.data_ptr(), nb, st.cuda_stream), "gemm")
+    e1.record(st)
+    torch.cuda.synchronize()
+    for h in handles:
+        rc = L.fgg_read_device_status(h[2].data_ptr(), st.cuda_stream)
+        _lib.check(rc, "kernel-only status")
+    return e0.elapsed_time(e1) / steps
+
+
+def time_e2e(sets, steps, warmup, dev, ws):
+    """Public API fed from pinned host memory: H2D of activations, the call,
+    D2H of the outputs, all inside the timed region."""
+    import ratchet_b200 as rb
+
+    R = len(sets)
+    host = []
+    for s in sets:
+        ha = [t.view(torch.uint8).cpu().pin_memory() for t in s["a"]]
+        hs = [t.view(torch.uint8).cpu().pin_memory() for t in s["a_sf"]]
+        da = [torch.empty_like(t) for t in ha]
+        ds = [torch.empty_like(t) for t in hs]
+        da = [t.to(dev) for t in da]
+        ds = [t.to(dev) for t in ds]
+        sm = sum(t.shape[0] for t in ha)
+        hout = torch.empty((sm, s["sizes"][0][1]), dtype=torch.bfloat16).pin_memory()
+        host.append((ha, hs, da, ds, hout))
+    h2d = sum(t.numel() for t in host[0][0]) + sum(t.numel() for t in host[0][1])
+    d2h = host[0][4].numel() * 2
+
+    def step(i):
+        s = sets[i % R]
+        ha, hs, da, ds, hout = host[i % R]
+        for x, y in zip(da, ha):
+            x.copy_(y, non_blocking=True)
+        for x, y in zip(ds, hs):
+            x.copy_(y, non_blocking=True)
+        outs = rb.nvfp4_grouped_gemm(da, [t.view(torch.float8_e4m3fn) for t in ds], s["b"],
+                                     s["b_sf"], s["sizes"], s["alpha"])
+        r = 0
+        for o in outs:
+            hout[r:r + o.shape[0]].copy_(o, non_blocking=True)
+            r += o.shape[0]
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(ws)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier(ws)
+    return e0.elapsed_time(e1) / steps, h2d, d2h
+
+
+def cpu_sample(wl, budget_s: float = 20.0, seed: int = 1234):
+    """The CPU oracle on a bounded sample of the workload: whole groups,
+    dequantise (torch CPU) + fp32 matmul, until ~budget_s of work is timed."""
+    from oracle import nvfp4 as ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(seed)
+    n, k = wl["n"], wl["k"]
+    t_total, f_total, groups = 0.0, 0.0, 0
+    for gi, m in enumerate(wl["m"]):
+        # the CPU cost does not depend on the values: random codes and scales
+        qa, sa, qb, sb = _random_codes(rng, m, n, k)
+        ga = gb = np.float32(1.0 / 2688.0)
+        t0 = time.perf_counter()
+        a = ref.nvfp4_dequantize_torch(qa, sa)
+        b = ref.nvfp4_dequantize_torch(qb, sb)
+        c = ((a @ b.T) * float(ga * gb)).to(torch.bfloat16)
+        t_total += time.perf_counter() - t0
+        f_total += 2.0 * m * n * k
+        groups += 1
+        del c
+        if t_total >= budget_s or groups >= len(wl["m"]):
+            break
+    return {"value": f_total / t_total / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{groups} of {len(wl['m'])} groups (N={n}, K={k}): torch-CPU dequantise "
+                      f"+ fp32 matmul + bf16, {t_total:.2f} s timed"}
+
+
+def _random_codes(rng, m, n, k):
+    """Random NVFP4 codes and E4M3 scales (bytes 0x30..0x5F, values 0.75..28)."""
+    qa = torch.from_numpy(rng.integers(0, 256, size=(m, k // 2), dtype=np.uint8))
+    sa = torch.from_numpy(rng.integers(0x30, 0x60, size=(m, k // 16), dtype=np.uint8))
+    qb = torch.from_numpy(rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8))
+    sb = torch.from_numpy(rng.integers(0x30, 0x60, size=(n, k // 16), dtype=np.uint8))
+    return qa, sa, qb, sb
+
+
+def traffic_from_profiles(config: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get(config)
+        except json.JSONDecodeError:
+            return None
+    return None
+
+
+# ------------------------------------------------------------------ arms
+def run_reference(args, wl):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import nvfp4 as ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(0)
+    n, k = wl["n"], wl["k"]
+    G = len(wl["m"])
+    data = []
+    for gi in range(min(G, 4)):
+        m = wl["m"][gi]
+        qa, sa, qb, sb = _random_codes(rng, m, n, k)
+        data.append((m, qa, sa, qb, sb, float(np.float32(1.0 / 2688.0) ** 2)))
+
+    def step(i):
+        m, qa, sa, qb, sb, al = data[i % len(data)]
+        a = ref.nvfp4_dequantize_torch(qa, sa)
+        b = ref.nvfp4_dequantize_torch(qb, sb)
+        ((a @ b.T) * al).to(torch.bfloat16)
+        return 2.0 * m * n * k
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    fl = 0.0
+    for i in range(args.steps):
+        fl += step(i)
+    dt = time.perf_counter() - t0
+    val = fl / dt / 1e12
+    line = {
+        "impl": "reference", "metric": "grouped-GEMM TFLOPS", "value": val, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (dequantised NVFP4)", "data": "synthetic",
+        "config": {"workload": wl["desc"], "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": "each step one whole group (cycling over the first "
+                                   f"{len(data)} groups): dequantise + fp32 matmul + bf16"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, wl):
+    ws, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import ratchet_b200 as rb  # noqa: F401  (fails loudly without the native library)
+
+    seed0 = 1000 * rank
+    per_set = set_bytes(wl)
+    R = max(1, min(8, int(np.ceil(2.0 * L2_BYTES / per_set)) + (1 if per_set < L2_BYTES else 0)))
+    sets = [make_set(wl, seed0 + s, dev) for s in range(R)]
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms = time_value(sets, args.steps, args.warmup, dev, ws)
+    clocks = sampler.stop()
+    ms = max_over_ranks(ms, ws, dev)
+    fl = flops(wl)
+    value = fl * ws / (ms * 1e-3) / 1e12
+
+    k_ms = time_kernel_only(sets, args.steps, dev)
+    k_ms = max_over_ranks(k_ms, ws, dev)
+    pk = peaks()
+    if wl["bound"] == "tensor":
+        achieved = fl / (k_ms * 1e-3) / 1e12
+        peak = 4.0 * pk["bf16"]
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": traffic_from_profiles(wl["name"]),
+                "peak_basis": f"4 x {pk['src']} dense bf16 ({pk['bf16']:.0f} TF/s)",
+                "kernel_ms": k_ms, "alg_bytes": alg_bytes(wl)}
+    else:
+        achieved = alg_bytes(wl) / (k_ms * 1e-3) / 1e9
+        peak = pk["hbm"]
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": traffic_from_profiles(wl["name"]),
+                "peak_basis": f"{pk['src']} HBM copy", "kernel_ms": k_ms,
+                "alg_bytes": alg_bytes(wl)}
+
+    e2e_ms, h2d, d2h = time_e2e(sets, max(3, args.steps // 2), min(args.warmup, 3), dev, ws)
+    e2e_ms = max_over_ranks(e2e_ms, ws, dev)
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = cpu_sample(wl)
+
+    if rank == 0:
+        line = {
+            "metric": "grouped-GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "nvfp4 (e2m1 x e2m1, e4m3/16 scales, fp32 acc, bf16 out)",
+            "data": "synthetic (seeded N(0,1) activations, N(0,w_std) weights, NVFP4-quantised)",
+            "config": {"workload": wl["desc"], "groups": len(wl["m"]), "sum_m": sum(wl["m"]),
+                       "n": wl["n"], "k": wl["k"], "parallelism": f"replicas x{ws}",
+                       "l2": f"{R} rotating input sets of {per_set / 1e6:.0f} MB (> L2 in total)"},
+            "clocks": clocks,
+            "e2e": {"value": fl * ws / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": 2 * args.steps,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["grouped", "dense", "decode"], default="grouped")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    wl = workload(args.config)
+    if args.impl == "reference":
+        return run_reference(args, wl)
+    return run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

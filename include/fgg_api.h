@@ -1,0 +1,185 @@
+/*
+ * fgg_api.h - C ABI of the B200 (sm_100a) block-scaled FP4 grouped GEMM.
+ *
+ * Every entry point takes plain pointers and sizes; no framework types cross
+ * this boundary.  Device buffers are owned by the caller.  Calls are
+ * stream-ordered on the `stream` argument (a cudaStream_t passed as void*,
+ * NULL = legacy default stream) and never synchronise the host, except
+ * fgg_read_device_status, which exists to do exactly that.
+ *
+ * Two operator families share one tcgen05 engine:
+ *
+ *  1. NVFP4 x NVFP4 grouped GEMM with per-group operand lists (the operator
+ *     the benchmark configs describe).  Semantics, for every group g:
+ *        C_g[m, n] = alpha_g * sum_k deq(A_g)[m, k] * deq(B_g)[n, k]
+ *        deq(X)[r, k] = e2m1(code(X, r, k)) * e4m3(sf(X)[r, k / 16])
+ *     with codes packed two per byte (element 2j in the LOW nibble of byte j),
+ *     one E4M3 scale per 16 contiguous K elements, fp32 accumulation, bf16
+ *     output.  alpha_g is the product of the two per-tensor fp32 global
+ *     (decode) scales.  The reference repository has no NVFP4 Blackwell kernel;
+ *     these entry points replace the operator described by its benchmark card
+ *     and restate the NVFP4 decode used by
+ *     tasks/muse_prefill_boundary/reference/submission.py:538-549 and :1847-1880
+ *     (e2m1 code x e4m3 block scale x fp32 global scale).
+ *
+ *  2. MXFP8 x MXFP4 M-grouped GEMM with contiguous grouping (m_indices), the
+ *     exact operator of kernels/gemm/fp4_grouped_gemm/b200/kernel.py:2788-2862
+ *     (`fp4_grouped_gemm(a, a_sf, b, b_sf, m_indices) -> c`).
+ *
+ * Return codes are FGG_OK (0) or one of the FGG_E* values below;
+ * fgg_last_error_detail() gives a message for the calling thread's last
+ * failure.
+ */
+#ifndef FGG_API_H
+#define FGG_API_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FGG_OK = 0,
+  FGG_EINVAL = 1,      /* null pointer, negative size, too many groups        */
+  FGG_EBADSHAPE = 2,   /* N % 128 != 0, K % 64 != 0, K < 64, ...               */
+  FGG_EALIGN = 3,      /* a device pointer is not 16-byte aligned             */
+  FGG_EWORKSPACE = 4,  /* workspace / weight pack smaller than required        */
+  FGG_ECUDA = 5,       /* a CUDA runtime call failed                           */
+  FGG_ETIMEOUT = 6,    /* a device-side wait hit its time limit (see status)   */
+  FGG_EARCH = 7        /* the current device is not an sm_100 part             */
+};
+
+/* Largest number of groups one call accepts (per-group metadata travels as
+ * kernel parameters). */
+#define FGG_MAX_GROUPS 512
+
+const char* fgg_error_string(int code);
+const char* fgg_last_error_detail(void);
+/* Library build identifier ("fgg <version> sm_100a"). */
+const char* fgg_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* NVFP4 x NVFP4 grouped GEMM                                                */
+/* ------------------------------------------------------------------------ */
+
+/* Expert / group weights.  B_g codes: [N, K/2] uint8, row-major.  B_g scales:
+ * [N, K/16] E4M3 bytes, row-major.  All groups share N and K. */
+typedef struct FggNvfp4Weights {
+  int32_t num_groups;
+  int32_t n;
+  int32_t k;
+  const void* const* b;     /* host array [G] of device pointers */
+  const void* const* b_sf;  /* host array [G] of device pointers */
+} FggNvfp4Weights;
+
+/* Size of the device buffer fgg_nvfp4_pack_weights fills: per-group TMA
+ * descriptors plus the scales repacked into the MMA's 512-byte SF atoms.
+ * Replaces the identity-cached host repack `_prepare` / `_pack_sf_wgt` of
+ * kernels/gemm/fp4_grouped_gemm/b200/kernel.py:2709-2786, done on the device. */
+size_t fgg_nvfp4_weight_pack_bytes(int32_t num_groups, int32_t n, int32_t k);
+int fgg_nvfp4_pack_weights(const FggNvfp4Weights* w, void* pack, size_t pack_bytes,
+                           void* stream);
+
+/* One grouped GEMM call.  A_g codes [M_g, K/2] uint8; A_g scales [M_g, K/16]
+ * E4M3; alpha: device fp32 [G]; out: device bf16 [sum_g M_g, N] where group g
+ * occupies rows [sum_{h<g} M_h, sum_{h<=g} M_h).  M_g may be 0. */
+typedef struct FggNvfp4Problem {
+  int32_t num_groups;
+  int32_t n;
+  int32_t k;
+  const int32_t* m;         /* host array [G] */
+  const void* const* a;     /* host array [G] of device pointers */
+  const void* const* a_sf;  /* host array [G] of device pointers */
+  const float* alpha;       /* device array [G] */
+  void* out;                /* device bf16 */
+} FggNvfp4Problem;
+
+/* Scratch the call needs (token-scale repack, per-group descriptors, tile
+ * list, status words).  Replaces the per-call part of `_prepare`
+ * (kernels/gemm/fp4_grouped_gemm/b200/kernel.py:2751-2786). */
+size_t fgg_nvfp4_workspace_bytes(const FggNvfp4Problem* p);
+/* Replaces `fp4_grouped_gemm` (kernel.py:2788-2862) for the NVFP4 format:
+ * validates, repacks the token scales, builds descriptors and launches the
+ * persistent tcgen05 kernel.  `pack` must come from fgg_nvfp4_pack_weights
+ * for the same G, N, K. */
+int fgg_nvfp4_grouped_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace,
+                           size_t ws_bytes, void* stream);
+/* The two halves of fgg_nvfp4_grouped_gemm, for callers that replay one
+ * problem (same pointers, same sizes) many times, e.g. inside a CUDA graph:
+ * fgg_nvfp4_prepare fills `workspace` (descriptors, token-scale repack, tile
+ * list); fgg_nvfp4_gemm launches the GEMM kernel on a prepared workspace and
+ * may be repeated.  The token scales must not change between the two. */
+int fgg_nvfp4_prepare(const FggNvfp4Problem* p, void* workspace, size_t ws_bytes, void* stream);
+int fgg_nvfp4_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace, size_t ws_bytes,
+                   void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* MXFP8 x MXFP4 contiguous M-grouped GEMM (reference operator)              */
+/* ------------------------------------------------------------------------ */
+
+/* Mirrors kernel.py:2788-2795 argument for argument:
+ *   a         [M_total, K]     float8_e4m3fn
+ *   a_sf      [M_total, K/128] fp32, powers of two (UE8M0-representable)
+ *   b         [G, N, K/2]      uint8, packed e2m1 pairs
+ *   b_sf      [G, N, K/32]     fp32, powers of two
+ *   m_indices [M_total]        int32 expert id per row, -1 = padding
+ *   c         [M_total, N]     bf16 output
+ * Every expert segment starts at a multiple of 224 rows (kernel.py:28-33).
+ * Shape rules follow kernel.py:2808-2824: N % 128 == 0, K % 128 == 0. */
+typedef struct FggMxProblem {
+  int32_t m_total;
+  int32_t n;
+  int32_t k;
+  int32_t num_groups;
+  const void* a;
+  const float* a_sf;
+  const void* b;
+  const float* b_sf;
+  const int32_t* m_indices;
+  void* c;
+  /* 1: `workspace` already holds the repacked scales and tile list of an
+   * earlier call on the same a_sf / b_sf / m_indices (the identity-keyed cache
+   * of kernel.py:2743-2786); the call then launches the GEMM alone. */
+  int32_t reuse_prepared;
+} FggMxProblem;
+
+/* Scratch for the MX call (repacked UE8M0 scales, block->expert table,
+ * descriptors, status): kernel.py:2679-2786 done on the device per call. */
+size_t fgg_mx_workspace_bytes(const FggMxProblem* p);
+int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
+                        void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* NVFP4 quantisation (activations and weights)                              */
+/* ------------------------------------------------------------------------ */
+
+/* amax of |x| over `count` elements into *amax_out (device fp32).
+ * x_dtype: 0 = fp32, 1 = bf16. */
+int fgg_amax(const void* x, int32_t x_dtype, int64_t count, float* amax_out, void* stream);
+
+/* Quantise a row-major [rows, k] tensor to NVFP4:
+ *   gs   = 2688 / amax (1 if amax == 0)            (device scalar, fp32)
+ *   s    = e4m3_rn_satfinite((blockmax / 6) * gs)    per 16 elements
+ *   q    = e2m1_rne(x * (gs / float(s)))             (0 where s == 0)
+ * codes [rows, k/2] uint8 (element 2j in the low nibble), sf [rows, k/16] E4M3.
+ * `amax` is a device fp32 scalar (from fgg_amax or supplied by the caller). */
+int fgg_nvfp4_quantize(const void* x, int32_t x_dtype, int64_t rows, int32_t k,
+                       const float* amax, void* codes, void* sf, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Status                                                                    */
+/* ------------------------------------------------------------------------ */
+
+/* Synchronises `stream`, then reads the status word a previous GEMM call left
+ * in `workspace` (the NVFP4 or MX workspace).  Returns FGG_OK, FGG_ETIMEOUT
+ * (a device wait ran out; the kernel stopped early and its output is
+ * incomplete) or FGG_ECUDA. */
+int fgg_read_device_status(const void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FGG_API_H */

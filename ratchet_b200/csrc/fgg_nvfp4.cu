@@ -1,0 +1,480 @@
+// fgg_nvfp4.cu - NVFP4 x NVFP4 grouped GEMM entry points (per-group lists).
+//
+// Per call:
+//   1. nvfp4_prepare_kernel  per-group TMA descriptors for the token tensors
+//                            (edited on the device from one host-encoded
+//                            template), the token scales repacked into 512-byte
+//                            SF atoms, the flat tile list, status reset.
+//   2. fgg_gemm_kernel<NVFP4 cfg>  (fgg_engine.cuh).
+// Weights are packed once by nvfp4_pack_weights_kernel (descriptors + SF
+// atoms) and cached by the caller, as kernel.py:2743-2786 caches its repack.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "fgg_engine.cuh"
+#include "fgg_host.cuh"
+
+namespace fgg {
+
+// ------------------------------------------------------- prepare kernels
+struct PrepParams {
+  CUtensorMap tmpl;  // token descriptor template (group 0's geometry)
+  const uint8_t* a[FGG_MAX_GROUPS];
+  const uint8_t* a_sf[FGG_MAX_GROUPS];
+  int32_t m[FGG_MAX_GROUPS];
+  int32_t xtile_begin[FGG_MAX_GROUPS + 1];
+  int32_t tile_begin[FGG_MAX_GROUPS + 1];
+  int32_t out_row[FGG_MAX_GROUPS];
+  CUtensorMap* tmap_out;
+  GroupInfo* ginfo_out;
+  uint32_t* tiles_out;
+  uint8_t* sfx_out;
+  int* status;
+  int32_t g, k, bn, ch, nk64p, nt, num_tiles, xt_total;
+  int32_t blocks_tmap, blocks_tiles;
+};
+
+__device__ __forceinline__ int find_group(const int32_t* begin, int g_count, int x) {
+  int lo = 0, hi = g_count;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (begin[mid] <= x)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(256) nvfp4_prepare_kernel(const __grid_constant__ PrepParams p) {
+  __shared__ alignas(128) CUtensorMap smap[8];
+  __shared__ int32_t sbegin[FGG_MAX_GROUPS + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int blk = blockIdx.x;
+  if (blk < p.blocks_tmap) {
+    if (blk == 0 && threadIdx.x == 0) {
+      p.status[0] = 0;
+      p.status[1] = 0;
+      p.status[2] = 0;
+    }
+    const int g = blk * 8 + warp;
+    if (g < p.g) {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(&p.tmpl);
+      reinterpret_cast<uint32_t*>(&smap[warp])[lane] = src[lane];
+      __syncwarp();
+      if (lane == 0) {
+        tmap_replace_address(smem_u32(&smap[warp]), reinterpret_cast<uint64_t>(p.a[g]));
+        tmap_replace_dim1(smem_u32(&smap[warp]), max(p.m[g], 1));
+        GroupInfo gi;
+        gi.m = p.m[g];
+        gi.out_row = p.out_row[g];
+        gi.xtile_begin = p.xtile_begin[g];
+        gi.xtiles = p.xtile_begin[g + 1] - p.xtile_begin[g];
+        p.ginfo_out[g] = gi;
+      }
+      __syncwarp();
+      tmap_publish(p.tmap_out + g, smem_u32(&smap[warp]));
+    }
+    return;
+  }
+  blk -= p.blocks_tmap;
+  if (blk < p.blocks_tiles) {
+    for (int i = threadIdx.x; i <= p.g; i += blockDim.x) sbegin[i] = p.tile_begin[i];
+    __syncthreads();
+    const int t = blk * blockDim.x + threadIdx.x;
+    if (t < p.num_tiles) {
+      const int g = find_group(sbegin, p.g, t);
+      const int local = t - sbegin[g];
+      const int xts = p.xtile_begin[g + 1] - p.xtile_begin[g];
+      p.tiles_out[t] = pack_tile(g, local / xts, local % xts);
+    }
+    return;
+  }
+  blk -= p.blocks_tiles;
+  // Token scales -> SF atoms.  One thread writes one 16-byte atom row:
+  //   atom byte (r % 32) * 16 + (r / 32) * 4 + b  <-  sf[row r][4 j + b]
+  for (int i = threadIdx.x; i <= p.g; i += blockDim.x) sbegin[i] = p.xtile_begin[i];
+  __syncthreads();
+  const int64_t line = int64_t(blk) * blockDim.x + threadIdx.x;
+  const int64_t lines_per_xt = int64_t(p.nk64p) * p.ch * 32;
+  if (line >= int64_t(p.xt_total) * lines_per_xt) return;
+  const int X = int(line / lines_per_xt);
+  const int rem = int(line - int64_t(X) * lines_per_xt);
+  const int j = rem / (p.ch * 32);
+  const int c = (rem / 32) % p.ch;
+  const int r0 = rem & 31;
+  const int g = find_group(sbegin, p.g, X);
+  const int xt = X - sbegin[g];
+  const int kq = p.k / 16;
+  uint32_t v[4];
+#pragma unroll
+  for (int r1 = 0; r1 < 4; ++r1) {
+    const int rr = c * 128 + r1 * 32 + r0;
+    const int row = xt * p.bn + rr;
+    v[r1] = 0u;
+    if (rr < p.bn && row < p.m[g] && 4 * j < kq)
+      v[r1] = __ldg(reinterpret_cast<const uint32_t*>(p.a_sf[g] + size_t(row) * kq + 4 * j));
+  }
+  uint4* dst = reinterpret_cast<uint4*>(p.sfx_out + (size_t(X) * p.nk64p + j) * (p.ch * 512u) +
+                                        size_t(c) * 512u + size_t(r0) * 16u);
+  *dst = make_uint4(v[0], v[1], v[2], v[3]);
+}
+
+struct PackParams {
+  CUtensorMap tmpl;
+  const uint8_t* b[FGG_MAX_GROUPS];
+  const uint8_t* b_sf[FGG_MAX_GROUPS];
+  PackHeader* header;
+  CUtensorMap* tmap_out;
+  uint8_t* sfw_out;
+  int32_t g, n, k, nk64p, nt;
+  int32_t blocks_tmap;
+};
+
+__global__ void __launch_bounds__(256) nvfp4_pack_weights_kernel(const __grid_constant__ PackParams p) {
+  __shared__ alignas(128) CUtensorMap smap[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int blk = blockIdx.x;
+  if (blk < p.blocks_tmap) {
+    if (blk == 0 && threadIdx.x == 0) {
+      PackHeader h;
+      h.magic = kPackMagic;
+      h.g = p.g;
+      h.n = p.n;
+      h.k = p.k;
+      *p.header = h;
+    }
+    const int g = blk * 8 + warp;
+    if (g < p.g) {
+      reinterpret_cast<uint32_t*>(&smap[warp])[lane] =
+          reinterpret_cast<const uint32_t*>(&p.tmpl)[lane];
+      __syncwarp();
+      if (lane == 0) tmap_replace_address(smem_u32(&smap[warp]), reinterpret_cast<uint64_t>(p.b[g]));
+      __syncwarp();
+      tmap_publish(p.tmap_out + g, smem_u32(&smap[warp]));
+    }
+    return;
+  }
+  blk -= p.blocks_tmap;
+  const int64_t line = int64_t(blk) * blockDim.x + threadIdx.x;
+  const int64_t total = int64_t(p.g) * p.nt * p.nk64p * 32;
+  if (line >= total) return;
+  const int r0 = int(line & 31);
+  int64_t rest = line >> 5;
+  const int j = int(rest % p.nk64p);
+  rest /= p.nk64p;
+  const int nt = int(rest % p.nt);
+  const int g = int(rest / p.nt);
+  const int kq = p.k / 16;
+  uint32_t v[4];
+#pragma unroll
+  for (int r1 = 0; r1 < 4; ++r1) {
+    const int row = nt * 128 + r1 * 32 + r0;
+    v[r1] = (4 * j < kq)
+                ? __ldg(reinterpret_cast<const uint32_t*>(p.b_sf[g] + size_t(row) * kq + 4 * j))
+                : 0u;
+  }
+  uint4* dst = reinterpret_cast<uint4*>(p.sfw_out + ((size_t(g) * p.nt + nt) * p.nk64p + j) * 512u +
+                                        size_t(r0) * 16u);
+  *dst = make_uint4(v[0], v[1], v[2], v[3]);
+}
+
+// ------------------------------------------------------------ host side
+using CfgPrefill = EngineCfg<false, 224, 4>;
+using CfgDecode = EngineCfg<false, 16, 8>;
+
+struct PackLayout {
+  size_t header, tmaps, sfw, total;
+};
+static PackLayout pack_layout(int g, int n, int k) {
+  const int nk64p = ((k / 64) + 3) / 4 * 4;
+  Carver cv;
+  PackLayout L;
+  L.header = cv.take(sizeof(PackHeader), 256);
+  L.tmaps = cv.take(size_t(g) * sizeof(CUtensorMap), 128);
+  L.sfw = cv.take(size_t(g) * (n / 128) * nk64p * 512, 256);
+  L.total = cv.off;
+  return L;
+}
+
+struct WsLayout {
+  int bn = 0, ch = 0, stages = 0;
+  int nk64p = 0, nk256 = 0, nt = 0;
+  int num_tiles = 0, xt_total = 0;
+  std::vector<int32_t> xtile_begin, tile_begin, out_row;
+  size_t status = 0, tmaps = 0, ginfo = 0, tiles = 0, sfx = 0, total = 0;
+};
+
+static int plan(const FggNvfp4Problem* p, WsLayout* L) {
+  if (p == nullptr) return set_error(FGG_EINVAL, "problem is null");
+  const int G = p->num_groups;
+  if (G < 1 || G > FGG_MAX_GROUPS)
+    return set_error(FGG_EINVAL, "num_groups=%d outside [1, %d]", G, FGG_MAX_GROUPS);
+  if (p->n <= 0 || p->n % 128 != 0)
+    return set_error(FGG_EBADSHAPE, "N=%d must be a positive multiple of 128", p->n);
+  if (p->k < 64 || p->k % 64 != 0)
+    return set_error(FGG_EBADSHAPE, "K=%d must be a positive multiple of 64", p->k);
+  if (p->m == nullptr) return set_error(FGG_EINVAL, "m (host problem sizes) is null");
+  if (p->n / 128 > 2047) return set_error(FGG_EBADSHAPE, "N=%d too large", p->n);
+  int maxm = 0;
+  for (int g = 0; g < G; ++g) {
+    if (p->m[g] < 0) return set_error(FGG_EINVAL, "m[%d]=%d is negative", g, p->m[g]);
+    maxm = std::max(maxm, p->m[g]);
+  }
+  const bool decode = maxm <= 16;
+  L->bn = decode ? CfgDecode::BN : CfgPrefill::BN;
+  L->ch = decode ? CfgDecode::CH : CfgPrefill::CH;
+  L->stages = decode ? CfgDecode::STAGES : CfgPrefill::STAGES;
+  L->nk256 = (p->k + 255) / 256;
+  L->nk64p = 4 * L->nk256;
+  L->nt = p->n / 128;
+  L->xtile_begin.assign(G + 1, 0);
+  L->tile_begin.assign(G + 1, 0);
+  L->out_row.assign(G, 0);
+  int64_t rows = 0, xts = 0, tiles = 0;
+  for (int g = 0; g < G; ++g) {
+    L->out_row[g] = int32_t(rows);
+    L->xtile_begin[g] = int32_t(xts);
+    L->tile_begin[g] = int32_t(tiles);
+    const int64_t xt = (p->m[g] + L->bn - 1) / L->bn;
+    if (xt > 2047) return set_error(FGG_EBADSHAPE, "m[%d]=%d too large", g, p->m[g]);
+    rows += p->m[g];
+    xts += xt;
+    tiles += xt * L->nt;
+  }
+  if (rows > INT32_MAX || tiles > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
+  L->xtile_begin[G] = int32_t(xts);
+  L->tile_begin[G] = int32_t(tiles);
+  L->num_tiles = int(tiles);
+  L->xt_total = int(xts);
+  Carver cv;
+  L->status = cv.take(kStatusBytes, 256);
+  L->tmaps = cv.take(size_t(G) * sizeof(CUtensorMap), 128);
+  L->ginfo = cv.take(size_t(G) * sizeof(GroupInfo), 256);
+  L->tiles = cv.take(size_t(std::max<int64_t>(tiles, 1)) * 4, 256);
+  L->sfx = cv.take(size_t(std::max<int64_t>(xts, 1)) * L->nk64p * L->ch * 512, 256);
+  L->total = cv.off;
+  return FGG_OK;
+}
+
+}  // namespace fgg
+
+using namespace fgg;
+
+extern "C" {
+
+size_t fgg_nvfp4_weight_pack_bytes(int32_t num_groups, int32_t n, int32_t k) {
+  if (num_groups < 1 || n <= 0 || k <= 0) return 0;
+  return pack_layout(num_groups, n, k).total;
+}
+
+int fgg_nvfp4_pack_weights(const FggNvfp4Weights* w, void* pack, size_t pack_bytes, void* stream) {
+  if (w == nullptr || pack == nullptr) return set_error(FGG_EINVAL, "weights or pack is null");
+  const int G = w->num_groups;
+  if (G < 1 || G > FGG_MAX_GROUPS)
+    return set_error(FGG_EINVAL, "num_groups=%d outside [1, %d]", G, FGG_MAX_GROUPS);
+  if (w->n <= 0 || w->n % 128 != 0)
+    return set_error(FGG_EBADSHAPE, "N=%d must be a positive multiple of 128", w->n);
+  if (w->k < 64 || w->k % 64 != 0)
+    return set_error(FGG_EBADSHAPE, "K=%d must be a positive multiple of 64", w->k);
+  if (w->b == nullptr || w->b_sf == nullptr) return set_error(FGG_EINVAL, "b / b_sf arrays are null");
+  for (int g = 0; g < G; ++g) {
+    if (w->b[g] == nullptr || w->b_sf[g] == nullptr)
+      return set_error(FGG_EINVAL, "group %d weight pointer is null", g);
+    if (!aligned16(w->b[g])) return set_error(FGG_EALIGN, "b[%d] is not 16-byte aligned", g);
+    if (!aligned4(w->b_sf[g])) return set_error(FGG_EALIGN, "b_sf[%d] is not 4-byte aligned", g);
+  }
+  if (!aligned16(pack)) return set_error(FGG_EALIGN, "pack is not 16-byte aligned");
+  const PackLayout L = pack_layout(G, w->n, w->k);
+  if (pack_bytes < L.total)
+    return set_error(FGG_EWORKSPACE, "pack has %zu bytes, needs %zu", pack_bytes, L.total);
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+
+  PackParams pp;
+  memset(&pp, 0, sizeof(pp));
+  if (int rc = encode_u8_2d(&pp.tmpl, w->b[0], uint64_t(w->k) / 2, uint64_t(w->n), 128, 128))
+    return rc;
+  for (int g = 0; g < G; ++g) {
+    pp.b[g] = static_cast<const uint8_t*>(w->b[g]);
+    pp.b_sf[g] = static_cast<const uint8_t*>(w->b_sf[g]);
+  }
+  uint8_t* base = static_cast<uint8_t*>(pack);
+  pp.header = reinterpret_cast<PackHeader*>(base + L.header);
+  pp.tmap_out = reinterpret_cast<CUtensorMap*>(base + L.tmaps);
+  pp.sfw_out = base + L.sfw;
+  pp.g = G;
+  pp.n = w->n;
+  pp.k = w->k;
+  pp.nk64p = ((w->k / 64) + 3) / 4 * 4;
+  pp.nt = w->n / 128;
+  pp.blocks_tmap = (G + 7) / 8;
+  const int64_t lines = int64_t(G) * pp.nt * pp.nk64p * 32;
+  const int64_t blocks = pp.blocks_tmap + (lines + 255) / 256;
+  if (blocks > INT32_MAX) return set_error(FGG_EBADSHAPE, "weights too large");
+  nvfp4_pack_weights_kernel<<<int(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(pp);
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+size_t fgg_nvfp4_workspace_bytes(const FggNvfp4Problem* p) {
+  WsLayout L;
+  if (plan(p, &L) != FGG_OK) return 0;
+  return L.total;
+}
+
+}  // extern "C"
+
+namespace fgg {
+namespace {
+
+// Checks shared by the prepare and GEMM halves.  Returns the first non-empty
+// group in *first (-1 when every group is empty).
+int check_problem(const FggNvfp4Problem* p, const WsLayout& L, void* workspace, size_t ws_bytes,
+                  int* first) {
+  if (workspace == nullptr) return set_error(FGG_EINVAL, "workspace is null");
+  if (!aligned16(workspace)) return set_error(FGG_EALIGN, "workspace must be 16-byte aligned");
+  if (ws_bytes < L.total)
+    return set_error(FGG_EWORKSPACE, "workspace has %zu bytes, needs %zu", ws_bytes, L.total);
+  if (p->alpha == nullptr || p->a == nullptr || p->a_sf == nullptr)
+    return set_error(FGG_EINVAL, "alpha / a / a_sf is null");
+  if (L.num_tiles > 0 && p->out == nullptr) return set_error(FGG_EINVAL, "out is null");
+  if (p->out != nullptr && !aligned16(p->out))
+    return set_error(FGG_EALIGN, "out is not 16-byte aligned");
+  *first = -1;
+  for (int g = 0; g < p->num_groups; ++g) {
+    if (p->m[g] == 0) continue;
+    if (p->a[g] == nullptr || p->a_sf[g] == nullptr)
+      return set_error(FGG_EINVAL, "group %d activation pointer is null", g);
+    if (!aligned16(p->a[g])) return set_error(FGG_EALIGN, "a[%d] is not 16-byte aligned", g);
+    if (!aligned4(p->a_sf[g])) return set_error(FGG_EALIGN, "a_sf[%d] is not 4-byte aligned", g);
+    if (*first < 0) *first = g;
+  }
+  return FGG_OK;
+}
+
+int prepare_impl(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8_t* ws,
+                 cudaStream_t s) {
+  const int G = p->num_groups;
+  if (L.num_tiles == 0) {
+    FGG_CUDA_CHECK(cudaMemsetAsync(ws + L.status, 0, kStatusBytes, s));
+    return FGG_OK;
+  }
+  static thread_local PrepParams pp;  // ~17 KB: keep it off the stack
+  memset(&pp, 0, sizeof(pp));
+  if (int rc = encode_u8_2d(&pp.tmpl, p->a[first], uint64_t(p->k) / 2, uint64_t(p->m[first]), 128,
+                            uint32_t(L.bn)))
+    return rc;
+  for (int g = 0; g < G; ++g) {
+    pp.a[g] = static_cast<const uint8_t*>(p->a[g]);
+    pp.a_sf[g] = static_cast<const uint8_t*>(p->a_sf[g]);
+    pp.m[g] = p->m[g];
+    pp.out_row[g] = L.out_row[g];
+  }
+  for (int g = 0; g <= G; ++g) {
+    pp.xtile_begin[g] = L.xtile_begin[g];
+    pp.tile_begin[g] = L.tile_begin[g];
+  }
+  pp.tmap_out = reinterpret_cast<CUtensorMap*>(ws + L.tmaps);
+  pp.ginfo_out = reinterpret_cast<GroupInfo*>(ws + L.ginfo);
+  pp.tiles_out = reinterpret_cast<uint32_t*>(ws + L.tiles);
+  pp.sfx_out = ws + L.sfx;
+  pp.status = reinterpret_cast<int*>(ws + L.status);
+  pp.g = G;
+  pp.k = p->k;
+  pp.bn = L.bn;
+  pp.ch = L.ch;
+  pp.nk64p = L.nk64p;
+  pp.nt = L.nt;
+  pp.num_tiles = L.num_tiles;
+  pp.xt_total = L.xt_total;
+  pp.blocks_tmap = (G + 7) / 8;
+  pp.blocks_tiles = (L.num_tiles + 255) / 256;
+  const int64_t sf_lines = int64_t(L.xt_total) * L.nk64p * L.ch * 32;
+  const int64_t blocks = int64_t(pp.blocks_tmap) + pp.blocks_tiles + (sf_lines + 255) / 256;
+  if (blocks > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
+  nvfp4_prepare_kernel<<<int(blocks), 256, 0, s>>>(pp);
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uint8_t* ws,
+              const DeviceInfo& dev, cudaStream_t s) {
+  if (L.num_tiles == 0) return FGG_OK;
+  if (pack == nullptr) return set_error(FGG_EINVAL, "pack is null");
+  if (!aligned16(pack)) return set_error(FGG_EALIGN, "pack must be 16-byte aligned");
+  const int G = p->num_groups;
+  const uint8_t* pk = static_cast<const uint8_t*>(pack);
+  const PackLayout PL = pack_layout(G, p->n, p->k);
+  GemmParams gp;
+  memset(&gp, 0, sizeof(gp));
+  gp.tmap_w = reinterpret_cast<const CUtensorMap*>(pk + PL.tmaps);
+  gp.tmap_x = reinterpret_cast<const CUtensorMap*>(ws + L.tmaps);
+  gp.sfw = pk + PL.sfw;
+  gp.sfx = ws + L.sfx;
+  gp.ginfo = reinterpret_cast<const GroupInfo*>(ws + L.ginfo);
+  gp.tiles = reinterpret_cast<const uint32_t*>(ws + L.tiles);
+  gp.alpha = p->alpha;
+  gp.pack = reinterpret_cast<const PackHeader*>(pk + PL.header);
+  gp.out = static_cast<__nv_bfloat16*>(p->out);
+  gp.status = reinterpret_cast<int*>(ws + L.status);
+  gp.g = G;
+  gp.n = p->n;
+  gp.k = p->k;
+  gp.m_total = 0;
+  gp.num_tiles = L.num_tiles;
+  gp.ksteps = L.nk256;
+  gp.nt = L.nt;
+  const cudaError_t e = (L.bn == CfgDecode::BN) ? launch_engine<CfgDecode>(gp, dev.sm_count, s)
+                                                 : launch_engine<CfgPrefill>(gp, dev.sm_count, s);
+  if (e != cudaSuccess) return set_error(FGG_ECUDA, "GEMM launch failed: %s", cudaGetErrorString(e));
+  return FGG_OK;
+}
+
+}  // namespace
+}  // namespace fgg
+
+extern "C" {
+
+int fgg_nvfp4_prepare(const FggNvfp4Problem* p, void* workspace, size_t ws_bytes, void* stream) {
+  WsLayout L;
+  if (int rc = plan(p, &L)) return rc;
+  int first = -1;
+  if (int rc = check_problem(p, L, workspace, ws_bytes, &first)) return rc;
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  return prepare_impl(p, L, first, static_cast<uint8_t*>(workspace),
+                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fgg_nvfp4_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace, size_t ws_bytes,
+                   void* stream) {
+  WsLayout L;
+  if (int rc = plan(p, &L)) return rc;
+  int first = -1;
+  if (int rc = check_problem(p, L, workspace, ws_bytes, &first)) return rc;
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  return gemm_impl(p, L, pack, static_cast<uint8_t*>(workspace), dev,
+                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fgg_nvfp4_grouped_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace,
+                           size_t ws_bytes, void* stream) {
+  WsLayout L;
+  if (int rc = plan(p, &L)) return rc;
+  int first = -1;
+  if (int rc = check_problem(p, L, workspace, ws_bytes, &first)) return rc;
+  if (L.num_tiles > 0 && pack == nullptr) return set_error(FGG_EINVAL, "pack is null");
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (int rc = prepare_impl(p, L, first, ws, s)) return rc;
+  return gemm_impl(p, L, pack, ws, dev, s);
+}
+
+}  // extern "C"

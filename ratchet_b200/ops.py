@@ -1,0 +1,299 @@
+"""Host-side mirror of the reference operator API, over the C ABI.
+
+Two operators:
+
+* `nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes, alpha)`
+  -> one bf16 [M_g, N] output per group (views of one buffer).  NVFP4 x NVFP4:
+  E2M1 codes packed two per byte, one E4M3 scale per 16 K, fp32 alpha_g
+  (= product of the two per-tensor global decode scales).
+
+* `fp4_grouped_gemm(a, a_sf, b, b_sf, m_indices) -> c`, the reference's own
+  signature and semantics (kernels/gemm/fp4_grouped_gemm/b200/kernel.py:2788-2862):
+  MXFP8 activations x MXFP4 expert weights, contiguous M grouping.
+
+Caching follows the reference's identity discipline (kernel.py:2743-2786): a
+key of (data_ptr, shape, stride, dtype, device, _version) per source tensor,
+and the cache entry holds the source tensors so their addresses cannot be
+recycled while it lives.  Like the reference, the caches are not thread-safe.
+
+Everything runs on the current CUDA stream; nothing here synchronises the host.
+"""
+from __future__ import annotations
+
+from collections import OrderedDict
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+
+_U8_DTYPES = {torch.uint8, torch.int8, torch.float8_e4m3fn}
+if hasattr(torch, "float4_e2m1fn_x2"):
+    _U8_DTYPES.add(torch.float4_e2m1fn_x2)
+
+_CACHE_MAX = 8
+
+
+def _identity(t: torch.Tensor):
+    return (int(t.data_ptr()), tuple(t.shape), tuple(t.stride()), str(t.dtype), str(t.device),
+            int(getattr(t, "_version", 0)))
+
+
+def _as_u8(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dtype not in _U8_DTYPES:
+        raise ValueError(f"{name}: dtype {t.dtype} is not a byte type (uint8/int8/float8/float4x2)")
+    return t if t.dtype == torch.uint8 else t.view(torch.uint8)
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return int(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr_array(tensors) -> np.ndarray:
+    return np.fromiter((t.data_ptr() for t in tensors), dtype=np.uint64, count=len(tensors))
+
+
+class _LRU(OrderedDict):
+    def get_or(self, key, make):
+        hit = self.get(key)
+        if hit is not None:
+            self.move_to_end(key)
+            return hit
+        val = make()
+        while len(self) >= _CACHE_MAX:
+            self.popitem(last=False)
+        self[key] = val
+        return val
+
+
+_PACKS = _LRU()
+_MX_PREP = _LRU()
+_last_ws: torch.Tensor | None = None
+
+
+class WeightPack:
+    """Device-side packed weights of one NVFP4 group list: per-group TMA
+    descriptors plus the scales in the MMA's 512-byte SF atoms."""
+
+    def __init__(self, b_list: Sequence[torch.Tensor], b_sf_list: Sequence[torch.Tensor]):
+        if len(b_list) != len(b_sf_list) or not b_list:
+            raise ValueError("b_list and b_sf_list must be non-empty and of equal length")
+        G = len(b_list)
+        if G > _lib.FGG_MAX_GROUPS:
+            raise ValueError(f"{G} groups > FGG_MAX_GROUPS={_lib.FGG_MAX_GROUPS}")
+        b0 = b_list[0]
+        if b0.dim() != 2:
+            raise ValueError(f"b[0] must be 2-D [N, K/2], got {tuple(b0.shape)}")
+        n, k = int(b0.shape[0]), int(b0.shape[1]) * 2
+        bs, sfs = [], []
+        for g, (b, s) in enumerate(zip(b_list, b_sf_list)):
+            b = _as_u8(b, f"b[{g}]")
+            s = _as_u8(s, f"b_sf[{g}]")
+            if tuple(b.shape) != (n, k // 2):
+                raise ValueError(f"b[{g}] has shape {tuple(b.shape)}, expected {(n, k // 2)}")
+            if tuple(s.shape) != (n, k // 16):
+                raise ValueError(f"b_sf[{g}] has shape {tuple(s.shape)}, expected {(n, k // 16)}")
+            if not (b.is_cuda and s.is_cuda and b.is_contiguous() and s.is_contiguous()):
+                raise ValueError(f"group {g}: weights must be contiguous CUDA tensors")
+            bs.append(b)
+            sfs.append(s)
+        self.G, self.n, self.k = G, n, k
+        self.device = b0.device
+        self.sources = (tuple(b_list), tuple(b_sf_list))  # keep addresses alive
+        L = _lib.lib()
+        nbytes = int(L.fgg_nvfp4_weight_pack_bytes(G, n, k))
+        if nbytes == 0:
+            raise ValueError(f"unsupported weight geometry G={G} N={n} K={k}")
+        self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        pb, psf = _ptr_array(bs), _ptr_array(sfs)
+        w = _lib.FggNvfp4Weights(G, n, k, pb.ctypes.data, psf.ctypes.data)
+        with torch.cuda.device(self.device):
+            _lib.check(L.fgg_nvfp4_pack_weights(w, self.buf.data_ptr(), nbytes,
+                                                _stream_ptr(self.device)),
+                       "fgg_nvfp4_pack_weights")
+
+
+def pack_weights(b_list, b_sf_list) -> WeightPack:
+    """Packed weights for these tensors, cached on tensor identity."""
+    key = tuple(_identity(t) for t in b_list) + tuple(_identity(t) for t in b_sf_list)
+    return _PACKS.get_or(key, lambda: WeightPack(b_list, b_sf_list))
+
+
+def _problem_sizes(problem_sizes, G, n, k, a_list):
+    if problem_sizes is None:
+        return [int(a.shape[0]) for a in a_list]
+    ps = problem_sizes.tolist() if isinstance(problem_sizes, torch.Tensor) else list(problem_sizes)
+    if len(ps) != G:
+        raise ValueError(f"problem_sizes has {len(ps)} entries for {G} groups")
+    ms = []
+    for g, row in enumerate(ps):
+        m_, n_, k_ = (int(v) for v in row)
+        if (n_, k_) != (n, k) or m_ != int(a_list[g].shape[0]):
+            raise ValueError(f"problem_sizes[{g}]={tuple(row)} disagrees with the tensors "
+                             f"(M={int(a_list[g].shape[0])}, N={n}, K={k})")
+        ms.append(m_)
+    return ms
+
+
+def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None, alpha=None,
+                       *, pack: WeightPack | None = None) -> list[torch.Tensor]:
+    """Per group g: C_g = alpha_g * deq(A_g) @ deq(B_g)^T as bf16 [M_g, N].
+
+    a_list[g]    [M_g, K/2]  packed E2M1 codes (uint8 / float4_e2m1fn_x2)
+    a_sf_list[g] [M_g, K/16] E4M3 scales (float8_e4m3fn / uint8), row-major
+    b_list[g]    [N, K/2], b_sf_list[g] [N, K/16]  (packed once, cached)
+    problem_sizes  G rows of (M_g, N, K), checked against the tensors
+    alpha        G floats or an fp32 tensor (default 1)
+    """
+    global _last_ws
+    G = len(a_list)
+    if not (G == len(a_sf_list) == len(b_list) == len(b_sf_list)) or G == 0:
+        raise ValueError("a_list, a_sf_list, b_list, b_sf_list must have the same non-zero length")
+    if pack is None:
+        pack = pack_weights(b_list, b_sf_list)
+    n, k, dev = pack.n, pack.k, pack.device
+    ms = _problem_sizes(problem_sizes, G, n, k, a_list)
+    a_u8, sf_u8 = [], []
+    for g in range(G):
+        a = _as_u8(a_list[g], f"a[{g}]")
+        s = _as_u8(a_sf_list[g], f"a_sf[{g}]")
+        if tuple(a.shape) != (ms[g], k // 2) or tuple(s.shape) != (ms[g], k // 16):
+            raise ValueError(f"group {g}: a {tuple(a.shape)} / a_sf {tuple(s.shape)} do not match "
+                             f"M={ms[g]}, K={k}")
+        if ms[g] > 0 and not (a.is_cuda and s.is_cuda and a.is_contiguous() and s.is_contiguous()):
+            raise ValueError(f"group {g}: activations must be contiguous CUDA tensors")
+        a_u8.append(a)
+        sf_u8.append(s)
+    if alpha is None:
+        alpha_t = torch.ones(G, dtype=torch.float32, device=dev)
+    elif isinstance(alpha, torch.Tensor):
+        alpha_t = alpha.to(device=dev, dtype=torch.float32).contiguous()
+    else:
+        alpha_t = torch.tensor([float(x) for x in alpha], dtype=torch.float32, device=dev)
+    if alpha_t.numel() != G:
+        raise ValueError(f"alpha has {alpha_t.numel()} entries for {G} groups")
+    total = sum(ms)
+    out = torch.empty((total, n), dtype=torch.bfloat16, device=dev)
+    L = _lib.lib()
+    m_arr = np.asarray(ms, dtype=np.int32)
+    pa, psf = _ptr_array(a_u8), _ptr_array(sf_u8)
+    prob = _lib.FggNvfp4Problem(G, n, k, m_arr.ctypes.data, pa.ctypes.data, psf.ctypes.data,
+                                alpha_t.data_ptr(), out.data_ptr())
+    nbytes = int(L.fgg_nvfp4_workspace_bytes(prob))
+    if nbytes == 0:
+        _lib.check(L.fgg_nvfp4_grouped_gemm(prob, None, None, 0, None), "nvfp4_grouped_gemm")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(L.fgg_nvfp4_grouped_gemm(prob, pack.buf.data_ptr(), ws.data_ptr(), nbytes,
+                                            _stream_ptr(dev)), "nvfp4_grouped_gemm")
+    _last_ws = ws
+    return list(out.split(ms, dim=0))
+
+
+class _MxPrepared:
+    def __init__(self, ws: torch.Tensor, sources):
+        self.ws = ws
+        self.sources = sources
+        self.ready = False
+
+
+def fp4_grouped_gemm(a: torch.Tensor, a_sf: torch.Tensor, b: torch.Tensor, b_sf: torch.Tensor,
+                     m_indices: torch.Tensor) -> torch.Tensor:
+    """Returns c [M_total, N] bf16; row i = dequant(a[i]) @ dequant(b[m_indices[i]])^T.
+
+    Same contract as kernels/gemm/fp4_grouped_gemm/b200/kernel.py:2788-2862:
+    a [M_total, K] float8_e4m3fn, a_sf [M_total, K/128] fp32 powers of two,
+    b [G, N, K/2] int8/uint8 packed e2m1, b_sf [G, N, K/32] fp32 powers of two,
+    m_indices [M_total] int32 (-1 = padding, segments aligned to 224 rows).
+    ValueError for N % 128 or K % 128 (kernel.py:2811-2816)."""
+    global _last_ws
+    if a.dim() != 2 or b.dim() != 3:
+        raise ValueError("a must be [M_total, K] and b [G, N, K/2]")
+    m_total, k = int(a.shape[0]), int(a.shape[1])
+    g, n = int(b.shape[0]), int(b.shape[1])
+    if n % 128 != 0:
+        raise ValueError(f"N={n} is not a multiple of BLOCK_N=128")
+    if k % 128 != 0:
+        raise ValueError(f"K={k} is not a multiple of BLOCK_K=128")
+    if int(b.shape[2]) * 2 != k:
+        raise ValueError(f"b has K/2={int(b.shape[2])}, a has K={k}")
+    if tuple(a_sf.shape) != (m_total, k // 128) or a_sf.dtype != torch.float32:
+        raise ValueError(f"a_sf must be fp32 [{m_total}, {k // 128}]")
+    if tuple(b_sf.shape) != (g, n, k // 32) or b_sf.dtype != torch.float32:
+        raise ValueError(f"b_sf must be fp32 [{g}, {n}, {k // 32}]")
+    if tuple(m_indices.shape) != (m_total,) or m_indices.dtype != torch.int32:
+        raise ValueError(f"m_indices must be int32 [{m_total}]")
+    a_u8 = _as_u8(a, "a")
+    b_u8 = _as_u8(b, "b")
+    for name, t in (("a", a_u8), ("a_sf", a_sf), ("b", b_u8), ("b_sf", b_sf), ("m_indices", m_indices)):
+        if not (t.is_cuda and t.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous CUDA tensor")
+    dev = a.device
+    c = torch.empty((m_total, n), dtype=torch.bfloat16, device=dev)
+    L = _lib.lib()
+    prob = _lib.FggMxProblem(m_total, n, k, g, a_u8.data_ptr(), a_sf.data_ptr(), b_u8.data_ptr(),
+                             b_sf.data_ptr(), m_indices.data_ptr(), c.data_ptr(), 0)
+    nbytes = int(L.fgg_mx_workspace_bytes(prob))
+    if nbytes == 0:
+        _lib.check(L.fgg_mx_grouped_gemm(prob, None, 0, None), "fp4_grouped_gemm")
+    key = (_identity(a_sf), _identity(b_sf), _identity(m_indices), m_total, n, k, g)
+    prep = _MX_PREP.get_or(key, lambda: _MxPrepared(
+        torch.empty(nbytes, dtype=torch.uint8, device=dev), (a_sf, b_sf, m_indices)))
+    prob.reuse_prepared = 1 if prep.ready else 0
+    with torch.cuda.device(dev):
+        _lib.check(L.fgg_mx_grouped_gemm(prob, prep.ws.data_ptr(), nbytes, _stream_ptr(dev)),
+                   "fp4_grouped_gemm")
+    prep.ready = True
+    _last_ws = prep.ws
+    return c
+
+
+def quantize_nvfp4(x: torch.Tensor, amax: torch.Tensor | None = None):
+    """Quantise a CUDA [rows, K] fp32/bf16 tensor to NVFP4 on the device.
+
+    Returns (codes uint8 [rows, K/2], sf float8_e4m3fn [rows, K/16], g) where g
+    is the fp32 per-tensor decode scale (0-dim device tensor): x ~ e2m1 * sf * g."""
+    if x.dim() != 2 or not x.is_cuda or not x.is_contiguous():
+        raise ValueError("x must be a contiguous 2-D CUDA tensor")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"x dtype {x.dtype} must be float32 or bfloat16")
+    rows, k = int(x.shape[0]), int(x.shape[1])
+    if k % 16 != 0:
+        raise ValueError(f"K={k} must be a multiple of 16")
+    dev = x.device
+    dt = 0 if x.dtype == torch.float32 else 1
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        s = _stream_ptr(dev)
+        if amax is None:
+            amax_t = torch.empty((), dtype=torch.float32, device=dev)
+            _lib.check(L.fgg_amax(x.data_ptr(), dt, x.numel(), amax_t.data_ptr(), s), "fgg_amax")
+        else:
+            amax_t = amax.to(device=dev, dtype=torch.float32).reshape(()).contiguous()
+        codes = torch.empty((rows, k // 2), dtype=torch.uint8, device=dev)
+        sf = torch.empty((rows, k // 16), dtype=torch.uint8, device=dev)
+        _lib.check(L.fgg_nvfp4_quantize(x.data_ptr(), dt, rows, k, amax_t.data_ptr(),
+                                        codes.data_ptr(), sf.data_ptr(), s), "fgg_nvfp4_quantize")
+    gs = torch.where(amax_t > 0, torch.tensor(2688.0, device=dev) / amax_t,
+                     torch.ones((), device=dev))
+    g = torch.ones((), device=dev) / gs
+    return codes, sf.view(torch.float8_e4m3fn), g
+
+
+def last_status() -> int:
+    """Synchronise the current stream and return the device status word of the
+    most recent GEMM call (0 = ok); raises FggError on a device timeout."""
+    if _last_ws is None:
+        return 0
+    L = _lib.lib()
+    dev = _last_ws.device
+    with torch.cuda.device(dev):
+        rc = L.fgg_read_device_status(_last_ws.data_ptr(), _stream_ptr(dev))
+    _lib.check(rc, "device status")
+    return 0
+
+
+def clear_caches() -> None:
+    _PACKS.clear()
+    _MX_PREP.clear()
