@@ -443,8 +443,11 @@ def run_ours(args, wl):
                 "peak_basis": f"{pk['src']} HBM copy", "kernel_ms": k_ms,
                 "alg_bytes": alg_bytes(wl)}
 
-    e2e_ms, h2d, d2h = time_e2e(sets, max(3, args.steps // 2), min(args.warmup, 3), dev, ws)
-    e2e_ms = max_over_ranks(e2e_ms, ws, dev)
+    if args.no_e2e:
+        e2e_ms, h2d, d2h = float("nan"), 0, 0
+    else:
+        e2e_ms, h2d, d2h = time_e2e(sets, max(3, args.steps // 2), min(args.warmup, 3), dev, ws)
+        e2e_ms = max_over_ranks(e2e_ms, ws, dev)
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
@@ -483,6 +486,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["grouped", "dense", "decode"], default="grouped")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = workload(args.config)

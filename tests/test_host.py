@@ -1,0 +1,78 @@
+"""CPU checks of the Python operator layer: argument validation mirrors the
+reference (ValueError for shapes, kernel.py:2811-2816), CPU tensors are
+refused (there is no CPU fallback), and the identity cache key tracks the
+reference's discipline (kernel.py:2746-2748)."""
+import pytest
+import torch
+
+import ratchet_b200 as rb
+from ratchet_b200 import ops
+
+
+def _mx_args(m_total=448, n=256, k=512, g=2, device="cpu"):
+    return (torch.zeros((m_total, k), dtype=torch.float8_e4m3fn, device=device),
+            torch.ones((m_total, k // 128), device=device),
+            torch.zeros((g, n, k // 2), dtype=torch.uint8, device=device),
+            torch.ones((g, n, k // 32), device=device),
+            torch.zeros((m_total,), dtype=torch.int32, device=device))
+
+
+def test_mx_rejects_n_not_multiple_of_128():
+    a, asf, b, bsf, mi = _mx_args(n=200)
+    with pytest.raises(ValueError, match="BLOCK_N"):
+        rb.fp4_grouped_gemm(a, asf, b, bsf, mi)
+
+
+def test_mx_rejects_k_not_multiple_of_128():
+    a, asf, b, bsf, mi = _mx_args(k=192)
+    with pytest.raises(ValueError, match="BLOCK_K"):
+        rb.fp4_grouped_gemm(a, asf, b, bsf, mi)
+
+
+def test_mx_rejects_cpu_tensors():
+    with pytest.raises(ValueError, match="CUDA"):
+        rb.fp4_grouped_gemm(*_mx_args())
+
+
+def test_mx_rejects_wrong_scale_dtype():
+    a, asf, b, bsf, mi = _mx_args()
+    with pytest.raises(ValueError, match="a_sf"):
+        rb.fp4_grouped_gemm(a, asf.half(), b, bsf, mi)
+
+
+def test_nvfp4_rejects_cpu_weights():
+    b = [torch.zeros((256, 256), dtype=torch.uint8)]
+    bsf = [torch.zeros((256, 32), dtype=torch.uint8)]
+    with pytest.raises(ValueError, match="CUDA"):
+        rb.pack_weights(b, bsf)
+
+
+def test_nvfp4_rejects_mismatched_lists():
+    with pytest.raises(ValueError):
+        rb.nvfp4_grouped_gemm([], [], [], [])
+
+
+def test_nvfp4_rejects_non_byte_dtype():
+    with pytest.raises(ValueError, match="byte type"):
+        ops._as_u8(torch.zeros(4, dtype=torch.float32), "x")
+
+
+def test_identity_key_tracks_version_and_view():
+    t = torch.zeros(8, dtype=torch.uint8)
+    k0 = ops._identity(t)
+    t.add_(1)                      # in-place write bumps _version
+    assert ops._identity(t) != k0
+    assert ops._identity(t[:4]) != ops._identity(t)
+
+
+def test_lru_evicts_oldest():
+    lru = ops._LRU()
+    for i in range(ops._CACHE_MAX + 3):
+        lru.get_or(i, lambda i=i: i)
+    assert len(lru) == ops._CACHE_MAX
+    assert 0 not in lru and (ops._CACHE_MAX + 2) in lru
+
+
+def test_quantize_rejects_cpu():
+    with pytest.raises(ValueError):
+        rb.quantize_nvfp4(torch.zeros((4, 32)))
