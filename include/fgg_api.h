@@ -36,6 +36,12 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#if defined(__GNUC__)
+#define FGG_API __attribute__((visibility("default")))
+#else
+#define FGG_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -55,10 +61,10 @@ enum {
  * kernel parameters). */
 #define FGG_MAX_GROUPS 512
 
-const char* fgg_error_string(int code);
-const char* fgg_last_error_detail(void);
+FGG_API const char* fgg_error_string(int code);
+FGG_API const char* fgg_last_error_detail(void);
 /* Library build identifier ("fgg <version> sm_100a"). */
-const char* fgg_version(void);
+FGG_API const char* fgg_version(void);
 
 /* ------------------------------------------------------------------------ */
 /* NVFP4 x NVFP4 grouped GEMM                                                */
@@ -78,8 +84,8 @@ typedef struct FggNvfp4Weights {
  * descriptors plus the scales repacked into the MMA's 512-byte SF atoms.
  * Replaces the identity-cached host repack `_prepare` / `_pack_sf_wgt` of
  * kernels/gemm/fp4_grouped_gemm/b200/kernel.py:2709-2786, done on the device. */
-size_t fgg_nvfp4_weight_pack_bytes(int32_t num_groups, int32_t n, int32_t k);
-int fgg_nvfp4_pack_weights(const FggNvfp4Weights* w, void* pack, size_t pack_bytes,
+FGG_API size_t fgg_nvfp4_weight_pack_bytes(int32_t num_groups, int32_t n, int32_t k);
+FGG_API int fgg_nvfp4_pack_weights(const FggNvfp4Weights* w, void* pack, size_t pack_bytes,
                            void* stream);
 
 /* One grouped GEMM call.  A_g codes [M_g, K/2] uint8; A_g scales [M_g, K/16]
@@ -99,20 +105,20 @@ typedef struct FggNvfp4Problem {
 /* Scratch the call needs (token-scale repack, per-group descriptors, tile
  * list, status words).  Replaces the per-call part of `_prepare`
  * (kernels/gemm/fp4_grouped_gemm/b200/kernel.py:2751-2786). */
-size_t fgg_nvfp4_workspace_bytes(const FggNvfp4Problem* p);
+FGG_API size_t fgg_nvfp4_workspace_bytes(const FggNvfp4Problem* p);
 /* Replaces `fp4_grouped_gemm` (kernel.py:2788-2862) for the NVFP4 format:
  * validates, repacks the token scales, builds descriptors and launches the
  * persistent tcgen05 kernel.  `pack` must come from fgg_nvfp4_pack_weights
  * for the same G, N, K. */
-int fgg_nvfp4_grouped_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace,
+FGG_API int fgg_nvfp4_grouped_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace,
                            size_t ws_bytes, void* stream);
 /* The two halves of fgg_nvfp4_grouped_gemm, for callers that replay one
  * problem (same pointers, same sizes) many times, e.g. inside a CUDA graph:
  * fgg_nvfp4_prepare fills `workspace` (descriptors, token-scale repack, tile
  * list); fgg_nvfp4_gemm launches the GEMM kernel on a prepared workspace and
  * may be repeated.  The token scales must not change between the two. */
-int fgg_nvfp4_prepare(const FggNvfp4Problem* p, void* workspace, size_t ws_bytes, void* stream);
-int fgg_nvfp4_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace, size_t ws_bytes,
+FGG_API int fgg_nvfp4_prepare(const FggNvfp4Problem* p, void* workspace, size_t ws_bytes, void* stream);
+FGG_API int fgg_nvfp4_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace, size_t ws_bytes,
                    void* stream);
 
 /* ------------------------------------------------------------------------ */
@@ -147,8 +153,8 @@ typedef struct FggMxProblem {
 
 /* Scratch for the MX call (repacked UE8M0 scales, block->expert table,
  * descriptors, status): kernel.py:2679-2786 done on the device per call. */
-size_t fgg_mx_workspace_bytes(const FggMxProblem* p);
-int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
+FGG_API size_t fgg_mx_workspace_bytes(const FggMxProblem* p);
+FGG_API int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
                         void* stream);
 
 /* ------------------------------------------------------------------------ */
@@ -157,7 +163,7 @@ int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
 
 /* amax of |x| over `count` elements into *amax_out (device fp32).
  * x_dtype: 0 = fp32, 1 = bf16. */
-int fgg_amax(const void* x, int32_t x_dtype, int64_t count, float* amax_out, void* stream);
+FGG_API int fgg_amax(const void* x, int32_t x_dtype, int64_t count, float* amax_out, void* stream);
 
 /* Quantise a row-major [rows, k] tensor to NVFP4:
  *   gs   = 2688 / amax (1 if amax == 0)            (device scalar, fp32)
@@ -165,7 +171,7 @@ int fgg_amax(const void* x, int32_t x_dtype, int64_t count, float* amax_out, voi
  *   q    = e2m1_rne(x * (gs / float(s)))             (0 where s == 0)
  * codes [rows, k/2] uint8 (element 2j in the low nibble), sf [rows, k/16] E4M3.
  * `amax` is a device fp32 scalar (from fgg_amax or supplied by the caller). */
-int fgg_nvfp4_quantize(const void* x, int32_t x_dtype, int64_t rows, int32_t k,
+FGG_API int fgg_nvfp4_quantize(const void* x, int32_t x_dtype, int64_t rows, int32_t k,
                        const float* amax, void* codes, void* sf, void* stream);
 
 /* ------------------------------------------------------------------------ */
@@ -176,7 +182,7 @@ int fgg_nvfp4_quantize(const void* x, int32_t x_dtype, int64_t rows, int32_t k,
  * in `workspace` (the NVFP4 or MX workspace).  Returns FGG_OK, FGG_ETIMEOUT
  * (a device wait ran out; the kernel stopped early and its output is
  * incomplete) or FGG_ECUDA. */
-int fgg_read_device_status(const void* workspace, void* stream);
+FGG_API int fgg_read_device_status(const void* workspace, void* stream);
 
 #ifdef __cplusplus
 }

@@ -50,7 +50,10 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     out_dir = PKG / "_build"
     out_dir.mkdir(exist_ok=True)
     objs = []
+    # Only the C ABI is exported: template statics stay private to this library
+    # even when another copy of it is loaded into the same process.
     common = [nvcc(), "-O3", "-std=c++17", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC",
+              "-Xcompiler", "-fvisibility=hidden", "-Xcompiler", "-fno-gnu-unique",
               "-I", str(ROOT / "include"), "--expt-relaxed-constexpr"]
     if ptxas_verbose:
         common += ["-Xptxas", "-v"]

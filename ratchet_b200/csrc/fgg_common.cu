@@ -92,6 +92,15 @@ int encode_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uin
   return encode(out, dtype, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+int encode_u64_rows(CUtensorMap* out, const void* base, uint64_t rows, uint32_t row_u64,
+                    uint32_t box_rows) {
+  cuuint64_t dims[2] = {row_u64, rows};
+  cuuint64_t strides[1] = {uint64_t(row_u64) * 8u};
+  cuuint32_t box[2] = {row_u64, box_rows};
+  return encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, base, dims, strides, box,
+                CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 int encode_3d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t d0,
               uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
               uint32_t b0, uint32_t b1, uint32_t b2) {

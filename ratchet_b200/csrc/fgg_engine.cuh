@@ -2,22 +2,31 @@
 // operand formats.
 //
 // Orientation ("swap AB", as kernels/gemm/fp4_grouped_gemm/b200/kernel.py:84-86
-// does with MMA-A = weights): the tensor core's M axis runs over 128 weight rows
+// does with MMA-A = weights): the tensor core's M axis runs over weight rows
 // (output columns n), its N axis over up to BN tokens of one group (output rows
 // m).  Ragged group sizes land on the MMA's N axis, sized per tile in steps of
-// 16, and the epilogue's lanes walk consecutive output columns.
+// 16 (32 for pairs), and the epilogue's lanes walk consecutive output columns.
 //
-// One CTA per SM, 256 threads, warp-specialised:
-//   warp 0     claims tiles from a global atomic counter (dynamic persistent
-//              schedule), broadcasts them through an smem ring, and issues the
-//              TMA / bulk loads of every K step into a STAGES-deep ring
-//   warp 1     one thread issues tcgen05.cp (scale factors -> TMEM) and the
-//              block-scaled tcgen05.mma chain into a double-buffered TMEM
-//              accumulator
-//   warp 2     allocates / frees TMEM
+// Warp roles (256 threads, one CTA per SM):
+//   warp 0     producer: one thread issues the TMA loads of every K step into
+//              a STAGES-deep shared-memory ring
+//   warp 1     MMA issuer: one thread issues tcgen05.cp (scale factors ->
+//              TMEM) and the block-scaled tcgen05.mma chain into a
+//              double-buffered TMEM accumulator
+//   warp 2     TMEM allocator
+//   warp 3     scheduler: claims tiles from a global atomic counter (dynamic
+//              persistent schedule) and publishes each tile with its metadata
+//              in an 8-deep shared-memory ring, ahead of every other role
 //   warps 4-7  epilogue: tcgen05.ld (each warp its 32-lane quadrant) -> fp32
 //              x alpha -> bf16 -> global, overlapped with the next tile's MMAs
+// The producer and MMA roles run on ONE thread each: between two K steps they
+// only test a barrier.  Every wait suspends in hardware (try_wait with a time
+// hint) so waiting warps do not steal issue slots from the MMA thread.
 //
+// Two kernels:
+//   fgg_gemm_kernel       one CTA per tile, 128 weight rows x BN tokens
+//   fgg_gemm_pair_kernel  a CTA pair (cta_group::2) per tile, 256 x 224: each
+//                         CTA loads half of the token tile
 // Two kinds (compile-time):
 //   NVFP4   .kind::mxf4nvf4 .scale_vec::4X: E2M1 x E2M1, one E4M3 scale per 16
 //           K; K step 256 = 4 MMAs of K 64, one SF slot per MMA.
@@ -53,6 +62,107 @@ struct PackHeader {
 
 constexpr int kStatusBadPack = 0x201;
 
+// One schedule-ring slot (32 bytes): what every role needs to know about a
+// tile, published by the scheduler warp.
+struct SchedSlot {
+  uint32_t tile;        // packed (group, weight tile, token tile) or kEndTile
+  int32_t rows;         // valid token rows of the tile
+  int32_t row0;         // output row of the tile's first token
+  float alpha;          // output scale
+  int32_t xtile_index;  // the token tile's index in the token-scale repack
+  int32_t pad[3];
+};
+static_assert(sizeof(SchedSlot) == 32, "slot is 8 words");
+
+struct GemmParams {
+  CUtensorMap mx_tmap_w;      // MX: 3-D map of the [G, N, K] weight codes
+  CUtensorMap mx_tmap_x;      // MX: 2-D map of the [M_total, K] fp8 activations
+  CUtensorMap sfw_map;        // pair kernel: the weight SF atoms as a 2-D uint64 tensor
+  CUtensorMap sfx_map;        // pair kernel: the token SF atoms as a 2-D uint64 tensor
+  const CUtensorMap* tmap_w;  // NVFP4: [G] per-group maps (global memory)
+  const CUtensorMap* tmap_x;  // NVFP4: [G] per-group maps (global memory)
+  const uint8_t* sfw;         // [G][NT128][KSTEPS][SFW_BYTES]
+  const uint8_t* sfx;         // [XT][KSTEPS][SFX_BYTES]
+  const GroupInfo* ginfo;     // NVFP4: [G]
+  const uint32_t* tiles;      // [T]
+  const float* alpha;         // NVFP4: [G]; MX: unused (1)
+  const PackHeader* pack;     // NVFP4: weight pack header; MX: null
+  __nv_bfloat16* out;
+  int* status;  // [0] status, [1] tile counter, [2] finished CTAs
+  int32_t g, n, k;
+  int32_t m_total;  // MX: rows of the contiguous activation tensor
+  int32_t num_tiles;
+  int32_t ksteps;
+  int32_t nt;     // weight tiles per group in the tile list (128 rows; 256 for pairs)
+  int32_t nt128;  // 128-row weight tiles per group (the SF pack's unit)
+};
+
+// Metadata of tile `tile` (scheduler warp, off the critical path).
+template <bool MX, int BN>
+__device__ __forceinline__ SchedSlot make_slot(const GemmParams& p, uint32_t tile) {
+  SchedSlot s;
+  s.tile = tile;
+  s.pad[0] = s.pad[1] = s.pad[2] = 0;
+  if (tile == kEndTile) {
+    s.rows = 0;
+    s.row0 = 0;
+    s.alpha = 0.0f;
+    s.xtile_index = 0;
+    return s;
+  }
+  const int g = int(tile >> 22);
+  const int xti = int(tile & 0x7FFu);
+  if constexpr (MX) {
+    s.rows = min(BN, p.m_total - xti * BN);
+    s.row0 = xti * BN;
+    s.alpha = 1.0f;
+    s.xtile_index = xti;
+  } else {
+    const GroupInfo gi = p.ginfo[g];
+    s.rows = min(BN, gi.m - xti * BN);
+    s.row0 = gi.out_row + xti * BN;
+    s.alpha = p.alpha[g];
+    s.xtile_index = gi.xtile_begin + xti;
+  }
+  return s;
+}
+
+__device__ __forceinline__ SchedSlot read_slot(const volatile SchedSlot* ring, int slot) {
+  SchedSlot s;
+  s.tile = ring[slot].tile;
+  s.rows = ring[slot].rows;
+  s.row0 = ring[slot].row0;
+  s.alpha = ring[slot].alpha;
+  s.xtile_index = ring[slot].xtile_index;
+  return s;
+}
+
+__device__ __forceinline__ void write_slot(volatile SchedSlot* ring, int slot,
+                                           const SchedSlot& s) {
+  ring[slot].tile = s.tile;
+  ring[slot].rows = s.rows;
+  ring[slot].row0 = s.row0;
+  ring[slot].alpha = s.alpha;
+  ring[slot].xtile_index = s.xtile_index;
+}
+
+// Epilogue of one tile for the calling warp: its 32 TMEM lanes (output
+// columns n) x `rows` tokens, fp32 -> x alpha -> bf16.
+__device__ __forceinline__ void epilogue_tile(__nv_bfloat16* out, int ldn, int n, size_t row0,
+                                              int rows, int ncols, float alpha, uint32_t taddr) {
+  __nv_bfloat16* orow = out + row0 * size_t(ldn) + size_t(n);
+  for (int c0 = 0; c0 < ncols; c0 += 16) {
+    uint32_t r[16];
+    tmem_ld16(taddr + c0, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (c0 + j < rows)
+        orow[size_t(c0 + j) * ldn] = __float2bfloat16_rn(alpha * __uint_as_float(r[j]));
+    }
+  }
+}
+
 template <bool MX_, int BN_, int STAGES_>
 struct EngineCfg {
   static constexpr bool MX = MX_;
@@ -81,34 +191,17 @@ struct EngineCfg {
   static constexpr int NSLOTS = NSLOTS_FIT > 8 ? 8 : NSLOTS_FIT;
   static_assert(NSLOTS >= 2, "not enough TMEM for the scale ring");
   static constexpr int COLS = SF_BASE + NSLOTS * SF_SLOT;
+  static_assert(COLS <= 512, "TMEM columns exceeded");
   static constexpr uint32_t TMEM_COLS =
       COLS <= 32 ? 32 : COLS <= 64 ? 64 : COLS <= 128 ? 128 : COLS <= 256 ? 256 : 512;
-  static constexpr int SCHED = 8;  // tile-broadcast ring depth
+  static constexpr int SCHED = 8;  // schedule ring depth
+  // readers of a schedule slot: producer, MMA thread, 4 epilogue warps
+  static constexpr uint32_t SCHED_READERS = 6;
   // barriers: full[S] empty[S] accf[2] acce[2] schedf[SCHED] schede[SCHED] tmem_ready drain
   static constexpr uint32_t NBARS = 2 * STAGES + 4 + 2 * SCHED + 2;
-  static constexpr uint32_t MISC_BYTES = 8 * NBARS + 4 * SCHED + 16;
+  static constexpr uint32_t MISC_BYTES = 8 * NBARS + 32 * SCHED + 16;
   static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + MISC_BYTES;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
-};
-
-struct GemmParams {
-  CUtensorMap mx_tmap_w;      // MX: 3-D map of the [G, N, K] weight codes
-  CUtensorMap mx_tmap_x;      // MX: 2-D map of the [M_total, K] fp8 activations
-  const CUtensorMap* tmap_w;  // NVFP4: [G] per-group maps (global memory)
-  const CUtensorMap* tmap_x;  // NVFP4: [G] per-group maps (global memory)
-  const uint8_t* sfw;         // [G][NT][KSTEPS][SFW_BYTES]
-  const uint8_t* sfx;         // [XT][KSTEPS][SFX_BYTES]
-  const GroupInfo* ginfo;     // NVFP4: [G]
-  const uint32_t* tiles;      // [T]
-  const float* alpha;         // NVFP4: [G]; MX: unused (1)
-  const PackHeader* pack;     // NVFP4: weight pack header; MX: null
-  __nv_bfloat16* out;
-  int* status;  // [0] status, [1] tile counter, [2] finished CTAs
-  int32_t g, n, k;
-  int32_t m_total;  // MX: rows of the contiguous activation tensor
-  int32_t num_tiles;
-  int32_t ksteps;
-  int32_t nt;
 };
 
 template <class C>
@@ -128,9 +221,10 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
   const uint32_t tmem_ready_bar = bars + 8u * (2 * C::STAGES + 4 + 2 * C::SCHED);
   const uint32_t drain_bar = tmem_ready_bar + 8u;
   uint8_t* const misc = gbase + C::STAGES * C::STAGE_BYTES + 8 * C::NBARS;
-  volatile uint32_t* const sched_tile = reinterpret_cast<volatile uint32_t*>(misc);
-  volatile uint32_t* const tmem_holder = reinterpret_cast<volatile uint32_t*>(misc + 4 * C::SCHED);
-  volatile int* const abort_flag = reinterpret_cast<volatile int*>(misc + 4 * C::SCHED + 4);
+  volatile SchedSlot* const ring = reinterpret_cast<volatile SchedSlot*>(misc);
+  volatile uint32_t* const tmem_holder =
+      reinterpret_cast<volatile uint32_t*>(misc + 32 * C::SCHED);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(misc + 32 * C::SCHED + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -140,15 +234,6 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
   auto sSFW = [&](int s) { return base + s * C::STAGE_BYTES + C::W_BYTES + C::X_BYTES; };
   auto sSFX = [&](int s) {
     return base + s * C::STAGE_BYTES + C::W_BYTES + C::X_BYTES + C::SFW_BYTES;
-  };
-
-  // rows of the token tile and the bf16 output base of its first row
-  auto tile_rows = [&](int g, int xti) -> int {
-    if constexpr (C::MX) {
-      return min(C::BN, p.m_total - xti * C::BN);
-    } else {
-      return min(C::BN, p.ginfo[g].m - xti * C::BN);
-    }
   };
 
   if (threadIdx.x == 0) {
@@ -162,7 +247,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
     }
     for (int i = 0; i < C::SCHED; ++i) {
       mbar_init(schedf_bar(i), 1);
-      mbar_init(schede_bar(i), 5);  // MMA warp + 4 epilogue warps
+      mbar_init(schede_bar(i), C::SCHED_READERS);
     }
     mbar_init(tmem_ready_bar, 1);
     mbar_init(drain_bar, 1);
@@ -189,64 +274,73 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
 
   const bool aborted_early = (*abort_flag != 0);
 
-  if (warp == 0 && !aborted_early) {
-    // ------------------------------------------------ producer + scheduler
-    int stage = 0;
-    uint32_t phase = 0;
-    int slot = 0;
-    uint32_t sphase = 0;
-    uint32_t arms = 0;
-    if constexpr (C::MX) {
-      if (lane == 0) {
+  if (warp == 3) {
+    // ------------------------------------------------------------ scheduler
+    if (lane == 0 && !aborted_early) {
+      int slot = 0;
+      uint32_t sphase = 0;
+      while (true) {
+        const int t = atomicAdd(p.status + 1, 1);
+        const uint32_t tile = (t < p.num_tiles) ? __ldg(p.tiles + t) : kEndTile;
+        const SchedSlot s = make_slot<C::MX, C::BN>(p, tile);
+        if (!mbar_wait1(schede_bar(slot), sphase ^ 1, abort_flag, p.status,
+                        kStatusTimeoutProducer))
+          break;
+        write_slot(ring, slot, s);
+        mbar_arrive(schedf_bar(slot));
+        if (++slot == C::SCHED) {
+          slot = 0;
+          sphase ^= 1;
+        }
+        if (tile == kEndTile) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 0) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0 && !aborted_early) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int slot = 0;
+      uint32_t sphase = 0;
+      uint32_t arms = 0;
+      if constexpr (C::MX) {
         prefetch_tensormap(&p.mx_tmap_w);
         prefetch_tensormap(&p.mx_tmap_x);
       }
-    }
-    while (true) {
-      int t = 0;
-      if (lane == 0) t = atomicAdd(p.status + 1, 1);
-      t = __shfl_sync(0xffffffffu, t, 0);
-      const uint32_t tile = (t < p.num_tiles) ? p.tiles[t] : kEndTile;
-      if (!mbar_wait(schede_bar(slot), sphase ^ 1, abort_flag, p.status, kStatusTimeoutProducer))
-        break;
-      if (lane == 0) {
-        sched_tile[slot] = tile;
-        mbar_arrive(schedf_bar(slot));
-      }
-      __syncwarp();
-      if (++slot == C::SCHED) {
-        slot = 0;
-        sphase ^= 1;
-      }
-      if (tile == kEndTile) break;
-      const int g = int(tile >> 22);
-      const int nti = int((tile >> 11) & 0x7FFu);
-      const int xti = int(tile & 0x7FFu);
-      const CUtensorMap* tw;
-      const CUtensorMap* tx;
-      const uint8_t* sfx;
-      if constexpr (C::MX) {
-        tw = &p.mx_tmap_w;
-        tx = &p.mx_tmap_x;
-        sfx = p.sfx + size_t(xti) * size_t(p.ksteps) * C::SFX_BYTES;
-      } else {
-        tw = p.tmap_w + g;
-        tx = p.tmap_x + g;
-        sfx = p.sfx + size_t(p.ginfo[g].xtile_begin + xti) * size_t(p.ksteps) * C::SFX_BYTES;
-        if (lane == 0) {
+      while (true) {
+        if (!mbar_wait1(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutProducer))
+          break;
+        const SchedSlot s = read_slot(ring, slot);
+        mbar_arrive(schede_bar(slot));
+        if (++slot == C::SCHED) {
+          slot = 0;
+          sphase ^= 1;
+        }
+        if (s.tile == kEndTile) break;
+        const int g = int(s.tile >> 22);
+        const int nti = int((s.tile >> 11) & 0x7FFu);
+        const int xti = int(s.tile & 0x7FFu);
+        const CUtensorMap* tw;
+        const CUtensorMap* tx;
+        if constexpr (C::MX) {
+          tw = &p.mx_tmap_w;
+          tx = &p.mx_tmap_x;
+        } else {
+          tw = p.tmap_w + g;
+          tx = p.tmap_x + g;
           tensormap_acquire(tw);
           tensormap_acquire(tx);
         }
-      }
-      const uint8_t* sfw = p.sfw + (size_t(g) * p.nt + nti) * size_t(p.ksteps) * C::SFW_BYTES;
-      bool ok = true;
-      for (int ks = 0; ks < p.ksteps; ++ks) {
-        if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.status,
-                       kStatusTimeoutProducer)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
+        const uint8_t* sfx = p.sfx + size_t(s.xtile_index) * size_t(p.ksteps) * C::SFX_BYTES;
+        const uint8_t* sfw = p.sfw + (size_t(g) * p.nt + nti) * size_t(p.ksteps) * C::SFW_BYTES;
+        bool ok = true;
+        for (int ks = 0; ks < p.ksteps; ++ks) {
+          if (!mbar_wait1(empty_bar(stage), phase ^ 1, abort_flag, p.status,
+                          kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
           const uint32_t fb = full_bar(stage);
           mbar_arrive_expect_tx(fb, C::TX_BYTES);
           if constexpr (C::MX) {
@@ -258,90 +352,83 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
           }
           bulk_g2s(sSFW(stage), sfw + size_t(ks) * C::SFW_BYTES, C::SFW_BYTES, fb);
           bulk_g2s(sSFX(stage), sfx + size_t(ks) * C::SFX_BYTES, C::SFX_BYTES, fb);
+          ++arms;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
-        __syncwarp();
-        ++arms;
-        if (++stage == C::STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
+        if (!ok) break;
       }
-      if (!ok) break;
-    }
-    // Every armed stage must land before the CTA may exit (normally already so).
-    if (lane == 0) {
+      // Every armed stage must land before the CTA may exit (normally already so).
       const uint32_t first = arms > uint32_t(C::STAGES) ? arms - C::STAGES : 0u;
       for (uint32_t a = first; a < arms; ++a)
         mbar_wait_one(full_bar(int(a % C::STAGES)), (a / C::STAGES) & 1u, 200000000ull);
     }
     __syncwarp();
-  } else if (warp == 1 && !aborted_early) {
-    // ------------------------------------------------------- MMA issuer
-    bool ok = mbar_wait(tmem_ready_bar, 0, abort_flag, p.status, kStatusTimeoutMma);
-    tc_fence_after();
-    const uint32_t tmem = *tmem_holder;
-    int stage = 0;
-    uint32_t phase = 0;
-    int slot = 0;
-    uint32_t sphase = 0;
-    uint32_t lt = 0;
-    int sfslot = 0;
-    bool issued_any = false;
-    while (ok) {
-      if (!mbar_wait(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutMma)) break;
-      const uint32_t tile = sched_tile[slot];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(schede_bar(slot));
-      if (++slot == C::SCHED) {
-        slot = 0;
-        sphase ^= 1;
-      }
-      if (tile == kEndTile) break;
-      const int g = int(tile >> 22);
-      const int xti = int(tile & 0x7FFu);
-      const int rows = tile_rows(g, xti);
-      const int ncols = min(C::BN, (rows + 15) & ~15);
-      const uint32_t b = lt & 1u;
-      if (!mbar_wait(acce_bar(b), ((lt >> 1) & 1u) ^ 1u, abort_flag, p.status,
-                     kStatusTimeoutMma))
-        break;
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0 && !aborted_early) {
+      bool ok = mbar_wait1(tmem_ready_bar, 0, abort_flag, p.status, kStatusTimeoutMma);
       tc_fence_after();
-      const uint32_t d_tmem = tmem + b * C::BN;
-      for (int ks = 0; ks < p.ksteps; ++ks) {
-        if (!mbar_wait(full_bar(stage), phase, abort_flag, p.status, kStatusTimeoutMma)) {
-          ok = false;
+      const uint32_t tmem = *tmem_holder;
+      int stage = 0;
+      uint32_t phase = 0;
+      int slot = 0;
+      uint32_t sphase = 0;
+      uint32_t lt = 0;
+      int sfslot = 0;
+      bool issued_any = false;
+      while (ok) {
+        if (!mbar_wait1(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutMma))
           break;
+        const SchedSlot s = read_slot(ring, slot);
+        mbar_arrive(schede_bar(slot));
+        if (++slot == C::SCHED) {
+          slot = 0;
+          sphase ^= 1;
         }
+        if (s.tile == kEndTile) break;
+        const int ncols = min(C::BN, (s.rows + 15) & ~15);
+        const int nsfx = (ncols + 127) >> 7;  // token SF atoms this tile needs
+        const uint32_t b = lt & 1u;
+        if (!mbar_wait1(acce_bar(b), ((lt >> 1) & 1u) ^ 1u, abort_flag, p.status,
+                        kStatusTimeoutMma))
+          break;
         tc_fence_after();
-        if (lane == 0) {
+        const uint32_t d_tmem = tmem + b * C::BN;
+        const uint32_t idesc =
+            C::MX ? 0u : idesc_block_scaled(kFmtNvf4E2M1, kFmtNvf4E2M1, 0, 128, ncols, 0, 0);
+        for (int ks = 0; ks < p.ksteps; ++ks) {
+          if (!mbar_wait1(full_bar(stage), phase, abort_flag, p.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           const uint64_t adesc = desc_k_sw128(sW(stage));
           const uint64_t bdesc = desc_k_sw128(sX(stage));
           if constexpr (C::MX) {
             const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
             tc_cp_sf(tmem + col, desc_sf_atom(sSFW(stage)));
-#pragma unroll
-            for (int c = 0; c < C::CH; ++c)
+            for (int c = 0; c < nsfx; ++c)
               tc_cp_sf(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(stage) + c * 512));
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               // K step of 32 one-byte elements = 32 bytes = +2 in the start field;
               // SF id j picks byte j of every scale column.
-              const uint32_t idesc =
+              const uint32_t idj =
                   idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 128, ncols, j, j);
-              tc_mma_mxf8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc,
+              tc_mma_mxf8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
                               (tmem + col) | (uint32_t(j) << 30),
                               (tmem + col + 4) | (uint32_t(j) << 30), (ks | j) != 0 ? 1u : 0u);
             }
             sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
           } else {
-            const uint32_t idesc =
-                idesc_block_scaled(kFmtNvf4E2M1, kFmtNvf4E2M1, 0, 128, ncols, 0, 0);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
               tc_cp_sf(tmem + col, desc_sf_atom(sSFW(stage) + j * 512));
-#pragma unroll
-              for (int c = 0; c < C::CH; ++c)
+              for (int c = 0; c < nsfx; ++c)
                 tc_cp_sf(tmem + col + 4 + 4 * c,
                          desc_sf_atom(sSFX(stage) + (j * C::CH + c) * 512));
               // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
@@ -351,27 +438,26 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
             }
           }
           tc_commit(empty_bar(stage));
+          issued_any = true;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
-        __syncwarp();
-        issued_any = true;
-        if (++stage == C::STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
+        if (!ok) break;
+        tc_commit(accf_bar(b));
+        ++lt;
       }
-      if (!ok) break;
-      if (lane == 0) tc_commit(accf_bar(b));
-      __syncwarp();
-      ++lt;
-    }
-    // Drain: every tcgen05 op this thread issued completes before TMEM is freed.
-    if (lane == 0 && issued_any) {
-      tc_commit(drain_bar);
-      if (!mbar_wait_one(drain_bar, 0, 200000000ull)) atomicCAS(p.status, 0, kStatusTimeoutDrain);
+      // Drain: every tcgen05 op this thread issued completes before TMEM is freed.
+      if (issued_any) {
+        tc_commit(drain_bar);
+        if (!mbar_wait_one(drain_bar, 0, 200000000ull))
+          atomicCAS(p.status, 0, kStatusTimeoutDrain);
+      }
     }
     __syncwarp();
   } else if (warp >= 4 && !aborted_early) {
-    // --------------------------------------------------------- epilogue
+    // ------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
     bool ok = mbar_wait(tmem_ready_bar, 0, abort_flag, p.status, kStatusTimeoutEpilogue);
     tc_fence_after();
@@ -382,44 +468,22 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
     while (ok) {
       if (!mbar_wait(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutEpilogue))
         break;
-      const uint32_t tile = sched_tile[slot];
+      const SchedSlot s = read_slot(ring, slot);
       __syncwarp();
       if (lane == 0) mbar_arrive(schede_bar(slot));
       if (++slot == C::SCHED) {
         slot = 0;
         sphase ^= 1;
       }
-      if (tile == kEndTile) break;
-      const int g = int(tile >> 22);
-      const int nti = int((tile >> 11) & 0x7FFu);
-      const int xti = int(tile & 0x7FFu);
-      const int rows = tile_rows(g, xti);
-      const int ncols = min(C::BN, (rows + 15) & ~15);
-      float alpha = 1.0f;
-      size_t row0;
-      if constexpr (C::MX) {
-        row0 = size_t(xti) * C::BN;
-      } else {
-        alpha = p.alpha[g];
-        row0 = size_t(p.ginfo[g].out_row) + size_t(xti) * C::BN;
-      }
+      if (s.tile == kEndTile) break;
+      const int nti = int((s.tile >> 11) & 0x7FFu);
+      const int ncols = min(C::BN, (s.rows + 15) & ~15);
       const uint32_t b = lt & 1u;
       if (!mbar_wait(accf_bar(b), (lt >> 1) & 1u, abort_flag, p.status, kStatusTimeoutEpilogue))
         break;
       tc_fence_after();
-      const int n = nti * 128 + q * 32 + lane;
-      __nv_bfloat16* orow = p.out + row0 * size_t(p.n) + size_t(n);
-      const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + b * C::BN;
-      for (int c0 = 0; c0 < ncols; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(taddr + c0, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (c0 + j < rows)
-            orow[size_t(c0 + j) * p.n] = __float2bfloat16_rn(alpha * __uint_as_float(r[j]));
-        }
-      }
+      epilogue_tile(p.out, p.n, nti * 128 + q * 32 + lane, size_t(s.row0), s.rows, ncols,
+                    s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(b));
@@ -441,6 +505,422 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
       atomicExch(p.status + 2, 0);
     }
   }
+}
+
+// ====================================================================
+// CTA-pair engine: cluster (2,1,1), tcgen05 .cta_group::2.
+//
+// The pair computes a 256 (weight rows) x 224 (tokens) tile: each CTA loads
+// its own 128 weight rows and HALF of the token rows, so the token tile
+// crosses L2 -> SM once per pair instead of once per CTA.  The leader (rank 0)
+// runs the scheduler (it publishes every slot into both CTAs' rings), arms one
+// full barrier per stage for both CTAs' bytes (every load of the pair books
+// its completion there: .cta_group::2 TMA), and issues the scale-factor
+// uploads and MMAs.  Commits arrive in both CTAs (empty stages, accumulator
+// ready); each CTA's epilogue drains its own TMEM (its 128 output columns) and
+// tells the leader's acc-empty barrier when it is done.
+// Scale factors: each CTA holds the atoms of its own weight rows and the atoms
+// of all 224 tokens; the leader's tcgen05.cp.cta_group::2 copies each CTA's
+// atoms into that CTA's TMEM.
+// Waits acquire at CTA scope (TMA / tcgen05 completions), except on the
+// schedule ring, whose slots the leader writes into the follower's shared
+// memory: those waits acquire at cluster scope.
+// ====================================================================
+template <bool MX_, int STAGES_>
+struct PairCfg {
+  static constexpr bool MX = MX_;
+  static constexpr int BN = 224;   // tokens per pair tile = MMA N
+  static constexpr int BNH = 112;  // token rows one CTA loads
+  static constexpr int STAGES = STAGES_;
+  static constexpr int CH = 2;     // 128-row token SF atoms per tile
+  static constexpr int K_STEP = MX ? 128 : 256;
+  static constexpr uint32_t W_BYTES = 128 * 128;
+  static constexpr uint32_t W_TX = MX ? 64 * 128 : 128 * 128;
+  static constexpr uint32_t X_BYTES = BNH * 128;
+  static constexpr uint32_t SFW_BYTES = MX ? 512 : 4 * 512;
+  static constexpr uint32_t SFX_BYTES = MX ? CH * 512 : 4 * CH * 512;
+  // SF atoms travel as 2-D uint64 boxes {ROW_U64, BOX_ROWS}
+  static constexpr uint32_t SFW_ROW_U64 = SFW_BYTES / 8 > 256 ? 256 : SFW_BYTES / 8;
+  static constexpr uint32_t SFW_BOX_ROWS = SFW_BYTES / (8 * SFW_ROW_U64);
+  static constexpr uint32_t SFX_ROW_U64 = SFX_BYTES / 8 > 256 ? 256 : SFX_BYTES / 8;
+  static constexpr uint32_t SFX_BOX_ROWS = SFX_BYTES / (8 * SFX_ROW_U64);
+  static constexpr uint32_t TX_CTA = W_TX + X_BYTES + SFW_BYTES + SFX_BYTES;
+  static constexpr uint32_t STAGE_BYTES =
+      (W_BYTES + X_BYTES + SFW_BYTES + SFX_BYTES + 1023) / 1024 * 1024;
+  static_assert((W_BYTES + X_BYTES) % 1024 == 0, "operand tiles must stay 1024 B aligned");
+  static constexpr int SF_BASE = 2 * BN;          // 448
+  static constexpr int SF_SLOT = 4 + 4 * CH;      // 12 columns
+  static constexpr int NSLOTS = (512 - SF_BASE) / SF_SLOT;
+  static_assert(NSLOTS >= 2, "not enough TMEM for the scale ring");
+  static_assert(SF_BASE + NSLOTS * SF_SLOT <= 512, "TMEM columns exceeded");
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr int SCHED = 8;
+  // readers of a slot: leader producer, MMA thread, 4 epilogue warps; follower
+  // producer and 4 epilogue warps
+  static constexpr uint32_t SCHED_READERS = 11;
+  static constexpr uint32_t NBARS = 2 * STAGES + 4 + 2 * SCHED + 2;
+  static constexpr uint32_t MISC_BYTES = 8 * NBARS + 32 * SCHED + 16;
+  static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + MISC_BYTES;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
+};
+
+template <class C>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+    fgg_gemm_pair_kernel(const __grid_constant__ GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+
+  const uint32_t bars = base + C::STAGES * C::STAGE_BYTES;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (C::STAGES + s); };
+  auto accf_bar = [&](int b) { return bars + 8u * (2 * C::STAGES + b); };
+  auto acce_bar = [&](int b) { return bars + 8u * (2 * C::STAGES + 2 + b); };
+  auto schedf_bar = [&](int i) { return bars + 8u * (2 * C::STAGES + 4 + i); };
+  auto schede_bar = [&](int i) { return bars + 8u * (2 * C::STAGES + 4 + C::SCHED + i); };
+  const uint32_t tmem_ready_bar = bars + 8u * (2 * C::STAGES + 4 + 2 * C::SCHED);
+  const uint32_t drain_bar = tmem_ready_bar + 8u;
+  uint8_t* const misc = gbase + C::STAGES * C::STAGE_BYTES + 8 * C::NBARS;
+  volatile SchedSlot* const ring = reinterpret_cast<volatile SchedSlot*>(misc);
+  volatile uint32_t* const tmem_holder =
+      reinterpret_cast<volatile uint32_t*>(misc + 32 * C::SCHED);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(misc + 32 * C::SCHED + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = (rank == 0);
+  const uint32_t peer = rank ^ 1u;
+
+  auto sW = [&](int s) { return base + s * C::STAGE_BYTES; };
+  auto sX = [&](int s) { return base + s * C::STAGE_BYTES + C::W_BYTES; };
+  auto sSFW = [&](int s) { return base + s * C::STAGE_BYTES + C::W_BYTES + C::X_BYTES; };
+  auto sSFX = [&](int s) {
+    return base + s * C::STAGE_BYTES + C::W_BYTES + C::X_BYTES + C::SFW_BYTES;
+  };
+  // MMA N of a tile: a multiple of 32 so that each CTA holds a multiple of 16 rows
+  auto tile_ncols = [&](int rows) -> int { return min(C::BN, (rows + 31) & ~31); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf_bar(b), 1);
+      mbar_init(acce_bar(b), 8);  // 4 epilogue warps in each CTA (leader's barrier)
+    }
+    for (int i = 0; i < C::SCHED; ++i) {
+      mbar_init(schedf_bar(i), 1);
+      mbar_init(schede_bar(i), C::SCHED_READERS);  // used on the leader
+    }
+    mbar_init(tmem_ready_bar, 1);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    if constexpr (!C::MX) {
+      const PackHeader h = *p.pack;
+      if (h.magic != kPackMagic || h.g != p.g || h.n != p.n || h.k != p.k) {
+        atomicCAS(p.status, 0, kStatusBadPack);
+        *abort_flag = 1;
+      }
+    }
+    fence_mbar_init();
+  }
+  // barrier inits visible to the peer before any of its loads or arrivals
+  cluster_sync();
+
+  if (warp == 2) {
+    tmem_alloc_pair(smem_u32(const_cast<uint32_t*>(tmem_holder)), C::TMEM_COLS);
+    tmem_relinquish_pair();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tmem_ready_bar);
+  }
+
+  const bool aborted_early = (*abort_flag != 0);
+  const uint32_t leader_schede0 = mapa_shared(schede_bar(0), 0);
+  const uint32_t leader_acce0 = mapa_shared(acce_bar(0), 0);
+  const uint32_t leader_full0 = mapa_shared(full_bar(0), 0);
+
+  // release a slot this thread has read: the leader's ring barrier counts the
+  // readers of both CTAs
+  auto release_slot = [&](int slot) {
+    if (leader)
+      mbar_arrive(schede_bar(slot));
+    else
+      mbar_arrive_remote(leader_schede0 + 8u * slot);
+  };
+
+  if (warp == 3) {
+    // ---------------------------------------------- scheduler (leader only)
+    if (lane == 0 && leader && !aborted_early) {
+      int slot = 0;
+      uint32_t sphase = 0;
+      const uint32_t remote_ring0 = mapa_shared(smem_u32(const_cast<SchedSlot*>(ring)), peer);
+      const uint32_t remote_schedf0 = mapa_shared(schedf_bar(0), peer);
+      while (true) {
+        const int t = atomicAdd(p.status + 1, 1);
+        const uint32_t tile = (t < p.num_tiles) ? __ldg(p.tiles + t) : kEndTile;
+        const SchedSlot s = make_slot<C::MX, C::BN>(p, tile);
+        if (!mbar_wait1<true>(schede_bar(slot), sphase ^ 1, abort_flag, p.status,
+                              kStatusTimeoutProducer))
+          break;
+        write_slot(ring, slot, s);
+        const uint32_t r = remote_ring0 + 32u * slot;
+        st_shared_remote_u32(r + 0, s.tile);
+        st_shared_remote_u32(r + 4, uint32_t(s.rows));
+        st_shared_remote_u32(r + 8, uint32_t(s.row0));
+        st_shared_remote_u32(r + 12, __float_as_uint(s.alpha));
+        st_shared_remote_u32(r + 16, uint32_t(s.xtile_index));
+        mbar_arrive(schedf_bar(slot));
+        mbar_arrive_remote(remote_schedf0 + 8u * slot);
+        if (++slot == C::SCHED) {
+          slot = 0;
+          sphase ^= 1;
+        }
+        if (tile == kEndTile) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 0) {
+    // ------------------------------------------------- producer (both CTAs)
+    if (lane == 0 && !aborted_early) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int slot = 0;
+      uint32_t sphase = 0;
+      uint32_t arms = 0;
+      if constexpr (C::MX) {
+        prefetch_tensormap(&p.mx_tmap_w);
+        prefetch_tensormap(&p.mx_tmap_x);
+      }
+      prefetch_tensormap(&p.sfw_map);
+      prefetch_tensormap(&p.sfx_map);
+      while (true) {
+        if (!mbar_wait1<true>(schedf_bar(slot), sphase, abort_flag, p.status,
+                              kStatusTimeoutProducer))
+          break;
+        const SchedSlot s = read_slot(ring, slot);
+        release_slot(slot);
+        if (++slot == C::SCHED) {
+          slot = 0;
+          sphase ^= 1;
+        }
+        if (s.tile == kEndTile) break;
+        const int g = int(s.tile >> 22);
+        const int nti = int((s.tile >> 11) & 0x7FFu);
+        const int xti = int(s.tile & 0x7FFu);
+        const int half = tile_ncols(s.rows) >> 1;
+        const CUtensorMap* tw;
+        const CUtensorMap* tx;
+        if constexpr (C::MX) {
+          tw = &p.mx_tmap_w;
+          tx = &p.mx_tmap_x;
+        } else {
+          tw = p.tmap_w + g;
+          tx = p.tmap_x + g;
+          tensormap_acquire(tw);
+          tensormap_acquire(tx);
+        }
+        const int wrow = nti * 256 + int(rank) * 128;
+        const int xrow = xti * C::BN + int(rank) * half;
+        const int sfw_y = ((g * p.nt128 + 2 * nti + int(rank)) * p.ksteps) * int(C::SFW_BOX_ROWS);
+        const int sfx_y = (s.xtile_index * p.ksteps) * int(C::SFX_BOX_ROWS);
+        bool ok = true;
+        for (int ks = 0; ks < p.ksteps; ++ks) {
+          if (!mbar_wait1(empty_bar(stage), phase ^ 1, abort_flag, p.status,
+                          kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2u * C::TX_CTA);
+          const uint32_t fb = leader_full0 + 8u * stage;
+          if constexpr (C::MX)
+            tma_load_3d_pair(sW(stage), tw, fb, ks * C::K_STEP, wrow, g);
+          else
+            tma_load_2d_pair(sW(stage), tw, fb, ks * 128, wrow);
+          tma_load_2d_pair(sX(stage), tx, fb, ks * 128, xrow);
+          tma_load_2d_pair(sSFW(stage), &p.sfw_map, fb, 0, sfw_y + ks * int(C::SFW_BOX_ROWS));
+          tma_load_2d_pair(sSFX(stage), &p.sfx_map, fb, 0, sfx_y + ks * int(C::SFX_BOX_ROWS));
+          ++arms;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+      // the leader's full barriers cover both CTAs' bytes: drain them before exit
+      if (leader) {
+        const uint32_t first = arms > uint32_t(C::STAGES) ? arms - C::STAGES : 0u;
+        for (uint32_t a = first; a < arms; ++a)
+          mbar_wait_one(full_bar(int(a % C::STAGES)), (a / C::STAGES) & 1u, 200000000ull);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1 && leader) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0 && !aborted_early) {
+      bool ok = mbar_wait1(tmem_ready_bar, 0, abort_flag, p.status, kStatusTimeoutMma);
+      tc_fence_after();
+      const uint32_t tmem = *tmem_holder;
+      int stage = 0;
+      uint32_t phase = 0;
+      int slot = 0;
+      uint32_t sphase = 0;
+      uint32_t lt = 0;
+      int sfslot = 0;
+      bool issued_any = false;
+      while (ok) {
+        if (!mbar_wait1<true>(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutMma))
+          break;
+        const SchedSlot s = read_slot(ring, slot);
+        mbar_arrive(schede_bar(slot));
+        if (++slot == C::SCHED) {
+          slot = 0;
+          sphase ^= 1;
+        }
+        if (s.tile == kEndTile) break;
+        const int ncols = tile_ncols(s.rows);
+        const int nsfx = (ncols + 127) >> 7;  // token SF atoms this tile needs
+        const uint32_t b = lt & 1u;
+        if (!mbar_wait1(acce_bar(b), ((lt >> 1) & 1u) ^ 1u, abort_flag, p.status,
+                        kStatusTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + b * C::BN;
+        const uint32_t idesc =
+            C::MX ? 0u : idesc_block_scaled(kFmtNvf4E2M1, kFmtNvf4E2M1, 0, 256, ncols, 0, 0);
+        for (int ks = 0; ks < p.ksteps; ++ks) {
+          if (!mbar_wait1(full_bar(stage), phase, abort_flag, p.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = desc_k_sw128(sW(stage));
+          const uint64_t bdesc = desc_k_sw128(sX(stage));
+          if constexpr (C::MX) {
+            const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
+            tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(stage)));
+            for (int c = 0; c < nsfx; ++c)
+              tc_cp_sf_pair(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(stage) + c * 512));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t idj =
+                  idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 256, ncols, j, j);
+              tc_mma_mxf8f6f4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
+                                   (tmem + col) | (uint32_t(j) << 30),
+                                   (tmem + col + 4) | (uint32_t(j) << 30), (ks | j) != 0 ? 1u : 0u);
+            }
+            sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
+              tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(stage) + j * 512));
+              for (int c = 0; c < nsfx; ++c)
+                tc_cp_sf_pair(tmem + col + 4 + 4 * c,
+                              desc_sf_atom(sSFX(stage) + (j * C::CH + c) * 512));
+              tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col,
+                               tmem + col + 4, (ks | j) != 0 ? 1u : 0u);
+              sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+            }
+          }
+          tc_commit_pair(empty_bar(stage), 0x3);
+          issued_any = true;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(accf_bar(b), 0x3);
+        ++lt;
+      }
+      if (issued_any) {
+        tc_commit_pair(drain_bar, 0x1);
+        if (!mbar_wait_one(drain_bar, 0, 200000000ull))
+          atomicCAS(p.status, 0, kStatusTimeoutDrain);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4 && !aborted_early) {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    bool ok = mbar_wait(tmem_ready_bar, 0, abort_flag, p.status, kStatusTimeoutEpilogue);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    int slot = 0;
+    uint32_t sphase = 0;
+    uint32_t lt = 0;
+    while (ok) {
+      if (!mbar_wait<true>(schedf_bar(slot), sphase, abort_flag, p.status,
+                           kStatusTimeoutEpilogue))
+        break;
+      const SchedSlot s = read_slot(ring, slot);
+      __syncwarp();
+      if (lane == 0) release_slot(slot);
+      if (++slot == C::SCHED) {
+        slot = 0;
+        sphase ^= 1;
+      }
+      if (s.tile == kEndTile) break;
+      const int nti = int((s.tile >> 11) & 0x7FFu);
+      const int ncols = tile_ncols(s.rows);
+      const uint32_t b = lt & 1u;
+      if (!mbar_wait(accf_bar(b), (lt >> 1) & 1u, abort_flag, p.status, kStatusTimeoutEpilogue))
+        break;
+      tc_fence_after();
+      epilogue_tile(p.out, p.n, nti * 256 + int(rank) * 128 + q * 32 + lane, size_t(s.row0),
+                    s.rows, ncols, s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(acce_bar(b));
+        else
+          mbar_arrive_remote(leader_acce0 + 8u * b);
+      }
+      ++lt;
+    }
+  }
+
+  __syncthreads();
+  // the leader's MMAs write the follower's TMEM and read its shared memory:
+  // neither CTA frees anything before both are done
+  cluster_sync();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(*tmem_holder, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.status + 2, 1) == int(gridDim.x) - 1) {
+      atomicExch(p.status + 1, 0);
+      atomicExch(p.status + 2, 0);
+    }
+  }
+}
+
+// Set the kernel's dynamic shared memory limit (once per device), then launch
+// one CTA pair per two SMs, or one per tile when there are fewer tiles.  Host only.
+template <class C>
+cudaError_t launch_pair(const GemmParams& gp, int sm_count, cudaStream_t s) {
+  static int configured_device = -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (configured_device != dev) {
+    e = cudaFuncSetAttribute(fgg_gemm_pair_kernel<C>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  const int pairs_avail = sm_count / 2;
+  const int pairs = gp.num_tiles < pairs_avail ? (gp.num_tiles > 0 ? gp.num_tiles : 1) : pairs_avail;
+  fgg_gemm_pair_kernel<C><<<2 * pairs, 256, C::SMEM_BYTES, s>>>(gp);
+  return cudaGetLastError();
 }
 
 // Set the kernel's dynamic shared memory limit (once per device), then launch

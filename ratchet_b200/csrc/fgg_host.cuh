@@ -13,7 +13,7 @@
 #include <cstdint>
 #include <cstdio>
 
-#include "../../include/fgg_api.h"
+#include "fgg_api.h"  // include/ is on the include path
 
 namespace fgg {
 
@@ -48,6 +48,10 @@ int encode_3d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uin
               uint32_t b0, uint32_t b1, uint32_t b2);
 int encode_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t d0,
               uint64_t d1, uint64_t stride1_bytes, uint32_t b0, uint32_t b1);
+// A contiguous byte buffer viewed as `rows` rows of `row_u64` uint64 values,
+// unswizzled, box {row_u64, box_rows}: how packed scale-factor atoms travel.
+int encode_u64_rows(CUtensorMap* out, const void* base, uint64_t rows, uint32_t row_u64,
+                    uint32_t box_rows);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

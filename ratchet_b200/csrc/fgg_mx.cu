@@ -24,7 +24,8 @@ namespace {
 
 constexpr int kMxBlockM = 224;  // token tile = the reference's ALIGN (kernel.py:274)
 
-using CfgMx = EngineCfg<true, kMxBlockM, 4>;
+using CfgMx = EngineCfg<true, kMxBlockM, 4>;  // one CTA per tile (N % 256 != 0)
+using CfgMxPair = PairCfg<true, 6>;          // CTA pairs, 256 x 224 tiles
 
 struct MxPrepParams {
   const float* a_sf;        // [M_total, K/128]
@@ -34,7 +35,7 @@ struct MxPrepParams {
   uint8_t* sfw_out;         // [G][NT][KS][512]
   uint32_t* tiles_out;      // [XB * NT]
   int* status;
-  int32_t m_total, n, k, g, nt, ksteps, xblocks;
+  int32_t m_total, n, k, g, nt, nt128, ksteps, xblocks;
   int32_t blocks_tiles, blocks_sfx;
 };
 
@@ -90,13 +91,13 @@ __global__ void __launch_bounds__(256) mx_prepare_kernel(const __grid_constant__
   blk -= p.blocks_sfx;
   {
     const int64_t line = int64_t(blk) * blockDim.x + threadIdx.x;
-    if (line >= int64_t(p.g) * p.nt * p.ksteps * 32) return;
+    if (line >= int64_t(p.g) * p.nt128 * p.ksteps * 32) return;
     const int r0 = int(line & 31);
     int64_t rest = line >> 5;
     const int ks = int(rest % p.ksteps);
     rest /= p.ksteps;
-    const int nti = int(rest % p.nt);
-    const int g = int(rest / p.nt);
+    const int nti = int(rest % p.nt128);
+    const int g = int(rest / p.nt128);
     const int kw = p.k / 32;  // weight scales per row
     uint32_t v[4];
 #pragma unroll
@@ -108,13 +109,14 @@ __global__ void __launch_bounds__(256) mx_prepare_kernel(const __grid_constant__
               (e8m0_byte(s.w) << 24);
     }
     uint4* dst = reinterpret_cast<uint4*>(
-        p.sfw_out + ((size_t(g) * p.nt + nti) * p.ksteps + ks) * 512u + size_t(r0) * 16u);
+        p.sfw_out + ((size_t(g) * p.nt128 + nti) * p.ksteps + ks) * 512u + size_t(r0) * 16u);
     *dst = make_uint4(v[0], v[1], v[2], v[3]);
   }
 }
 
 struct MxLayout {
-  int xblocks = 0, nt = 0, ksteps = 0, num_tiles = 0;
+  bool pair = false;
+  int xblocks = 0, nt = 0, nt128 = 0, ksteps = 0, num_tiles = 0;
   size_t status = 0, tiles = 0, sfx = 0, sfw = 0, total = 0;
 };
 
@@ -129,7 +131,9 @@ int mx_plan(const FggMxProblem* p, MxLayout* L) {
   if (p->k <= 0 || p->k % 128 != 0)
     return set_error(FGG_EBADSHAPE, "K=%d is not a multiple of BLOCK_K=128", p->k);
   L->xblocks = (p->m_total + kMxBlockM - 1) / kMxBlockM;
-  L->nt = p->n / 128;
+  L->pair = (p->n % 256 == 0);
+  L->nt128 = p->n / 128;
+  L->nt = L->pair ? p->n / 256 : L->nt128;
   L->ksteps = p->k / 128;
   if (L->xblocks > 2047 || L->nt > 2047) return set_error(FGG_EBADSHAPE, "problem too large");
   L->num_tiles = L->xblocks * L->nt;
@@ -137,7 +141,7 @@ int mx_plan(const FggMxProblem* p, MxLayout* L) {
   L->status = cv.take(kStatusBytes, 256);
   L->tiles = cv.take(size_t(std::max(L->num_tiles, 1)) * 4, 256);
   L->sfx = cv.take(size_t(std::max(L->xblocks, 1)) * L->ksteps * 1024, 256);
-  L->sfw = cv.take(size_t(p->num_groups) * L->nt * L->ksteps * 512, 256);
+  L->sfw = cv.take(size_t(p->num_groups) * L->nt128 * L->ksteps * 512, 256);
   L->total = cv.off;
   return FGG_OK;
 }
@@ -194,11 +198,12 @@ int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
     pp.k = p->k;
     pp.g = p->num_groups;
     pp.nt = L.nt;
+    pp.nt128 = L.nt128;
     pp.ksteps = L.ksteps;
     pp.xblocks = L.xblocks;
     pp.blocks_tiles = (L.num_tiles + 255) / 256;
     pp.blocks_sfx = int((int64_t(L.xblocks) * L.ksteps * 64 + 255) / 256);
-    const int64_t sfw_lines = int64_t(p->num_groups) * L.nt * L.ksteps * 32;
+    const int64_t sfw_lines = int64_t(p->num_groups) * L.nt128 * L.ksteps * 32;
     const int64_t blocks = int64_t(pp.blocks_tiles) + pp.blocks_sfx + (sfw_lines + 255) / 256;
     mx_prepare_kernel<<<int(blocks), 256, 0, s>>>(pp);
     FGG_CUDA_CHECK(cudaGetLastError());
@@ -213,7 +218,8 @@ int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
                          uint64_t(p->k) / 2, uint64_t(p->n) * uint64_t(p->k) / 2, 128, 128, 1))
     return rc;
   if (int rc = encode_2d(&gp.mx_tmap_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, p->a, uint64_t(p->k),
-                         uint64_t(p->m_total), uint64_t(p->k), 128, kMxBlockM))
+                         uint64_t(p->m_total), uint64_t(p->k), 128,
+                         L.pair ? CfgMxPair::BNH : kMxBlockM))
     return rc;
   gp.sfw = ws + L.sfw;
   gp.sfx = ws + L.sfx;
@@ -227,7 +233,20 @@ int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
   gp.num_tiles = L.num_tiles;
   gp.ksteps = L.ksteps;
   gp.nt = L.nt;
-  const cudaError_t e = launch_engine<CfgMx>(gp, dev.sm_count, s);
+  gp.nt128 = L.nt128;
+  cudaError_t e;
+  if (L.pair) {
+    if (int rc = encode_u64_rows(&gp.sfw_map, gp.sfw,
+                                 uint64_t(p->num_groups) * L.nt128 * L.ksteps,
+                                 CfgMxPair::SFW_ROW_U64, CfgMxPair::SFW_BOX_ROWS))
+      return rc;
+    if (int rc = encode_u64_rows(&gp.sfx_map, gp.sfx, uint64_t(L.xblocks) * L.ksteps,
+                                 CfgMxPair::SFX_ROW_U64, CfgMxPair::SFX_BOX_ROWS))
+      return rc;
+    e = launch_pair<CfgMxPair>(gp, dev.sm_count, s);
+  } else {
+    e = launch_engine<CfgMx>(gp, dev.sm_count, s);
+  }
   if (e != cudaSuccess) return set_error(FGG_ECUDA, "MX GEMM launch failed: %s", cudaGetErrorString(e));
   return FGG_OK;
 }

@@ -183,8 +183,9 @@ __global__ void __launch_bounds__(256) nvfp4_pack_weights_kernel(const __grid_co
 }
 
 // ------------------------------------------------------------ host side
-using CfgPrefill = EngineCfg<false, 224, 4>;
-using CfgDecode = EngineCfg<false, 16, 8>;
+using CfgPrefill = EngineCfg<false, 224, 4>;   // one CTA per tile (N % 256 != 0)
+using CfgDecode = EngineCfg<false, 16, 8>;     // every group has M <= 16
+using CfgPair = PairCfg<false, 6>;             // CTA pairs, 256 x 224 tiles
 
 struct PackLayout {
   size_t header, tmaps, sfw, total;
@@ -202,7 +203,9 @@ static PackLayout pack_layout(int g, int n, int k) {
 
 struct WsLayout {
   int bn = 0, ch = 0, stages = 0;
-  int nk64p = 0, nk256 = 0, nt = 0;
+  bool pair = false;
+  int box_rows = 0;  // token rows per TMA box (a pair CTA loads half a tile)
+  int nk64p = 0, nk256 = 0, nt = 0, nt128 = 0;
   int num_tiles = 0, xt_total = 0;
   std::vector<int32_t> xtile_begin, tile_begin, out_row;
   size_t status = 0, tmaps = 0, ginfo = 0, tiles = 0, sfx = 0, total = 0;
@@ -225,12 +228,15 @@ static int plan(const FggNvfp4Problem* p, WsLayout* L) {
     maxm = std::max(maxm, p->m[g]);
   }
   const bool decode = maxm <= 16;
-  L->bn = decode ? CfgDecode::BN : CfgPrefill::BN;
+  L->pair = !decode && (p->n % 256 == 0);
+  L->bn = decode ? CfgDecode::BN : CfgPrefill::BN;  // 224 for both the pair and single CTA
   L->ch = decode ? CfgDecode::CH : CfgPrefill::CH;
-  L->stages = decode ? CfgDecode::STAGES : CfgPrefill::STAGES;
+  L->stages = decode ? CfgDecode::STAGES : (L->pair ? CfgPair::STAGES : CfgPrefill::STAGES);
+  L->box_rows = L->pair ? CfgPair::BNH : L->bn;
   L->nk256 = (p->k + 255) / 256;
   L->nk64p = 4 * L->nk256;
-  L->nt = p->n / 128;
+  L->nt128 = p->n / 128;
+  L->nt = L->pair ? p->n / 256 : L->nt128;
   L->xtile_begin.assign(G + 1, 0);
   L->tile_begin.assign(G + 1, 0);
   L->out_row.assign(G, 0);
@@ -366,7 +372,7 @@ int prepare_impl(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8_t
   static thread_local PrepParams pp;  // ~17 KB: keep it off the stack
   memset(&pp, 0, sizeof(pp));
   if (int rc = encode_u8_2d(&pp.tmpl, p->a[first], uint64_t(p->k) / 2, uint64_t(p->m[first]), 128,
-                            uint32_t(L.bn)))
+                            uint32_t(L.box_rows)))
     return rc;
   for (int g = 0; g < G; ++g) {
     pp.a[g] = static_cast<const uint8_t*>(p->a[g]);
@@ -428,8 +434,24 @@ int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uin
   gp.num_tiles = L.num_tiles;
   gp.ksteps = L.nk256;
   gp.nt = L.nt;
-  const cudaError_t e = (L.bn == CfgDecode::BN) ? launch_engine<CfgDecode>(gp, dev.sm_count, s)
-                                                 : launch_engine<CfgPrefill>(gp, dev.sm_count, s);
+  gp.nt128 = L.nt128;
+  cudaError_t e;
+  if (L.pair) {
+    // scale-factor atoms as 2-D uint64 tensors: weights 2 KB per (group, 128-row
+    // tile, K step); tokens 4 KB per (token tile, K step) as two 2 KB rows
+    if (int rc = encode_u64_rows(&gp.sfw_map, gp.sfw, uint64_t(G) * L.nt128 * L.nk256,
+                                 CfgPair::SFW_ROW_U64, CfgPair::SFW_BOX_ROWS))
+      return rc;
+    if (int rc = encode_u64_rows(&gp.sfx_map, gp.sfx,
+                                 uint64_t(L.xt_total) * L.nk256 * CfgPair::SFX_BOX_ROWS,
+                                 CfgPair::SFX_ROW_U64, CfgPair::SFX_BOX_ROWS))
+      return rc;
+    e = launch_pair<CfgPair>(gp, dev.sm_count, s);
+  } else if (L.bn == CfgDecode::BN) {
+    e = launch_engine<CfgDecode>(gp, dev.sm_count, s);
+  } else {
+    e = launch_engine<CfgPrefill>(gp, dev.sm_count, s);
+  }
   if (e != cudaSuccess) return set_error(FGG_ECUDA, "GEMM launch failed: %s", cudaGetErrorString(e));
   return FGG_OK;
 }

@@ -81,7 +81,8 @@ def _ws_bytes_py(ms, n, k):
     nk256 = (k + 255) // 256
     nk64p = 4 * nk256
     xts = sum((m + bn - 1) // bn for m in ms)
-    tiles = xts * (n // 128)
+    pair = bn == 224 and n % 256 == 0   # CTA pairs cover 256 weight rows per tile
+    tiles = xts * (n // (256 if pair else 128))
     off = 0
     def take(nbytes, align):
         nonlocal off
@@ -96,7 +97,8 @@ def _ws_bytes_py(ms, n, k):
 
 
 @pytest.mark.parametrize("ms,n,k", [([128], 256, 512), ([0, 1, 224, 225], 256, 768),
-                                    ([3, 16, 9], 7168, 2048), ([881, 676, 555], 4096, 7168)])
+                                    ([3, 16, 9], 7168, 2048), ([881, 676, 555], 4096, 7168),
+                                    ([300, 40], 384, 512)])
 def test_workspace_bytes(L, ms, n, k):
     p, keep = _problem(ms, n, k)
     assert L.fgg_nvfp4_workspace_bytes(p) == _ws_bytes_py(ms, n, k)

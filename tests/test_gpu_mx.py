@@ -29,8 +29,10 @@ def _check(prob, c):
 
 
 @pytest.mark.parametrize("rows", [[224], [100, 0, 300, 1], [500, 224, 225]])
-def test_mx_small(cuda_device, rows):
-    prob = mref.random_problem(rows, 256, 512, seed=len(rows))
+@pytest.mark.parametrize("n", [256, 384])
+def test_mx_small(cuda_device, rows, n):
+    """N=256 runs on CTA pairs, N=384 on single CTAs."""
+    prob = mref.random_problem(rows, n, 512, seed=len(rows))
     _check(prob, _run(prob, cuda_device))
 
 

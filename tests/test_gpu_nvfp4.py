@@ -81,6 +81,20 @@ def test_ragged_groups_and_k_tails(cuda_device, k):
     _run_and_check(prob, 256, k, cuda_device)
 
 
+@pytest.mark.parametrize("n", [384, 640])
+def test_single_cta_path(cuda_device, n):
+    """N % 256 != 0 takes the one-CTA kernel (pairs need 256 weight rows)."""
+    prob = ref.random_problem([300, 17, 224, 1], n, 512, seed=n)
+    _run_and_check(prob, n, 512, cuda_device)
+
+
+@pytest.mark.parametrize("ms", [[32], [33], [200], [230, 31, 96]])
+def test_pair_partial_tiles(cuda_device, ms):
+    """Pair tiles whose token count is not a multiple of 32 split unevenly."""
+    prob = ref.random_problem(ms, 512, 768, seed=sum(ms))
+    _run_and_check(prob, 512, 768, cuda_device)
+
+
 def test_decode_tiles(cuda_device):
     """All groups M <= 16 take the BN=16 decode configuration."""
     rng = np.random.default_rng(3)
