@@ -16,7 +16,8 @@
 //   warp 2     TMEM allocator
 //   warp 3     scheduler: claims tiles from a global atomic counter (dynamic
 //              persistent schedule) and publishes each tile with its metadata
-//              in an 8-deep shared-memory ring, ahead of every other role
+//              in an 8-deep shared-memory ring, one tile ahead of the
+//              producer (the ring's depth covers the roles that lag behind)
 //   warps 4-7  epilogue: tcgen05.ld (each warp its 32-lane quadrant) -> fp32
 //              x alpha -> bf16 -> global, overlapped with the next tile's MMAs
 // The producer and MMA roles run on ONE thread each: between two K steps they
@@ -197,8 +198,9 @@ struct EngineCfg {
   static constexpr int SCHED = 8;  // schedule ring depth
   // readers of a schedule slot: producer, MMA thread, 4 epilogue warps
   static constexpr uint32_t SCHED_READERS = 6;
-  // barriers: full[S] empty[S] accf[2] acce[2] schedf[SCHED] schede[SCHED] tmem_ready drain
-  static constexpr uint32_t NBARS = 2 * STAGES + 4 + 2 * SCHED + 2;
+  // barriers: full[S] empty[S] accf[2] acce[2] schedf[SCHED] schede[SCHED] tmem_ready
+  // drain taken
+  static constexpr uint32_t NBARS = 2 * STAGES + 4 + 2 * SCHED + 3;
   static constexpr uint32_t MISC_BYTES = 8 * NBARS + 32 * SCHED + 16;
   static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + MISC_BYTES;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
@@ -220,6 +222,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
   auto schede_bar = [&](int i) { return bars + 8u * (2 * C::STAGES + 4 + C::SCHED + i); };
   const uint32_t tmem_ready_bar = bars + 8u * (2 * C::STAGES + 4 + 2 * C::SCHED);
   const uint32_t drain_bar = tmem_ready_bar + 8u;
+  const uint32_t taken_bar = tmem_ready_bar + 16u;  // producer took a slot
   uint8_t* const misc = gbase + C::STAGES * C::STAGE_BYTES + 8 * C::NBARS;
   volatile SchedSlot* const ring = reinterpret_cast<volatile SchedSlot*>(misc);
   volatile uint32_t* const tmem_holder =
@@ -251,6 +254,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
     }
     mbar_init(tmem_ready_bar, 1);
     mbar_init(drain_bar, 1);
+    mbar_init(taken_bar, 1);
     *abort_flag = 0;
     if constexpr (!C::MX) {
       // A pack built for a different problem is refused before any load.
@@ -279,7 +283,14 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
     if (lane == 0 && !aborted_early) {
       int slot = 0;
       uint32_t sphase = 0;
-      while (true) {
+      for (uint32_t n = 0;; ++n) {
+        // Claim tile n only once the producer has taken tile n-1: a CTA holds
+        // at most one tile it has not started, so the tail of the tile list
+        // spreads over every CTA.  (The producer cannot take tile n before it
+        // is published, so the parity below is unambiguous.)
+        if (n > 0 && !mbar_wait1(taken_bar, (n - 1) & 1u, abort_flag, p.status,
+                                 kStatusTimeoutProducer))
+          break;
         const int t = atomicAdd(p.status + 1, 1);
         const uint32_t tile = (t < p.num_tiles) ? __ldg(p.tiles + t) : kEndTile;
         const SchedSlot s = make_slot<C::MX, C::BN>(p, tile);
@@ -313,6 +324,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
           break;
         const SchedSlot s = read_slot(ring, slot);
         mbar_arrive(schede_bar(slot));
+        mbar_arrive(taken_bar);
         if (++slot == C::SCHED) {
           slot = 0;
           sphase ^= 1;
@@ -390,7 +402,6 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
         }
         if (s.tile == kEndTile) break;
         const int ncols = min(C::BN, (s.rows + 15) & ~15);
-        const int nsfx = (ncols + 127) >> 7;  // token SF atoms this tile needs
         const uint32_t b = lt & 1u;
         if (!mbar_wait1(acce_bar(b), ((lt >> 1) & 1u) ^ 1u, abort_flag, p.status,
                         kStatusTimeoutMma))
@@ -410,7 +421,8 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
           if constexpr (C::MX) {
             const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
             tc_cp_sf(tmem + col, desc_sf_atom(sSFW(stage)));
-            for (int c = 0; c < nsfx; ++c)
+#pragma unroll
+            for (int c = 0; c < C::CH; ++c)
               tc_cp_sf(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(stage) + c * 512));
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -428,7 +440,8 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
             for (int j = 0; j < 4; ++j) {
               const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
               tc_cp_sf(tmem + col, desc_sf_atom(sSFW(stage) + j * 512));
-              for (int c = 0; c < nsfx; ++c)
+#pragma unroll
+              for (int c = 0; c < C::CH; ++c)
                 tc_cp_sf(tmem + col + 4 + 4 * c,
                          desc_sf_atom(sSFX(stage) + (j * C::CH + c) * 512));
               // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
@@ -558,7 +571,7 @@ struct PairCfg {
   // readers of a slot: leader producer, MMA thread, 4 epilogue warps; follower
   // producer and 4 epilogue warps
   static constexpr uint32_t SCHED_READERS = 11;
-  static constexpr uint32_t NBARS = 2 * STAGES + 4 + 2 * SCHED + 2;
+  static constexpr uint32_t NBARS = 2 * STAGES + 4 + 2 * SCHED + 3;
   static constexpr uint32_t MISC_BYTES = 8 * NBARS + 32 * SCHED + 16;
   static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + MISC_BYTES;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
@@ -581,6 +594,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   auto schede_bar = [&](int i) { return bars + 8u * (2 * C::STAGES + 4 + C::SCHED + i); };
   const uint32_t tmem_ready_bar = bars + 8u * (2 * C::STAGES + 4 + 2 * C::SCHED);
   const uint32_t drain_bar = tmem_ready_bar + 8u;
+  const uint32_t taken_bar = tmem_ready_bar + 16u;  // producer took a slot
   uint8_t* const misc = gbase + C::STAGES * C::STAGE_BYTES + 8 * C::NBARS;
   volatile SchedSlot* const ring = reinterpret_cast<volatile SchedSlot*>(misc);
   volatile uint32_t* const tmem_holder =
@@ -617,6 +631,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     }
     mbar_init(tmem_ready_bar, 1);
     mbar_init(drain_bar, 1);
+    mbar_init(taken_bar, 1);
     *abort_flag = 0;
     if constexpr (!C::MX) {
       const PackHeader h = *p.pack;
@@ -659,7 +674,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       uint32_t sphase = 0;
       const uint32_t remote_ring0 = mapa_shared(smem_u32(const_cast<SchedSlot*>(ring)), peer);
       const uint32_t remote_schedf0 = mapa_shared(schedf_bar(0), peer);
-      while (true) {
+      for (uint32_t n = 0;; ++n) {
+        // one unstarted tile per pair at most (see the single-CTA kernel)
+        if (n > 0 && !mbar_wait1(taken_bar, (n - 1) & 1u, abort_flag, p.status,
+                                 kStatusTimeoutProducer))
+          break;
         const int t = atomicAdd(p.status + 1, 1);
         const uint32_t tile = (t < p.num_tiles) ? __ldg(p.tiles + t) : kEndTile;
         const SchedSlot s = make_slot<C::MX, C::BN>(p, tile);
@@ -703,6 +722,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           break;
         const SchedSlot s = read_slot(ring, slot);
         release_slot(slot);
+        if (leader) mbar_arrive(taken_bar);
         if (++slot == C::SCHED) {
           slot = 0;
           sphase ^= 1;
@@ -783,7 +803,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         }
         if (s.tile == kEndTile) break;
         const int ncols = tile_ncols(s.rows);
-        const int nsfx = (ncols + 127) >> 7;  // token SF atoms this tile needs
         const uint32_t b = lt & 1u;
         if (!mbar_wait1(acce_bar(b), ((lt >> 1) & 1u) ^ 1u, abort_flag, p.status,
                         kStatusTimeoutMma))
@@ -803,7 +822,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           if constexpr (C::MX) {
             const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
             tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(stage)));
-            for (int c = 0; c < nsfx; ++c)
+#pragma unroll
+            for (int c = 0; c < C::CH; ++c)
               tc_cp_sf_pair(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(stage) + c * 512));
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -819,7 +839,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             for (int j = 0; j < 4; ++j) {
               const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
               tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(stage) + j * 512));
-              for (int c = 0; c < nsfx; ++c)
+#pragma unroll
+              for (int c = 0; c < C::CH; ++c)
                 tc_cp_sf_pair(tmem + col + 4 + 4 * c,
                               desc_sf_atom(sSFX(stage) + (j * C::CH + c) * 512));
               tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col,
