@@ -12,7 +12,6 @@
 
 #include <algorithm>
 #include <cstring>
-#include <vector>
 
 #include "fgg_engine.cuh"
 #include "fgg_host.cuh"
@@ -207,7 +206,10 @@ struct WsLayout {
   int box_rows = 0;  // token rows per TMA box (a pair CTA loads half a tile)
   int nk64p = 0, nk256 = 0, nt = 0, nt128 = 0;
   int num_tiles = 0, xt_total = 0;
-  std::vector<int32_t> xtile_begin, tile_begin, out_row;
+  // per-group bookkeeping in fixed arrays: planning a call touches no host heap
+  int32_t xtile_begin[FGG_MAX_GROUPS + 1];
+  int32_t tile_begin[FGG_MAX_GROUPS + 1];
+  int32_t out_row[FGG_MAX_GROUPS];
   size_t status = 0, tmaps = 0, ginfo = 0, tiles = 0, sfx = 0, total = 0;
 };
 
@@ -237,9 +239,6 @@ static int plan(const FggNvfp4Problem* p, WsLayout* L) {
   L->nk64p = 4 * L->nk256;
   L->nt128 = p->n / 128;
   L->nt = L->pair ? p->n / 256 : L->nt128;
-  L->xtile_begin.assign(G + 1, 0);
-  L->tile_begin.assign(G + 1, 0);
-  L->out_row.assign(G, 0);
   int64_t rows = 0, xts = 0, tiles = 0;
   for (int g = 0; g < G; ++g) {
     L->out_row[g] = int32_t(rows);
