@@ -5,9 +5,10 @@ Drop-in for the reference operator `fp4_grouped_gemm(a, a_sf, b, b_sf, m_indices
 per-group-list operator `nvfp4_grouped_gemm`, both on one hand-written tcgen05
 kernel behind the C ABI in include/fgg_api.h.
 """
+from ._lib import FggError
 from .ops import (WeightPack, clear_caches, fp4_grouped_gemm, last_status, nvfp4_grouped_gemm,
                   pack_weights, quantize_nvfp4)
 
 __all__ = ["fp4_grouped_gemm", "nvfp4_grouped_gemm", "pack_weights", "WeightPack",
-           "quantize_nvfp4", "last_status", "clear_caches"]
+           "quantize_nvfp4", "last_status", "clear_caches", "FggError"]
 __version__ = "0.1.0"
