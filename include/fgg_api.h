@@ -121,6 +121,36 @@ FGG_API int fgg_nvfp4_prepare(const FggNvfp4Problem* p, void* workspace, size_t 
 FGG_API int fgg_nvfp4_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace, size_t ws_bytes,
                    void* stream);
 
+/* No counterpart in the reference (its operator always allocates its scale
+ * repack and outputs through torch).  fgg_nvfp4_grouped_gemm for callers that
+ * cannot allocate device memory at call time: a serving loop that owns a
+ * fixed memory budget, or a host without an allocator on the call path.  The
+ * call runs the same kernels with its scratch in a fixed device array inside
+ * this library (FGG_NOALLOC_SCRATCH_BYTES per device) instead of a caller
+ * workspace; it allocates nothing: no cudaMalloc / cudaFree and no allocating
+ * library call, and its host-side bookkeeping lives in fixed arrays.
+ *   - Limit: a problem whose fgg_nvfp4_workspace_bytes exceeds
+ *     FGG_NOALLOC_SCRATCH_BYTES is refused with FGG_EWORKSPACE before any
+ *     device work (use fgg_nvfp4_grouped_gemm with a caller workspace).
+ *   - Nothing in the scratch has to start at zero: every call rewrites its
+ *     status words and tile counters before the GEMM kernel reads them, and
+ *     writes every other byte it later reads.
+ *   - One scratch per device, shared by every call on that device: calls
+ *     whose device work overlaps in time (different streams, or host threads
+ *     without ordering between them) corrupt each other.  Issue them on one
+ *     stream, or order them with events.
+ *   - The first call on each device performs one-time set-up (the scratch
+ *     array's address via cudaGetSymbolAddress, which also loads its module,
+ *     and the kernels' shared-memory attribute); make that first call before
+ *     any stream capture.
+ *   - status_out: optional device pointer to one int32; when non-null the call
+ *     ends with a stream-ordered copy of the device status word there
+ *     (0 = clean; non-zero = a bounded wait gave up), since the scratch that
+ *     holds it is not visible to the caller. */
+#define FGG_NOALLOC_SCRATCH_BYTES (32u << 20)
+FGG_API int fgg_nvfp4_grouped_gemm_noalloc(const FggNvfp4Problem* p, const void* pack,
+                                           void* status_out, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* MXFP8 x MXFP4 contiguous M-grouped GEMM (reference operator)              */
 /* ------------------------------------------------------------------------ */

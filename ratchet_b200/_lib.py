@@ -20,6 +20,7 @@ FGG_ECUDA = 5
 FGG_ETIMEOUT = 6
 FGG_EARCH = 7
 FGG_MAX_GROUPS = 512
+FGG_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 _VOIDP = ctypes.c_void_p
 _PTRS = ctypes.POINTER(ctypes.c_void_p)
@@ -60,6 +61,7 @@ _SIGS = {
     "fgg_nvfp4_grouped_gemm": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_nvfp4_prepare": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_nvfp4_gemm": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, ctypes.c_size_t, _VOIDP]),
+    "fgg_nvfp4_grouped_gemm_noalloc": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, _VOIDP]),
     "fgg_mx_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(FggMxProblem)]),
     "fgg_mx_grouped_gemm": (ctypes.c_int, [ctypes.POINTER(FggMxProblem), _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_amax": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int64, _VOIDP, _VOIDP]),

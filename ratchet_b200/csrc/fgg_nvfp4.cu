@@ -499,3 +499,40 @@ int fgg_nvfp4_grouped_gemm(const FggNvfp4Problem* p, const void* pack, void* wor
 }
 
 }  // extern "C"
+
+namespace fgg {
+int noalloc_scratch(void** out);  // fgg_scratch.cu
+}  // namespace fgg
+
+extern "C" {
+
+int fgg_nvfp4_grouped_gemm_noalloc(const FggNvfp4Problem* p, const void* pack, void* status_out,
+                                   void* stream) {
+  WsLayout L;
+  if (int rc = plan(p, &L)) return rc;
+  // refused before any device work
+  if (L.total > size_t(FGG_NOALLOC_SCRATCH_BYTES))
+    return set_error(FGG_EWORKSPACE,
+                     "problem needs %zu bytes of scratch, the static scratch holds %zu; "
+                     "use fgg_nvfp4_grouped_gemm with a caller workspace",
+                     L.total, size_t(FGG_NOALLOC_SCRATCH_BYTES));
+  if (status_out != nullptr && !aligned4(status_out))
+    return set_error(FGG_EALIGN, "status_out is not 4-byte aligned");
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  int first = -1;
+  if (int rc = check_problem(p, L, scratch, size_t(FGG_NOALLOC_SCRATCH_BYTES), &first)) return rc;
+  if (L.num_tiles > 0 && pack == nullptr) return set_error(FGG_EINVAL, "pack is null");
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  if (int rc = prepare_impl(p, L, first, ws, s)) return rc;
+  if (int rc = gemm_impl(p, L, pack, ws, dev, s)) return rc;
+  if (status_out != nullptr)
+    FGG_CUDA_CHECK(
+        cudaMemcpyAsync(status_out, ws + L.status, sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+  return FGG_OK;
+}
+
+}  // extern "C"
