@@ -14,8 +14,9 @@ timed between barriers, max over ranks.
   value       TFLOP/s of the public operator call (prepare + GEMM kernels)
               with inputs resident in HBM, K steps back to back; R rotating
               input sets whose total exceeds the 126 MB L2 (config.l2)
-  e2e         the same call fed from pinned host buffers: per step H2D of the
-              activation codes + scales, the call, D2H of every output
+  e2e         the same call fed from pinned host buffers: per step one H2D of
+              the activation codes + scales, the call, one D2H of the output,
+              pipelined over three streams (copy-in / compute / copy-out)
   roofline    the GEMM kernel alone (CUDA events around K launches on the
               launching stream) against 4 x the measured dense bf16 peak
               (B200's dense FP4 rate is 4x its bf16 rate), or against the
@@ -29,7 +30,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -86,56 +86,69 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling while the timed region runs."""
+    """SM clock, power and throttle reasons sampled through NVML (the source
+    nvidia-smi reads) every ~1 ms on a thread while the timed region runs.
+    The GPU is found by UUID, so CUDA_VISIBLE_DEVICES remapping is harmless."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+    def __init__(self, device: int):
+        self.device = device
+        self.samples: list[tuple[int, int, int]] = []
+        self.err = None
+        self.nv = None
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.nv = pynvml
+        except Exception as e:  # no NVML: report why instead of clocks
+            self.err = f"nvml unavailable: {e}"
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        self.stop_flag = threading.Event()
+        if self.nv is None:
+            return
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv, h = self.nv, self.h
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h),
+                                     nv.nvmlDeviceGetPowerUsage(h)))
+            except Exception as e:
+                self.err = str(e)
+                return
+            time.sleep(0.001)
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        self.stop_flag.set()
+        if self.nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": self.err}
+        self.t.join(timeout=5)
+        reasons = set()
+        for _, bits, _ in self.samples:
+            for name, attr in self.REASONS:
+                if bits & getattr(self.nv, attr, 0):
+                    reasons.add(name)
+        sm = [c for c, _, _ in self.samples]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(p for _, _, p in self.samples) / 1000.0 if sm else None,
+                "source": "NVML, ~1 ms polling during the timed region"}
 
 
 def dist_init():
@@ -260,64 +273,97 @@ def time_kernel_only(sets, steps, dev):
 
 
 def time_e2e(sets, steps, warmup, dev, ws):
-    """Public API fed from pinned host memory: H2D of activations, the call,
-    D2H of the outputs, all inside the timed region."""
+    """The public call fed from pinned host memory, pipelined over three
+    streams the way a serving loop runs it.  Step i: one H2D copy of its
+    activation codes + scales (one pinned buffer per input set) on the copy
+    stream, nvfp4_grouped_gemm on the compute stream (out= a per-set device
+    buffer), one D2H copy of the whole bf16 output on the read-back stream.
+    Step i's H2D overlaps step i-1's GEMM and step i-2's D2H; events keep
+    each set's buffers from being reused before their last reader is done.
+    Timed with events from the first H2D to the last D2H."""
     import ratchet_b200 as rb
 
     R = len(sets)
-    host = []
+    n = sets[0]["sizes"][0][1]
+    k = sets[0]["sizes"][0][2]
+    bufs = []
     for s in sets:
-        ha = [t.view(torch.uint8).cpu().pin_memory() for t in s["a"]]
-        hs = [t.view(torch.uint8).cpu().pin_memory() for t in s["a_sf"]]
-        da = [torch.empty_like(t) for t in ha]
-        ds = [torch.empty_like(t) for t in hs]
-        da = [t.to(dev) for t in da]
-        ds = [t.to(dev) for t in ds]
-        sm = sum(t.shape[0] for t in ha)
-        hout = torch.empty((sm, s["sizes"][0][1]), dtype=torch.bfloat16).pin_memory()
-        host.append((ha, hs, da, ds, hout))
-    h2d = sum(t.numel() for t in host[0][0]) + sum(t.numel() for t in host[0][1])
-    d2h = host[0][4].numel() * 2
+        ms = [int(t.shape[0]) for t in s["a"]]
+        rows = sum(ms)
+        codes = torch.cat([t.view(torch.uint8) for t in s["a"]]).cpu().pin_memory()
+        scales = torch.cat([t.view(torch.uint8) for t in s["a_sf"]]).cpu().pin_memory()
+        d_codes, d_scales = codes.to(dev), scales.to(dev)
+        # per-group views into the device staging buffers, made once
+        a_views = list(d_codes.split(ms))
+        sf_views = [v.view(torch.float8_e4m3fn) for v in d_scales.split(ms)]
+        out = torch.empty((rows, n), dtype=torch.bfloat16, device=dev)
+        hout = torch.empty((rows, n), dtype=torch.bfloat16).pin_memory()
+        bufs.append(dict(codes=codes, scales=scales, d_codes=d_codes, d_scales=d_scales,
+                         a=a_views, sf=sf_views, out=out, hout=hout))
+    h2d = bufs[0]["codes"].numel() + bufs[0]["scales"].numel()
+    d2h = bufs[0]["hout"].numel() * 2
+    s_in, s_run, s_back = (torch.cuda.Stream(dev) for _ in range(3))
+    ev = lambda: torch.cuda.Event()
+    ready = [ev() for _ in range(R)]      # set b's inputs are on the device
+    computed = [ev() for _ in range(R)]   # set b's GEMM is done
+    drained = [ev() for _ in range(R)]    # set b's output is back on the host
+    used = [False] * R
 
     def step(i):
-        s = sets[i % R]
-        ha, hs, da, ds, hout = host[i % R]
-        for x, y in zip(da, ha):
-            x.copy_(y, non_blocking=True)
-        for x, y in zip(ds, hs):
-            x.copy_(y, non_blocking=True)
-        outs = rb.nvfp4_grouped_gemm(da, [t.view(torch.float8_e4m3fn) for t in ds], s["b"],
-                                     s["b_sf"], s["sizes"], s["alpha"])
-        r = 0
-        for o in outs:
-            hout[r:r + o.shape[0]].copy_(o, non_blocking=True)
-            r += o.shape[0]
+        b = i % R
+        s, B = sets[b], bufs[b]
+        with torch.cuda.stream(s_in):
+            if used[b]:
+                s_in.wait_event(computed[b])  # the previous GEMM on set b has read its inputs
+            B["d_codes"].copy_(B["codes"], non_blocking=True)
+            B["d_scales"].copy_(B["scales"], non_blocking=True)
+            ready[b].record(s_in)
+        with torch.cuda.stream(s_run):
+            s_run.wait_event(ready[b])
+            if used[b]:
+                s_run.wait_event(drained[b])  # the previous read-back of set b's output
+            rb.nvfp4_grouped_gemm(B["a"], B["sf"], s["b"], s["b_sf"], s["sizes"], s["alpha"],
+                                  out=B["out"])
+            computed[b].record(s_run)
+        with torch.cuda.stream(s_back):
+            s_back.wait_event(computed[b])
+            B["hout"].copy_(B["out"], non_blocking=True)
+            drained[b].record(s_back)
+        used[b] = True
 
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
     barrier(ws)
-    st = torch.cuda.current_stream()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
+    e0.record(s_in)
+    s_run.wait_event(e0)
+    s_back.wait_event(e0)
     for i in range(steps):
-        step(i)
-    e1.record(st)
+        step(warmup + i)
+    s_back.wait_stream(s_in)
+    s_back.wait_stream(s_run)
+    e1.record(s_back)
     torch.cuda.synchronize()
     barrier(ws)
+    torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps, h2d, d2h
 
 
-def cpu_sample(wl, budget_s: float = 20.0, seed: int = 1234):
-    """The CPU oracle on a bounded sample of the workload: whole groups,
-    dequantise (torch CPU) + fp32 matmul, until ~budget_s of work is timed."""
+def cpu_sample(wl, budget_s: float = 10.0, seed: int = 1234):
+    """The CPU oracle on a bounded sample of the workload: whole groups in
+    order, dequantise (torch CPU) + fp32 matmul + bf16, repeated over the
+    group list until about budget_s of work has been timed."""
     from oracle import nvfp4 as ref
 
     torch.set_num_threads(os.cpu_count() or 1)
     rng = np.random.default_rng(seed)
     n, k = wl["n"], wl["k"]
-    t_total, f_total, groups = 0.0, 0.0, 0
-    for gi, m in enumerate(wl["m"]):
+    G = len(wl["m"])
+    t_total, f_total, done = 0.0, 0.0, 0
+    while t_total < budget_s and done < 64 * G:
+        m = wl["m"][done % G]
         # the CPU cost does not depend on the values: random codes and scales
         qa, sa, qb, sb = _random_codes(rng, m, n, k)
         ga = gb = np.float32(1.0 / 2688.0)
@@ -327,14 +373,12 @@ def cpu_sample(wl, budget_s: float = 20.0, seed: int = 1234):
         c = ((a @ b.T) * float(ga * gb)).to(torch.bfloat16)
         t_total += time.perf_counter() - t0
         f_total += 2.0 * m * n * k
-        groups += 1
+        done += 1
         del c
-        if t_total >= budget_s or groups >= len(wl["m"]):
-            break
     return {"value": f_total / t_total / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"{groups} of {len(wl['m'])} groups (N={n}, K={k}): torch-CPU dequantise "
-                      f"+ fp32 matmul + bf16, {t_total:.2f} s timed"}
+            "sample": f"{done} group GEMMs ({done / G:.1f} passes over the {G} groups, N={n}, "
+                      f"K={k}): torch-CPU dequantise + fp32 matmul + bf16, {t_total:.1f} s timed"}
 
 
 def _random_codes(rng, m, n, k):
@@ -446,7 +490,7 @@ def run_ours(args, wl):
     if args.no_e2e:
         e2e_ms, h2d, d2h = float("nan"), 0, 0
     else:
-        e2e_ms, h2d, d2h = time_e2e(sets, max(3, args.steps // 2), min(args.warmup, 3), dev, ws)
+        e2e_ms, h2d, d2h = time_e2e(sets, args.steps, args.warmup, dev, ws)
         e2e_ms = max_over_ranks(e2e_ms, ws, dev)
 
     cpu = None
@@ -481,8 +525,8 @@ def run_ours(args, wl):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["grouped", "dense", "decode"], default="grouped")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")

@@ -100,7 +100,10 @@ class WeightPack:
             sfs.append(s)
         self.G, self.n, self.k = G, n, k
         self.device = b0.device
-        self.sources = (tuple(b_list), tuple(b_sf_list))  # keep addresses alive
+        # The pack keeps its source tensors alive, so their id()s stay unique
+        # while it is cached; their version counters reveal in-place writes.
+        self.sources = (tuple(b_list), tuple(b_sf_list))
+        self.versions = _versions(b_list, b_sf_list)
         L = _lib.lib()
         nbytes = int(L.fgg_nvfp4_weight_pack_bytes(G, n, k))
         if nbytes == 0:
@@ -114,9 +117,20 @@ class WeightPack:
                        "fgg_nvfp4_pack_weights")
 
 
+def _versions(b_list, b_sf_list) -> list[int]:
+    return [t._version for t in b_list] + [t._version for t in b_sf_list]
+
+
 def pack_weights(b_list, b_sf_list) -> WeightPack:
-    """Packed weights for these tensors, cached on tensor identity."""
-    key = tuple(_identity(t) for t in b_list) + tuple(_identity(t) for t in b_sf_list)
+    """Packed weights for these tensors, cached on tensor identity: the same
+    tensor objects, unmodified since the pack was built (version counters)."""
+    key = (tuple(map(id, b_list)), tuple(map(id, b_sf_list)))
+    hit = _PACKS.get(key)
+    if hit is not None and hit.versions == _versions(b_list, b_sf_list):
+        _PACKS.move_to_end(key)
+        return hit
+    if hit is not None:
+        del _PACKS[key]
     return _PACKS.get_or(key, lambda: WeightPack(b_list, b_sf_list))
 
 
@@ -137,7 +151,8 @@ def _problem_sizes(problem_sizes, G, n, k, a_list):
 
 
 def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None, alpha=None,
-                       *, pack: WeightPack | None = None) -> list[torch.Tensor]:
+                       *, pack: WeightPack | None = None,
+                       out: torch.Tensor | None = None) -> list[torch.Tensor]:
     """Per group g: C_g = alpha_g * deq(A_g) @ deq(B_g)^T as bf16 [M_g, N].
 
     a_list[g]    [M_g, K/2]  packed E2M1 codes (uint8 / float4_e2m1fn_x2)
@@ -145,6 +160,8 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
     b_list[g]    [N, K/2], b_sf_list[g] [N, K/16]  (packed once, cached)
     problem_sizes  G rows of (M_g, N, K), checked against the tensors
     alpha        G floats or an fp32 tensor (default 1)
+    out          optional contiguous bf16 [sum M_g, N] on the weights' device;
+                 the returned per-group tensors are row slices of it
     """
     global _last_ws
     G = len(a_list)
@@ -154,14 +171,17 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
         pack = pack_weights(b_list, b_sf_list)
     n, k, dev = pack.n, pack.k, pack.device
     ms = _problem_sizes(problem_sizes, G, n, k, a_list)
+    kh, ks = k // 2, k // 16
     a_u8, sf_u8 = [], []
-    for g in range(G):
-        a = _as_u8(a_list[g], f"a[{g}]")
-        s = _as_u8(a_sf_list[g], f"a_sf[{g}]")
-        if tuple(a.shape) != (ms[g], k // 2) or tuple(s.shape) != (ms[g], k // 16):
+    for g, (a, s, m) in enumerate(zip(a_list, a_sf_list, ms)):
+        if a.dtype is not torch.uint8:
+            a = _as_u8(a, f"a[{g}]")
+        if s.dtype is not torch.uint8:
+            s = _as_u8(s, f"a_sf[{g}]")
+        if a.shape != (m, kh) or s.shape != (m, ks):
             raise ValueError(f"group {g}: a {tuple(a.shape)} / a_sf {tuple(s.shape)} do not match "
-                             f"M={ms[g]}, K={k}")
-        if ms[g] > 0 and not (a.is_cuda and s.is_cuda and a.is_contiguous() and s.is_contiguous()):
+                             f"M={m}, K={k}")
+        if m and not (a.is_cuda and s.is_cuda and a.is_contiguous() and s.is_contiguous()):
             raise ValueError(f"group {g}: activations must be contiguous CUDA tensors")
         a_u8.append(a)
         sf_u8.append(s)
@@ -174,7 +194,11 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
     if alpha_t.numel() != G:
         raise ValueError(f"alpha has {alpha_t.numel()} entries for {G} groups")
     total = sum(ms)
-    out = torch.empty((total, n), dtype=torch.bfloat16, device=dev)
+    if out is None:
+        out = torch.empty((total, n), dtype=torch.bfloat16, device=dev)
+    elif (out.dtype != torch.bfloat16 or out.shape != (total, n) or not out.is_contiguous()
+          or out.device != dev):
+        raise ValueError(f"out must be a contiguous bf16 [{total}, {n}] tensor on {dev}")
     L = _lib.lib()
     m_arr = np.asarray(ms, dtype=np.int32)
     pa, psf = _ptr_array(a_u8), _ptr_array(sf_u8)

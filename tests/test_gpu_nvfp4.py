@@ -135,6 +135,42 @@ def test_bad_shapes_raise(cuda_device):
         rb.nvfp4_grouped_gemm(a, a_sf, bad_b, bad_sf, None, alpha)
 
 
+def test_pack_cache_tracks_inplace_weight_writes(cuda_device):
+    """A cached weight pack is reused for the same tensors and rebuilt after an
+    in-place write to any of them."""
+    import ratchet_b200 as rb
+
+    prob = ref.random_problem([64, 30], 256, 512, seed=11)
+    a, a_sf, b, b_sf, alpha = _dev_problem(prob, cuda_device)
+    p1 = rb.pack_weights(b, b_sf)
+    assert rb.pack_weights(b, b_sf) is p1
+    o1 = rb.nvfp4_grouped_gemm(a, a_sf, b, b_sf, None, alpha)
+    b[1].copy_(b[0])  # group 1 now holds group 0's weights
+    b_sf[1].copy_(b_sf[0])
+    p2 = rb.pack_weights(b, b_sf)
+    assert p2 is not p1
+    o2 = rb.nvfp4_grouped_gemm(a, a_sf, b, b_sf, None, alpha)
+    assert torch.equal(o1[0], o2[0])
+    refs = ref.grouped_gemm(prob["a"], prob["a_sf"], [prob["b"][0]] * 2, [prob["b_sf"][0]] * 2,
+                            prob["alpha"])
+    ok, st = ref.check_close(o2[1].cpu(), refs[1])
+    assert ok, st
+
+
+def test_out_parameter(cuda_device):
+    import ratchet_b200 as rb
+
+    prob = ref.random_problem([17, 0, 230], 256, 512, seed=12)
+    a, a_sf, b, b_sf, alpha = _dev_problem(prob, cuda_device)
+    want = rb.nvfp4_grouped_gemm(a, a_sf, b, b_sf, None, alpha)
+    out = torch.full((247, 256), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    got = rb.nvfp4_grouped_gemm(a, a_sf, b, b_sf, None, alpha, out=out)
+    assert all(g.data_ptr() == out[r:].data_ptr() for g, r in zip(got, [0, 17, 17]) if g.numel())
+    assert torch.equal(torch.cat(got), torch.cat(want))
+    with pytest.raises(ValueError):
+        rb.nvfp4_grouped_gemm(a, a_sf, b, b_sf, None, alpha, out=out[:-1])
+
+
 @pytest.mark.slow
 def test_config2_full_size(cuda_device):
     """BASELINE configs[1] at full size: 8 groups, M ~ U[64, 1024], N=4096, K=7168."""
