@@ -52,6 +52,11 @@ def workload(name: str, seed: int = 0) -> dict:
     if name == "dense":
         return dict(name="dense", desc="single group M=N=K=8192", m=[8192], n=8192, k=8192,
                     w_std=1.0, bound="tensor")
+    if name == "moe":
+        return dict(name="moe", desc="MoE expert layer: 4096 tokens, top-8 of 64 experts "
+                    "(Zipf s=1.1, seed 0), N=4096 (gate+up), K=7168, expert-parallel",
+                    m=[4096 * 8], n=4096, k=7168, w_std=1.0, bound="tensor",
+                    tokens=4096, experts=64, topk=8)
     if name == "decode":
         ms = [int(v) for v in rng.integers(1, 17, size=256)]
         return dict(name="decode", desc="256 groups, M_g~U[1,16] seed 0, N=7168, K=2048",
@@ -414,7 +419,7 @@ def run_reference(args, wl):
     G = len(wl["m"])
     data = []
     for gi in range(min(G, 4)):
-        m = wl["m"][gi]
+        m = min(wl["m"][gi], 1024)  # bounded sample per step
         qa, sa, qb, sb = _random_codes(rng, m, n, k)
         data.append((m, qa, sa, qb, sb, float(np.float32(1.0 / 2688.0) ** 2)))
 
@@ -436,13 +441,15 @@ def run_reference(args, wl):
     line = {
         "impl": "reference", "metric": "grouped-GEMM TFLOPS", "value": val, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong" if wl["name"] == "moe" else "weak",
         "vs_baseline": None, "dtype": "f32 (dequantised NVFP4)", "data": "synthetic",
         "config": {"workload": wl["desc"], "parallelism": "cpu"},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": "each step one whole group (cycling over the first "
-                                   f"{len(data)} groups): dequantise + fp32 matmul + bf16"},
+                         "sample": "each step one group of at most 1024 rows (cycling over "
+                                   f"the first {len(data)} groups): dequantise + fp32 matmul + "
+                                   "bf16"},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -521,6 +528,137 @@ def run_ours(args, wl):
         dist.destroy_process_group()
     return 0
 
+def run_moe(args, wl):
+    """one expert-parallel MoE projection over N ranks.
+    The 4096 tokens are split evenly over the ranks (each rank routes its own
+    share); the 64 experts are placed by expected load (LPT, equal counts).
+    A step = plan + all-to-all dispatch + grouped GEMM + all-to-all combine
+    with the router-weighted sum per token.  Total work is fixed, so the
+    scaling is strong; value = all FLOPs / the slowest rank's step time."""
+    from ratchet_b200 import moe
+
+    ws, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import ratchet_b200 as rb
+
+    T, E, topk, n, k = wl["tokens"], wl["experts"], wl["topk"], wl["n"], wl["k"]
+    if T % ws or E % ws:
+        raise SystemExit(f"--gpus {ws} must divide {T} tokens and {E} experts")
+    tl = T // ws
+    ids_all, w_all = moe.zipf_routing(T, E, topk, s=1.1, seed=0)
+    owner, slot = moe.place_experts(moe.expert_popularity(E, s=1.1, seed=0), ws)
+    mine = sorted(np.flatnonzero(owner == rank).tolist(), key=lambda e: slot[e])
+    wc, wsf, wg = [], [], []
+    for e in mine:  # each expert's weights depend only on its id, not on N
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(7000 + e)
+        q, sf, g = rb.quantize_nvfp4(torch.randn((n, k), generator=gen, device=dev))
+        wc.append(q)
+        wsf.append(sf)
+        wg.append(g)
+    layer = moe.ExpertParallelMoE(wc, wsf, wg, owner, slot)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(9000 + rank)
+    xc, xs, xg = rb.quantize_nvfp4(torch.randn((tl, k), generator=gen, device=dev))
+    ids = torch.from_numpy(ids_all[rank * tl:(rank + 1) * tl]).to(dev)
+    wts = torch.from_numpy(w_all[rank * tl:(rank + 1) * tl]).to(dev)
+    torch.cuda.synchronize()
+    fl = 2.0 * T * topk * n * k
+
+    def step(ev=None):
+        return layer.forward(xc, xs, xg, ids, wts, gemm_events=ev)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    e0.record()
+    for i in range(args.steps):
+        step(gev[i])
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    rb.last_status()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws, dev)
+    g_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in gev) / args.steps, ws, dev)
+    # GEMM rows on this rank (the kernel's FLOPs): the routes of its experts from every rank
+    counts = np.bincount(ids_all.ravel(), minlength=E)
+    my_rows = int(counts[np.asarray(mine)].sum())
+    g_fl = max_over_ranks(2.0 * my_rows * n * k, ws, dev)
+    pk = peaks()
+    achieved = g_fl / (g_ms * 1e-3) / 1e12
+    peak = 4.0 * pk["bf16"]
+    roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "traffic": traffic_from_profiles("moe"),
+            "peak_basis": f"4 x {pk['src']} dense bf16 ({pk['bf16']:.0f} TF/s)",
+            "kernel_ms": g_ms, "kernel": "grouped GEMM inside the layer (prepare + GEMM), "
+                                        "slowest rank"}
+
+    # end to end: this rank's activations from pinned host memory, the output back
+    h_xc = xc.cpu().pin_memory()
+    h_xs = xs.view(torch.uint8).cpu().pin_memory()
+    d_xc, d_xs = torch.empty_like(xc), torch.empty_like(xs.view(torch.uint8))
+    h_out = torch.empty((tl, n), dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, args.steps // 2)
+
+    def e2e_step():
+        d_xc.copy_(h_xc, non_blocking=True)
+        d_xs.copy_(h_xs, non_blocking=True)
+        out = layer.forward(d_xc, d_xs.view(torch.float8_e4m3fn), xg, ids, wts)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, ws, dev)
+
+    if rank == 0:
+        line = {
+            "metric": "grouped-GEMM TFLOPS", "value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "nvfp4 (e2m1 x e2m1, e4m3/16 scales, fp32 acc, bf16 out)",
+            "data": "synthetic (seeded N(0,1) tokens and expert weights, NVFP4-quantised; "
+                    "Zipf(1.1) top-8 routing)",
+            "config": {"workload": wl["desc"], "tokens": T, "experts": E, "topk": topk,
+                       "n": n, "k": k, "parallelism": f"ep{ws}",
+                       "placement": "LPT on expected expert load, equal expert counts",
+                       "l2": f"expert weights {E * n * k * 0.5625 / ws / 1e6:.0f} MB per rank "
+                             "read every step"},
+            "clocks": clocks,
+            "e2e": {"value": fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": int(h_xc.numel() + h_xs.numel()) * ws,
+                    "d2h_bytes_per_step": int(h_out.numel() * 2) * ws, "ms_per_step": e2e_ms},
+            "gpu_launches": 2 * args.steps,
+            "roofline": roof,
+            "cpu_baseline": cpu_sample(wl) if (ws == 1 and not args.no_cpu) else None,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -528,7 +666,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["grouped", "dense", "decode"], default="grouped")
+    ap.add_argument("--config", choices=["grouped", "dense", "decode", "moe"], default="grouped")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     args = ap.parse_args()
@@ -536,6 +674,8 @@ def main():
     wl = workload(args.config)
     if args.impl == "reference":
         return run_reference(args, wl)
+    if wl["name"] == "moe":
+        return run_moe(args, wl)
     return run_ours(args, wl)
 
 

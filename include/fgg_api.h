@@ -100,6 +100,12 @@ typedef struct FggNvfp4Problem {
   const void* const* a_sf;  /* host array [G] of device pointers */
   const float* alpha;       /* device array [G] */
   void* out;                /* device bf16 */
+  /* Optional: host array [G], the weight group (in `pack`) problem group g
+   * multiplies with; NULL = group g uses weight group g.  Lets several
+   * problem groups (e.g. the per-source chunks of one expert after an
+   * all-to-all dispatch) share one packed weight group. */
+  const int32_t* b_index;
+  int32_t num_weight_groups; /* groups in `pack` when b_index is set */
 } FggNvfp4Problem;
 
 /* Scratch the call needs (token-scale repack, per-group descriptors, tile
@@ -109,7 +115,8 @@ FGG_API size_t fgg_nvfp4_workspace_bytes(const FggNvfp4Problem* p);
 /* Replaces `fp4_grouped_gemm` (kernel.py:2788-2862) for the NVFP4 format:
  * validates, repacks the token scales, builds descriptors and launches the
  * persistent tcgen05 kernel.  `pack` must come from fgg_nvfp4_pack_weights
- * for the same G, N, K. */
+ * for the same N, K and G weight groups (num_weight_groups when b_index is
+ * set). */
 FGG_API int fgg_nvfp4_grouped_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace,
                            size_t ws_bytes, void* stream);
 /* The two halves of fgg_nvfp4_grouped_gemm, for callers that replay one

@@ -34,7 +34,7 @@ class FggNvfp4Weights(ctypes.Structure):
 class FggNvfp4Problem(ctypes.Structure):
     _fields_ = [("num_groups", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
                 ("m", _VOIDP), ("a", _VOIDP), ("a_sf", _VOIDP), ("alpha", _VOIDP),
-                ("out", _VOIDP)]
+                ("out", _VOIDP), ("b_index", _VOIDP), ("num_weight_groups", ctypes.c_int32)]
 
 
 class FggMxProblem(ctypes.Structure):

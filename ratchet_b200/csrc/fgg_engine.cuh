@@ -46,7 +46,7 @@ struct GroupInfo {
   int32_t m;            // rows of A_g
   int32_t out_row;      // first output row of the group
   int32_t xtile_begin;  // index of the group's first token tile in the SF repack
-  int32_t xtiles;       // token tiles of the group
+  int32_t wgroup;       // weight group (in the pack) this problem group multiplies with
 };
 
 // A tile is packed into 32 bits: group (10) | weight tile (11) | token tile (11).
@@ -62,6 +62,7 @@ struct PackHeader {
 };
 
 constexpr int kStatusBadPack = 0x201;
+constexpr int kStatusBadTile = 0x202;  // a schedule slot named a group outside the problem
 
 // One schedule-ring slot (32 bytes): what every role needs to know about a
 // tile, published by the scheduler warp.
@@ -71,7 +72,8 @@ struct SchedSlot {
   int32_t row0;         // output row of the tile's first token
   float alpha;          // output scale
   int32_t xtile_index;  // the token tile's index in the token-scale repack
-  int32_t pad[3];
+  int32_t wgroup;       // weight group of the tile (NVFP4 pack index; MX expert)
+  int32_t pad[2];
 };
 static_assert(sizeof(SchedSlot) == 32, "slot is 8 words");
 
@@ -91,6 +93,7 @@ struct GemmParams {
   __nv_bfloat16* out;
   int* status;  // [0] status, [1] tile counter, [2] finished CTAs
   int32_t g, n, k;
+  int32_t wg;       // NVFP4: weight groups in the pack (problem groups index into it)
   int32_t m_total;  // MX: rows of the contiguous activation tensor
   int32_t num_tiles;
   int32_t ksteps;
@@ -103,12 +106,13 @@ template <bool MX, int BN>
 __device__ __forceinline__ SchedSlot make_slot(const GemmParams& p, uint32_t tile) {
   SchedSlot s;
   s.tile = tile;
-  s.pad[0] = s.pad[1] = s.pad[2] = 0;
+  s.pad[0] = s.pad[1] = 0;
   if (tile == kEndTile) {
     s.rows = 0;
     s.row0 = 0;
     s.alpha = 0.0f;
     s.xtile_index = 0;
+    s.wgroup = 0;
     return s;
   }
   const int g = int(tile >> 22);
@@ -118,12 +122,14 @@ __device__ __forceinline__ SchedSlot make_slot(const GemmParams& p, uint32_t til
     s.row0 = xti * BN;
     s.alpha = 1.0f;
     s.xtile_index = xti;
+    s.wgroup = g;
   } else {
     const GroupInfo gi = p.ginfo[g];
     s.rows = min(BN, gi.m - xti * BN);
     s.row0 = gi.out_row + xti * BN;
     s.alpha = p.alpha[g];
     s.xtile_index = gi.xtile_begin + xti;
+    s.wgroup = gi.wgroup;
   }
   return s;
 }
@@ -135,7 +141,25 @@ __device__ __forceinline__ SchedSlot read_slot(const volatile SchedSlot* ring, i
   s.row0 = ring[slot].row0;
   s.alpha = ring[slot].alpha;
   s.xtile_index = ring[slot].xtile_index;
+  s.wgroup = ring[slot].wgroup;
   return s;
+}
+
+// Publish a slot into the peer CTA's ring (cluster address of its slot 0):
+// every 32-bit word of the slot, so no field can be left stale in the peer.
+__device__ __forceinline__ void write_slot_remote(uint32_t remote_ring0, int slot,
+                                                  const SchedSlot& s) {
+  const uint32_t words[8] = {s.tile,
+                             uint32_t(s.rows),
+                             uint32_t(s.row0),
+                             __float_as_uint(s.alpha),
+                             uint32_t(s.xtile_index),
+                             uint32_t(s.wgroup),
+                             uint32_t(s.pad[0]),
+                             uint32_t(s.pad[1])};
+  static_assert(sizeof(SchedSlot) == sizeof(words), "every word of the slot is stored");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) st_shared_remote_u32(remote_ring0 + 32u * slot + 4u * i, words[i]);
 }
 
 __device__ __forceinline__ void write_slot(volatile SchedSlot* ring, int slot,
@@ -145,6 +169,7 @@ __device__ __forceinline__ void write_slot(volatile SchedSlot* ring, int slot,
   ring[slot].row0 = s.row0;
   ring[slot].alpha = s.alpha;
   ring[slot].xtile_index = s.xtile_index;
+  ring[slot].wgroup = s.wgroup;
 }
 
 // Epilogue of one tile for the calling warp: its 32 TMEM lanes (output
@@ -259,7 +284,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
     if constexpr (!C::MX) {
       // A pack built for a different problem is refused before any load.
       const PackHeader h = *p.pack;
-      if (h.magic != kPackMagic || h.g != p.g || h.n != p.n || h.k != p.k) {
+      if (h.magic != kPackMagic || h.g != p.wg || h.n != p.n || h.k != p.k) {
         atomicCAS(p.status, 0, kStatusBadPack);
         *abort_flag = 1;
       }
@@ -333,19 +358,26 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
         const int g = int(s.tile >> 22);
         const int nti = int((s.tile >> 11) & 0x7FFu);
         const int xti = int(s.tile & 0x7FFu);
+        // the group and weight group index descriptor arrays: never trust them blindly
+        if (g >= p.g || unsigned(s.wgroup) >= unsigned(p.wg)) {
+          atomicCAS(p.status, 0, kStatusBadTile);
+          *abort_flag = 1;
+          break;
+        }
         const CUtensorMap* tw;
         const CUtensorMap* tx;
         if constexpr (C::MX) {
           tw = &p.mx_tmap_w;
           tx = &p.mx_tmap_x;
         } else {
-          tw = p.tmap_w + g;
+          tw = p.tmap_w + s.wgroup;
           tx = p.tmap_x + g;
           tensormap_acquire(tw);
           tensormap_acquire(tx);
         }
         const uint8_t* sfx = p.sfx + size_t(s.xtile_index) * size_t(p.ksteps) * C::SFX_BYTES;
-        const uint8_t* sfw = p.sfw + (size_t(g) * p.nt + nti) * size_t(p.ksteps) * C::SFW_BYTES;
+        const uint8_t* sfw =
+            p.sfw + (size_t(s.wgroup) * p.nt + nti) * size_t(p.ksteps) * C::SFW_BYTES;
         bool ok = true;
         for (int ks = 0; ks < p.ksteps; ++ks) {
           if (!mbar_wait1(empty_bar(stage), phase ^ 1, abort_flag, p.status,
@@ -635,7 +667,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     *abort_flag = 0;
     if constexpr (!C::MX) {
       const PackHeader h = *p.pack;
-      if (h.magic != kPackMagic || h.g != p.g || h.n != p.n || h.k != p.k) {
+      if (h.magic != kPackMagic || h.g != p.wg || h.n != p.n || h.k != p.k) {
         atomicCAS(p.status, 0, kStatusBadPack);
         *abort_flag = 1;
       }
@@ -686,12 +718,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                               kStatusTimeoutProducer))
           break;
         write_slot(ring, slot, s);
-        const uint32_t r = remote_ring0 + 32u * slot;
-        st_shared_remote_u32(r + 0, s.tile);
-        st_shared_remote_u32(r + 4, uint32_t(s.rows));
-        st_shared_remote_u32(r + 8, uint32_t(s.row0));
-        st_shared_remote_u32(r + 12, __float_as_uint(s.alpha));
-        st_shared_remote_u32(r + 16, uint32_t(s.xtile_index));
+        write_slot_remote(remote_ring0, slot, s);
         mbar_arrive(schedf_bar(slot));
         mbar_arrive_remote(remote_schedf0 + 8u * slot);
         if (++slot == C::SCHED) {
@@ -731,6 +758,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const int g = int(s.tile >> 22);
         const int nti = int((s.tile >> 11) & 0x7FFu);
         const int xti = int(s.tile & 0x7FFu);
+        // the group and weight group index descriptor arrays: never trust them blindly
+        if (g >= p.g || unsigned(s.wgroup) >= unsigned(p.wg)) {
+          atomicCAS(p.status, 0, kStatusBadTile);
+          *abort_flag = 1;
+          break;
+        }
         const int half = tile_ncols(s.rows) >> 1;
         const CUtensorMap* tw;
         const CUtensorMap* tx;
@@ -738,14 +771,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           tw = &p.mx_tmap_w;
           tx = &p.mx_tmap_x;
         } else {
-          tw = p.tmap_w + g;
+          tw = p.tmap_w + s.wgroup;
           tx = p.tmap_x + g;
           tensormap_acquire(tw);
           tensormap_acquire(tx);
         }
         const int wrow = nti * 256 + int(rank) * 128;
         const int xrow = xti * C::BN + int(rank) * half;
-        const int sfw_y = ((g * p.nt128 + 2 * nti + int(rank)) * p.ksteps) * int(C::SFW_BOX_ROWS);
+        const int sfw_y =
+            ((s.wgroup * p.nt128 + 2 * nti + int(rank)) * p.ksteps) * int(C::SFW_BOX_ROWS);
         const int sfx_y = (s.xtile_index * p.ksteps) * int(C::SFX_BOX_ROWS);
         bool ok = true;
         for (int ks = 0; ks < p.ksteps; ++ks) {

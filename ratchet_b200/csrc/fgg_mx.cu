@@ -227,6 +227,7 @@ int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
   gp.out = static_cast<__nv_bfloat16*>(p->c);
   gp.status = reinterpret_cast<int*>(ws + L.status);
   gp.g = p->num_groups;
+  gp.wg = p->num_groups;
   gp.n = p->n;
   gp.k = p->k;
   gp.m_total = p->m_total;

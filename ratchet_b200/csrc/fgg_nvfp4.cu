@@ -27,6 +27,7 @@ struct PrepParams {
   int32_t xtile_begin[FGG_MAX_GROUPS + 1];
   int32_t tile_begin[FGG_MAX_GROUPS + 1];
   int32_t out_row[FGG_MAX_GROUPS];
+  int32_t wgroup[FGG_MAX_GROUPS];  // weight group of each problem group
   CUtensorMap* tmap_out;
   GroupInfo* ginfo_out;
   uint32_t* tiles_out;
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(256) nvfp4_prepare_kernel(const __grid_constan
         gi.m = p.m[g];
         gi.out_row = p.out_row[g];
         gi.xtile_begin = p.xtile_begin[g];
-        gi.xtiles = p.xtile_begin[g + 1] - p.xtile_begin[g];
+        gi.wgroup = p.wgroup[g];
         p.ginfo_out[g] = gi;
       }
       __syncwarp();
@@ -210,6 +211,7 @@ struct WsLayout {
   int32_t xtile_begin[FGG_MAX_GROUPS + 1];
   int32_t tile_begin[FGG_MAX_GROUPS + 1];
   int32_t out_row[FGG_MAX_GROUPS];
+  int wg = 0;  // weight groups the problem groups index into
   size_t status = 0, tmaps = 0, ginfo = 0, tiles = 0, sfx = 0, total = 0;
 };
 
@@ -224,6 +226,19 @@ static int plan(const FggNvfp4Problem* p, WsLayout* L) {
     return set_error(FGG_EBADSHAPE, "K=%d must be a positive multiple of 64", p->k);
   if (p->m == nullptr) return set_error(FGG_EINVAL, "m (host problem sizes) is null");
   if (p->n / 128 > 2047) return set_error(FGG_EBADSHAPE, "N=%d too large", p->n);
+  L->wg = G;
+  if (p->b_index != nullptr) {
+    // several problem groups may share one packed weight group (e.g. the
+    // per-source chunks of one expert after an all-to-all dispatch)
+    if (p->num_weight_groups < 1 || p->num_weight_groups > FGG_MAX_GROUPS)
+      return set_error(FGG_EINVAL, "num_weight_groups=%d outside [1, %d]", p->num_weight_groups,
+                       FGG_MAX_GROUPS);
+    for (int g = 0; g < G; ++g)
+      if (p->b_index[g] < 0 || p->b_index[g] >= p->num_weight_groups)
+        return set_error(FGG_EINVAL, "b_index[%d]=%d outside [0, %d)", g, p->b_index[g],
+                         p->num_weight_groups);
+    L->wg = p->num_weight_groups;
+  }
   int maxm = 0;
   for (int g = 0; g < G; ++g) {
     if (p->m[g] < 0) return set_error(FGG_EINVAL, "m[%d]=%d is negative", g, p->m[g]);
@@ -378,6 +393,7 @@ int prepare_impl(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8_t
     pp.a_sf[g] = static_cast<const uint8_t*>(p->a_sf[g]);
     pp.m[g] = p->m[g];
     pp.out_row[g] = L.out_row[g];
+    pp.wgroup[g] = p->b_index != nullptr ? p->b_index[g] : g;
   }
   for (int g = 0; g <= G; ++g) {
     pp.xtile_begin[g] = L.xtile_begin[g];
@@ -413,7 +429,7 @@ int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uin
   if (!aligned16(pack)) return set_error(FGG_EALIGN, "pack must be 16-byte aligned");
   const int G = p->num_groups;
   const uint8_t* pk = static_cast<const uint8_t*>(pack);
-  const PackLayout PL = pack_layout(G, p->n, p->k);
+  const PackLayout PL = pack_layout(L.wg, p->n, p->k);
   GemmParams gp;
   memset(&gp, 0, sizeof(gp));
   gp.tmap_w = reinterpret_cast<const CUtensorMap*>(pk + PL.tmaps);
@@ -427,6 +443,7 @@ int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uin
   gp.out = static_cast<__nv_bfloat16*>(p->out);
   gp.status = reinterpret_cast<int*>(ws + L.status);
   gp.g = G;
+  gp.wg = L.wg;
   gp.n = p->n;
   gp.k = p->k;
   gp.m_total = 0;
@@ -438,7 +455,7 @@ int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uin
   if (L.pair) {
     // scale-factor atoms as 2-D uint64 tensors: weights 2 KB per (group, 128-row
     // tile, K step); tokens 4 KB per (token tile, K step) as two 2 KB rows
-    if (int rc = encode_u64_rows(&gp.sfw_map, gp.sfw, uint64_t(G) * L.nt128 * L.nk256,
+    if (int rc = encode_u64_rows(&gp.sfw_map, gp.sfw, uint64_t(L.wg) * L.nt128 * L.nk256,
                                  CfgPair::SFW_ROW_U64, CfgPair::SFW_BOX_ROWS))
       return rc;
     if (int rc = encode_u64_rows(&gp.sfx_map, gp.sfx,

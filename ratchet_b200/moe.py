@@ -1,0 +1,245 @@
+"""Expert-parallel NVFP4 MoE layer: route -> dispatch -> grouped GEMM -> combine.
+
+The single-GPU analogue in the reference is `_moe_forward`
+(tasks/muse_prefill_boundary/reference/submission.py:843-895): a gather plan
+puts the routed token rows of each expert together, one grouped GEMM runs
+every expert, and a combine weights the rows and sums them back per token.
+Here the experts are sharded over the ranks of a process group (one process
+per GPU) and the rows travel between ranks:
+
+  1. plan      every (token, k) route gets its owner rank and the expert's
+               slot on that rank; routes are ordered by (rank, slot) with one
+               stable sort, and counted per (rank, slot)
+  2. dispatch  all-to-all of the counts, then of the NVFP4 rows (codes and
+               E4M3 scales) in that order, plus an all-gather of each rank's
+               activation decode scale
+  3. GEMM      the received rows are source-major: the rows of one local
+               expert arrive as one contiguous chunk per source rank.  Each
+               (source, expert) chunk is one problem group of the grouped
+               GEMM, pointing at the expert's packed weights through b_index,
+               so nothing is permuted on the receiving side
+  4. combine   all-to-all of the bf16 output rows back along the same splits,
+               an index_copy_ that undoes the plan's order, and (with router
+               weights) the weighted sum over each token's k routes
+
+Collectives go through torch.distributed (NCCL on GPUs, gloo for the CPU
+tests of this host logic).  The expert compute is the library's tcgen05
+grouped GEMM; `gemm_fn` may replace it only to test the host logic without
+a GPU.
+"""
+from __future__ import annotations
+
+from typing import Callable, Sequence
+
+import numpy as np
+import torch
+
+from . import ops
+
+
+# ------------------------------------------------------------------ routing
+def zipf_routing(num_tokens: int, num_experts: int, topk: int, s: float = 1.1, seed: int = 0):
+    """Seeded top-k routing with Zipf(s) expert popularity.
+
+    A seeded permutation ranks the experts; expert with rank r (1-based) has
+    weight r^-s.  Each token draws `topk` DISTINCT experts without
+    replacement in proportion to those weights (Gumbel top-k), so no expert
+    receives more than `num_tokens` rows.  Router weights are the drawn
+    experts' popularity renormalised over the token's k routes.
+    Returns (ids int32 [T, k], weights float32 [T, k]).
+    """
+    if not 0 < topk <= num_experts:
+        raise ValueError(f"topk={topk} must be in [1, {num_experts}]")
+    rng = np.random.default_rng(seed)
+    rank_of = rng.permutation(num_experts)  # expert e has popularity rank rank_of[e]
+    pop = (rank_of + 1.0) ** (-s)
+    pop /= pop.sum()
+    gumbel = -np.log(-np.log(rng.random((num_tokens, num_experts))))
+    keys = np.log(pop)[None, :] + gumbel
+    ids = np.argpartition(-keys, topk - 1, axis=1)[:, :topk]
+    # order each token's routes by key (largest first) so the result is deterministic
+    kk = np.take_along_axis(keys, ids, axis=1)
+    ids = np.take_along_axis(ids, np.argsort(-kk, axis=1), axis=1).astype(np.int32)
+    w = pop[ids]
+    w = (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
+    return ids, w
+
+
+def expert_popularity(num_experts: int, s: float = 1.1, seed: int = 0) -> np.ndarray:
+    """The per-expert weights zipf_routing draws with (same seed, same order)."""
+    rng = np.random.default_rng(seed)
+    rank_of = rng.permutation(num_experts)
+    pop = (rank_of + 1.0) ** (-s)
+    return pop / pop.sum()
+
+
+def place_experts(load: Sequence[float], world: int):
+    """Static expert -> rank placement that spreads the expected load.
+
+    Longest-processing-time first with equal expert counts per rank: experts
+    in decreasing load go to the least-loaded rank that still has room
+    (ties: lower rank).  Returns (owner int32 [E], slot int32 [E]) where
+    slot is the expert's index among its owner's experts, in expert order.
+    """
+    load = np.asarray(load, dtype=np.float64)
+    E = load.shape[0]
+    if world < 1 or E % world != 0:
+        raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+    per = E // world
+    owner = np.full(E, -1, dtype=np.int32)
+    acc = np.zeros(world)
+    cnt = np.zeros(world, dtype=np.int64)
+    for e in sorted(range(E), key=lambda e: (-load[e], e)):
+        room = [r for r in range(world) if cnt[r] < per]
+        r = min(room, key=lambda r: (acc[r], r))
+        owner[e] = r
+        acc[r] += load[e]
+        cnt[r] += 1
+    slot = np.zeros(E, dtype=np.int32)
+    for r in range(world):
+        for i, e in enumerate(np.flatnonzero(owner == r)):
+            slot[e] = i
+    return owner, slot
+
+
+# ------------------------------------------------------------------ layer
+GemmFn = Callable[[list, list, list, torch.Tensor, torch.Tensor], None]
+
+
+class ExpertParallelMoE:
+    """One expert-parallel MoE projection (e.g. the fused gate+up of every
+    expert) over the ranks of `group`.
+
+    w_codes / w_sf / w_scale: this rank's experts, in slot order: codes
+    [N, K/2] uint8, E4M3 scales [N, K/16], fp32 decode scale (0-dim tensor
+    or float).  owner / slot: the placement of every expert (place_experts).
+    """
+
+    def __init__(self, w_codes: Sequence[torch.Tensor], w_sf: Sequence[torch.Tensor],
+                 w_scale: Sequence, owner: np.ndarray, slot: np.ndarray, group=None,
+                 gemm_fn: GemmFn | None = None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        owner = np.asarray(owner, dtype=np.int32)
+        slot = np.asarray(slot, dtype=np.int32)
+        if owner.max() >= self.world or owner.min() < 0:
+            raise ValueError("owner names a rank outside the process group")
+        self.num_experts = int(owner.shape[0])
+        self.local = int((owner == self.rank).sum())
+        if self.local != len(w_codes) or len(w_codes) != len(w_sf) or len(w_sf) != len(w_scale):
+            raise ValueError(f"rank {self.rank} owns {self.local} experts, got {len(w_codes)} weights")
+        counts = np.bincount(owner, minlength=self.world)
+        if (counts != counts[0]).any():
+            raise ValueError("every rank must own the same number of experts")
+        self.w_codes = list(w_codes)
+        self.w_sf = list(w_sf)
+        self.n = int(self.w_codes[0].shape[0])
+        self.k = int(self.w_codes[0].shape[1]) * 2
+        dev = self.w_codes[0].device
+        self.device = dev
+        self.w_scale = torch.stack([torch.as_tensor(s, dtype=torch.float32, device=dev).reshape(())
+                                    for s in w_scale])
+        self.owner_t = torch.from_numpy(owner).to(dev, torch.int64)
+        self.slot_t = torch.from_numpy(slot).to(dev, torch.int64)
+        self.gemm_fn = gemm_fn
+        self.pack = None
+        if gemm_fn is None:
+            # the product path: packed once, reused by every forward
+            self.pack = ops.pack_weights(self.w_codes, self.w_sf)
+        # problem group g = (source rank, local slot), source-major
+        self.b_index = [e for _ in range(self.world) for e in range(self.local)]
+
+    # -------------------------------------------------------------- pieces
+    def plan(self, topk_ids: torch.Tensor):
+        """Order of the routes by (owner rank, slot) and their counts."""
+        flat = topk_ids.reshape(-1).to(self.owner_t.device, torch.int64)
+        key = self.owner_t[flat] * self.local + self.slot_t[flat]
+        order = torch.argsort(key, stable=True)
+        counts = torch.bincount(key, minlength=self.world * self.local).to(torch.int32)
+        return order, counts
+
+    def _a2a(self, out, inp, out_splits=None, in_splits=None):
+        import torch.distributed as dist
+
+        if inp.dtype == torch.bfloat16:  # rows as bytes: bit-exact on every backend
+            out, inp = out.view(torch.uint8), inp.view(torch.uint8)
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, x_codes: torch.Tensor, x_sf: torch.Tensor, x_scale, topk_ids: torch.Tensor,
+                topk_weights: torch.Tensor | None = None, gemm_events=None) -> torch.Tensor:
+        """x_codes [T, K/2] uint8 and x_sf [T, K/16] E4M3: this rank's tokens,
+        quantised with decode scale x_scale.  topk_ids [T, k] expert ids.
+        Returns [T, k, N] bf16 per-route outputs, or [T, N] bf16 (the
+        weighted sum over k) when topk_weights [T, k] is given.
+        gemm_events: optional (start, end) CUDA events recorded around the
+        grouped GEMM on the current stream (for timing the kernel alone)."""
+        import torch.distributed as dist
+
+        T, topk = int(topk_ids.shape[0]), int(topk_ids.shape[1])
+        kh, ks = self.k // 2, self.k // 16
+        x_u8 = x_codes.view(torch.uint8)
+        s_u8 = x_sf.view(torch.uint8)
+        if x_u8.shape != (T, kh) or s_u8.shape != (T, ks):
+            raise ValueError(f"x_codes {tuple(x_u8.shape)} / x_sf {tuple(s_u8.shape)} do not match "
+                             f"T={T}, K={self.k}")
+        dev = x_u8.device
+        W, E = self.world, self.local
+        # 1. plan
+        order, counts = self.plan(topk_ids)
+        # 2. dispatch: counts first, then the rows they describe
+        if W == 1:
+            recv_counts = counts
+        else:
+            recv_counts = torch.empty_like(counts)
+            self._a2a(recv_counts, counts)
+        both = torch.stack([counts, recv_counts]).cpu()  # one host sync per forward
+        send_ce, recv_ce = both[0].view(W, E), both[1].view(W, E)
+        send_splits = send_ce.sum(1).tolist()
+        recv_splits = recv_ce.sum(1).tolist()
+        rows = order // topk
+        send_codes = x_u8.index_select(0, rows)
+        send_sf = s_u8.index_select(0, rows)
+        R = int(sum(recv_splits))
+        xs = torch.as_tensor(x_scale, dtype=torch.float32, device=dev).reshape(1)
+        if W == 1:  # nothing leaves the rank
+            recv_codes, recv_sf, src_scale = send_codes, send_sf, xs
+        else:
+            recv_codes = torch.empty((R, kh), dtype=torch.uint8, device=dev)
+            recv_sf = torch.empty((R, ks), dtype=torch.uint8, device=dev)
+            self._a2a(recv_codes, send_codes, recv_splits, send_splits)
+            self._a2a(recv_sf, send_sf, recv_splits, send_splits)
+            parts = [torch.empty_like(xs) for _ in range(W)]
+            dist.all_gather(parts, xs, group=self.group)
+            src_scale = torch.cat(parts)
+        # 3. grouped GEMM over the (source, slot) chunks
+        ms = recv_ce.reshape(-1).tolist()
+        a_list = list(recv_codes.split(ms))
+        sf_list = [t.view(torch.float8_e4m3fn) for t in recv_sf.split(ms)]
+        alpha = (src_scale[:, None] * self.w_scale[None, :]).reshape(-1).contiguous()
+        out = torch.empty((R, self.n), dtype=torch.bfloat16, device=dev)
+        if gemm_events is not None:
+            gemm_events[0].record()
+        if self.gemm_fn is None:
+            if R > 0:
+                ops.nvfp4_grouped_gemm(a_list, sf_list, self.w_codes, self.w_sf, None, alpha,
+                                       pack=self.pack, out=out, b_index=self.b_index)
+        else:
+            self.gemm_fn(a_list, sf_list, self.b_index, alpha, out)
+        if gemm_events is not None:
+            gemm_events[1].record()
+        # 4. combine: rows go back along the dispatch splits, then to route order
+        if W == 1:
+            back = out
+        else:
+            back = torch.empty((T * topk, self.n), dtype=torch.bfloat16, device=dev)
+            self._a2a(back, out, send_splits, recv_splits)
+        res = torch.empty_like(back)
+        res.index_copy_(0, order, back)
+        res = res.view(T, topk, self.n)
+        if topk_weights is None:
+            return res
+        w = topk_weights.to(dev, torch.float32).view(T, topk, 1)
+        return (res.float() * w).sum(1).to(torch.bfloat16)

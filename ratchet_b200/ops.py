@@ -151,8 +151,8 @@ def _problem_sizes(problem_sizes, G, n, k, a_list):
 
 
 def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None, alpha=None,
-                       *, pack: WeightPack | None = None,
-                       out: torch.Tensor | None = None) -> list[torch.Tensor]:
+                       *, pack: WeightPack | None = None, out: torch.Tensor | None = None,
+                       b_index=None) -> list[torch.Tensor]:
     """Per group g: C_g = alpha_g * deq(A_g) @ deq(B_g)^T as bf16 [M_g, N].
 
     a_list[g]    [M_g, K/2]  packed E2M1 codes (uint8 / float4_e2m1fn_x2)
@@ -162,11 +162,23 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
     alpha        G floats or an fp32 tensor (default 1)
     out          optional contiguous bf16 [sum M_g, N] on the weights' device;
                  the returned per-group tensors are row slices of it
+    b_index      optional: problem group g multiplies with weight group
+                 b_index[g] (b_list then holds the weight groups, any count);
+                 several problem groups may share one weight group
     """
     global _last_ws
     G = len(a_list)
-    if not (G == len(a_sf_list) == len(b_list) == len(b_sf_list)) or G == 0:
-        raise ValueError("a_list, a_sf_list, b_list, b_sf_list must have the same non-zero length")
+    if G == 0 or G != len(a_sf_list) or len(b_list) != len(b_sf_list) or not b_list:
+        raise ValueError("a_list/a_sf_list and b_list/b_sf_list must be non-empty, pairwise equal length")
+    if b_index is None:
+        if len(b_list) != G:
+            raise ValueError(f"{G} activation groups but {len(b_list)} weight groups "
+                             "(pass b_index to map groups to weights)")
+        bidx = None
+    else:
+        bidx = np.asarray([int(i) for i in b_index], dtype=np.int32)
+        if bidx.shape != (G,) or (bidx < 0).any() or (bidx >= len(b_list)).any():
+            raise ValueError(f"b_index must hold {G} weight-group indices in [0, {len(b_list)})")
     if pack is None:
         pack = pack_weights(b_list, b_sf_list)
     n, k, dev = pack.n, pack.k, pack.device
@@ -203,7 +215,8 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
     m_arr = np.asarray(ms, dtype=np.int32)
     pa, psf = _ptr_array(a_u8), _ptr_array(sf_u8)
     prob = _lib.FggNvfp4Problem(G, n, k, m_arr.ctypes.data, pa.ctypes.data, psf.ctypes.data,
-                                alpha_t.data_ptr(), out.data_ptr())
+                                alpha_t.data_ptr(), out.data_ptr(),
+                                None if bidx is None else bidx.ctypes.data, len(b_list))
     nbytes = int(L.fgg_nvfp4_workspace_bytes(prob))
     if nbytes == 0:
         _lib.check(L.fgg_nvfp4_grouped_gemm(prob, None, None, 0, None), "nvfp4_grouped_gemm")

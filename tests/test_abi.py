@@ -149,3 +149,23 @@ def test_check_maps_codes_to_exceptions():
         _lib.check(_lib.FGG_EBADSHAPE, "x")
     with pytest.raises(_lib.FggError):
         _lib.check(_lib.FGG_ETIMEOUT, "x")
+
+
+def test_b_index_validated_before_device(L):
+    """A problem group may name a shared weight group; out-of-range indices and
+    a bad weight-group count are refused on the host."""
+    G = 3
+    m = np.asarray([16, 0, 40], dtype=np.int32)
+    fake = np.full(G, 1 << 20, dtype=np.uint64)
+    bad = np.asarray([0, 2, 1], dtype=np.int32)
+    p = _lib.FggNvfp4Problem(G, 256, 512, m.ctypes.data, fake.ctypes.data, fake.ctypes.data,
+                             1 << 20, 1 << 20, bad.ctypes.data, 2)
+    assert L.fgg_nvfp4_workspace_bytes(p) == 0
+    assert L.fgg_nvfp4_grouped_gemm(p, None, None, 0, None) == _lib.FGG_EINVAL
+    assert b"b_index[1]=2" in L.fgg_last_error_detail()
+    good = np.asarray([0, 1, 1], dtype=np.int32)
+    p = _lib.FggNvfp4Problem(G, 256, 512, m.ctypes.data, fake.ctypes.data, fake.ctypes.data,
+                             1 << 20, 1 << 20, good.ctypes.data, 0)
+    assert L.fgg_nvfp4_grouped_gemm(p, None, None, 0, None) == _lib.FGG_EINVAL
+    p.num_weight_groups = 2
+    assert L.fgg_nvfp4_workspace_bytes(p) > 0

@@ -1,0 +1,110 @@
+"""Expert-parallel MoE layer on B200 with the tcgen05 grouped GEMM, against
+the CPU oracle: world size 1 on one GPU, and two NCCL ranks when two GPUs are
+visible.  Tolerance: the operator's (max|err|/max|ref| <= 1e-2; per element
+|err| <= 2e-2 |ref| + 1e-2 max|ref|)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import nvfp4 as ref
+from ratchet_b200 import moe
+
+pytestmark = pytest.mark.gpu
+
+E, N, K, TOPK = 8, 256, 512, 4
+
+
+def _weights(seed=1):
+    rng = np.random.default_rng(seed)
+    return [ref.nvfp4_quantize(rng.standard_normal((N, K), dtype=np.float32)) for _ in range(E)]
+
+
+def _expected(xc, xs, xg, ids, w_all):
+    X = torch.from_numpy(ref.nvfp4_dequantize(xc, xs))
+    Wd = [torch.from_numpy(ref.nvfp4_dequantize(c, s)) for c, s, _ in w_all]
+    T = ids.shape[0]
+    out = torch.empty((T, TOPK, N))
+    for e in range(E):
+        sel = np.argwhere(ids == e)
+        if len(sel):
+            t = torch.from_numpy(sel[:, 0])
+            out[t, torch.from_numpy(sel[:, 1])] = (X[t] @ Wd[e].T) * float(np.float32(xg * w_all[e][2]))
+    return out.to(torch.bfloat16)
+
+
+def _layer(w_all, owner, slot, rank, dev):
+    mine = sorted(np.flatnonzero(owner == rank).tolist(), key=lambda e: slot[e])
+    return moe.ExpertParallelMoE([torch.from_numpy(w_all[e][0]).to(dev) for e in mine],
+                                 [torch.from_numpy(w_all[e][1]).to(dev).view(torch.float8_e4m3fn)
+                                  for e in mine],
+                                 [float(w_all[e][2]) for e in mine], owner, slot)
+
+
+def _check(layer, rank, T, dev, w_all):
+    rng = np.random.default_rng(100 + rank)
+    xc, xs, xg = ref.nvfp4_quantize(rng.standard_normal((T, K), dtype=np.float32))
+    ids, w = moe.zipf_routing(T, E, TOPK, seed=30 + rank)
+    got = layer.forward(torch.from_numpy(xc).to(dev),
+                        torch.from_numpy(xs).to(dev).view(torch.float8_e4m3fn), float(xg),
+                        torch.from_numpy(ids).to(dev))
+    want = _expected(xc, xs, xg, ids, w_all)
+    ok, st = ref.check_close(got.cpu().float(), want.float())
+    summed = layer.forward(torch.from_numpy(xc).to(dev),
+                           torch.from_numpy(xs).to(dev).view(torch.float8_e4m3fn), float(xg),
+                           torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev))
+    ok2, st2 = ref.check_close(summed.cpu().float(),
+                               (want.float() * torch.from_numpy(w)[..., None]).sum(1))
+    return ok and ok2, (st, st2)
+
+
+def test_moe_world1(cuda_device):
+    import ratchet_b200 as rb
+
+    w_all = _weights()
+    owner, slot = moe.place_experts(moe.expert_popularity(E, seed=2), 1)
+    layer = _layer(w_all, owner, slot, 0, cuda_device)
+    ok, st = _check(layer, 0, 333, cuda_device, w_all)
+    assert ok, st
+    rb.last_status()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, result_dir):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        w_all = _weights()
+        owner, slot = moe.place_experts(moe.expert_popularity(E, seed=2), world)
+        layer = _layer(w_all, owner, slot, rank, dev)
+        ok, st = _check(layer, rank, 200 + 57 * rank, dev, w_all)
+        with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
+            f.write(f"{int(ok)} {st}\n")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_moe_two_nccl_ranks(cuda_device, tmp_path):
+    import torch.multiprocessing as mp
+
+    mp.spawn(_nccl_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        line = (tmp_path / f"rank{r}.txt").read_text()
+        assert line.startswith("1 "), f"rank {r}: {line}"

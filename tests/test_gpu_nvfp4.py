@@ -171,6 +171,29 @@ def test_out_parameter(cuda_device):
         rb.nvfp4_grouped_gemm(a, a_sf, b, b_sf, None, alpha, out=out[:-1])
 
 
+@pytest.mark.parametrize("n", [256, 384])
+def test_shared_weight_groups(cuda_device, n):
+    """b_index: five activation groups over two packed weight groups (the
+    layout of expert chunks after an all-to-all dispatch)."""
+    import ratchet_b200 as rb
+
+    ms = [40, 0, 230, 17, 300]
+    bidx = [1, 0, 1, 1, 0]
+    wprob = ref.random_problem([1, 1], n, 512, seed=21)       # two weight groups
+    aprob = ref.random_problem(ms, n, 512, seed=22)           # five activation groups
+    a, a_sf, _, _, _ = _dev_problem(aprob, cuda_device)
+    _, _, b, b_sf, _ = _dev_problem(wprob, cuda_device)
+    alpha = np.asarray([0.25 * (g + 1) for g in range(5)], dtype=np.float32)
+    outs = rb.nvfp4_grouped_gemm(a, a_sf, b, b_sf, None, torch.from_numpy(alpha).to(cuda_device),
+                                 b_index=bidx)
+    refs = ref.grouped_gemm(aprob["a"], aprob["a_sf"], [wprob["b"][i] for i in bidx],
+                            [wprob["b_sf"][i] for i in bidx], alpha)
+    for g, (o, r) in enumerate(zip(outs, refs)):
+        ok, st = ref.check_close(o.cpu(), r)
+        assert ok, f"group {g}: {st}"
+    rb.last_status()
+
+
 @pytest.mark.slow
 def test_config2_full_size(cuda_device):
     """BASELINE configs[1] at full size: 8 groups, M ~ U[64, 1024], N=4096, K=7168."""
