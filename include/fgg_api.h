@@ -195,6 +195,29 @@ FGG_API int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t w
                         void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Expert-parallel MoE: the byte-moving kernels around the grouped GEMM      */
+/* ------------------------------------------------------------------------ */
+
+/* Dispatch gather: out row r = source row src_row[r] of both NVFP4 tensors
+ * (codes [rows_in, code_bytes], scales [rows_in, sf_bytes]).  Row sizes and
+ * pointers must be multiples of 4 bytes (16 for the vector path).  A source
+ * index outside [0, rows_in) is skipped and sets *bad (device int) to 1.
+ * Replaces the row gather of `moe_gather_plan`
+ * (tasks/muse_prefill_boundary/reference/submission.py:843-895). */
+FGG_API int fgg_moe_gather_rows(const void* codes, const void* sf, int64_t rows_in,
+                                int32_t code_bytes, int32_t sf_bytes, const int32_t* src_row,
+                                int64_t num_rows, void* out_codes, void* out_sf, int* bad,
+                                void* stream);
+/* Combine: out[t, :] = bf16(sum_k weights[t, k] * rows[route_row[t*topk + k], :])
+ * with fp32 accumulation; rows bf16 [num_rows, n], n % 8 == 0, 16-byte
+ * aligned.  A route row outside [0, num_rows) is skipped and sets *bad.
+ * Replaces `moe_combine` (submission.py:843-895: weight the rows, sum them
+ * back per token). */
+FGG_API int fgg_moe_combine(const void* rows, int64_t num_rows, const int32_t* route_row,
+                            const float* weights, int32_t num_tokens, int32_t topk, int32_t n,
+                            void* out, int* bad, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* NVFP4 quantisation (activations and weights)                              */
 /* ------------------------------------------------------------------------ */
 

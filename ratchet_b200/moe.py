@@ -34,7 +34,7 @@ from typing import Callable, Sequence
 import numpy as np
 import torch
 
-from . import ops
+from . import _lib, ops
 
 
 # ------------------------------------------------------------------ routing
@@ -146,9 +146,13 @@ class ExpertParallelMoE:
         self.slot_t = torch.from_numpy(slot).to(dev, torch.int64)
         self.gemm_fn = gemm_fn
         self.pack = None
+        self.bad = None
         if gemm_fn is None:
-            # the product path: packed once, reused by every forward
+            # the product path: weights packed once and reused by every
+            # forward; the gather / combine kernels raise this flag on an
+            # out-of-range row index (see check())
             self.pack = ops.pack_weights(self.w_codes, self.w_sf)
+            self.bad = torch.zeros(1, dtype=torch.int32, device=dev)
         # problem group g = (source rank, local slot), source-major
         self.b_index = [e for _ in range(self.world) for e in range(self.local)]
 
@@ -200,8 +204,18 @@ class ExpertParallelMoE:
         send_splits = send_ce.sum(1).tolist()
         recv_splits = recv_ce.sum(1).tolist()
         rows = order // topk
-        send_codes = x_u8.index_select(0, rows)
-        send_sf = s_u8.index_select(0, rows)
+        if self.gemm_fn is None:
+            S = T * topk
+            send_codes = torch.empty((S, kh), dtype=torch.uint8, device=dev)
+            send_sf = torch.empty((S, ks), dtype=torch.uint8, device=dev)
+            src = rows.to(torch.int32)
+            _lib.check(_lib.lib().fgg_moe_gather_rows(
+                x_u8.data_ptr(), s_u8.data_ptr(), T, kh, ks, src.data_ptr(), S,
+                send_codes.data_ptr(), send_sf.data_ptr(), self.bad.data_ptr(),
+                torch.cuda.current_stream(dev).cuda_stream), "fgg_moe_gather_rows")
+        else:  # host-logic tests without a GPU
+            send_codes = x_u8.index_select(0, rows)
+            send_sf = s_u8.index_select(0, rows)
         R = int(sum(recv_splits))
         xs = torch.as_tensor(x_scale, dtype=torch.float32, device=dev).reshape(1)
         if W == 1:  # nothing leaves the rank
@@ -236,6 +250,18 @@ class ExpertParallelMoE:
         else:
             back = torch.empty((T * topk, self.n), dtype=torch.bfloat16, device=dev)
             self._a2a(back, out, send_splits, recv_splits)
+        if topk_weights is not None and self.gemm_fn is None:
+            # one pass: each token reads its k rows where the dispatch order
+            # left them and writes the weighted sum
+            route_row = torch.empty(T * topk, dtype=torch.int32, device=dev)
+            route_row[order] = torch.arange(T * topk, dtype=torch.int32, device=dev)
+            w = topk_weights.to(dev, torch.float32).contiguous()
+            res = torch.empty((T, self.n), dtype=torch.bfloat16, device=dev)
+            _lib.check(_lib.lib().fgg_moe_combine(
+                back.data_ptr(), T * topk, route_row.data_ptr(), w.data_ptr(), T, topk, self.n,
+                res.data_ptr(), self.bad.data_ptr(), torch.cuda.current_stream(dev).cuda_stream),
+                "fgg_moe_combine")
+            return res
         res = torch.empty_like(back)
         res.index_copy_(0, order, back)
         res = res.view(T, topk, self.n)
@@ -243,3 +269,10 @@ class ExpertParallelMoE:
             return res
         w = topk_weights.to(dev, torch.float32).view(T, topk, 1)
         return (res.float() * w).sum(1).to(torch.bfloat16)
+
+    def check(self) -> None:
+        """Raise if a gather or combine kernel met an out-of-range row index
+        (synchronises the device)."""
+        if self.bad is not None and int(self.bad.item()) != 0:
+            raise _lib.FggError(_lib.FGG_EINVAL, "ExpertParallelMoE",
+                                "a dispatch or combine row index was out of range")

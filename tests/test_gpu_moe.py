@@ -69,6 +69,57 @@ def test_moe_world1(cuda_device):
     ok, st = _check(layer, 0, 333, cuda_device, w_all)
     assert ok, st
     rb.last_status()
+    layer.check()
+
+
+@pytest.mark.parametrize("kh,ks", [(3584, 448), (36, 4)])
+def test_gather_rows_bitexact(cuda_device, kh, ks):
+    """fgg_moe_gather_rows is a byte copy: equal to index_select; an index
+    outside the source is skipped and raises the flag."""
+    from ratchet_b200 import _lib
+
+    L = _lib.lib()
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    src_c = torch.randint(0, 256, (300, kh), dtype=torch.uint8, device=cuda_device, generator=g)
+    src_s = torch.randint(0, 256, (300, ks), dtype=torch.uint8, device=cuda_device, generator=g)
+    idx = torch.randint(0, 300, (1000,), dtype=torch.int32, device=cuda_device, generator=g)
+    out_c = torch.empty((1000, kh), dtype=torch.uint8, device=cuda_device)
+    out_s = torch.empty((1000, ks), dtype=torch.uint8, device=cuda_device)
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(L.fgg_moe_gather_rows(src_c.data_ptr(), src_s.data_ptr(), 300, kh, ks, idx.data_ptr(),
+                                     1000, out_c.data_ptr(), out_s.data_ptr(), bad.data_ptr(), st),
+               "gather")
+    assert torch.equal(out_c, src_c.index_select(0, idx.long()))
+    assert torch.equal(out_s, src_s.index_select(0, idx.long()))
+    assert int(bad.item()) == 0
+    idx[7] = 300  # one past the end: skipped, flagged
+    _lib.check(L.fgg_moe_gather_rows(src_c.data_ptr(), src_s.data_ptr(), 300, kh, ks, idx.data_ptr(),
+                                     1000, out_c.data_ptr(), out_s.data_ptr(), bad.data_ptr(), st),
+               "gather")
+    assert int(bad.item()) == 1
+
+
+def test_combine_matches_fp32_reference(cuda_device):
+    """fgg_moe_combine against plain PyTorch fp32: sum_k w[t,k] * rows[route[t,k]],
+    rounded to bf16 once (tolerance: one bf16 ulp of the result)."""
+    from ratchet_b200 import _lib
+
+    L = _lib.lib()
+    T, k, n = 257, 8, 4096
+    g = torch.Generator(device=cuda_device).manual_seed(6)
+    rows = torch.randn((T * k, n), generator=g, device=cuda_device).to(torch.bfloat16)
+    route = torch.randperm(T * k, generator=g, device=cuda_device).to(torch.int32)
+    w = torch.rand((T, k), generator=g, device=cuda_device)
+    out = torch.empty((T, n), dtype=torch.bfloat16, device=cuda_device)
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    _lib.check(L.fgg_moe_combine(rows.data_ptr(), T * k, route.data_ptr(), w.data_ptr(), T, k, n,
+                                 out.data_ptr(), bad.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream), "combine")
+    want = (rows.float()[route.long()].view(T, k, n) * w[..., None]).sum(1)
+    err = (out.float() - want).abs()
+    assert (err <= want.abs() * 2.0 ** -7 + 1e-6).all()
+    assert int(bad.item()) == 0
 
 
 def _free_port():
