@@ -198,6 +198,19 @@ FGG_API int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t w
 /* Expert-parallel MoE: the byte-moving kernels around the grouped GEMM      */
 /* ------------------------------------------------------------------------ */
 
+/* Dispatch plan: a stable counting sort of the num_tokens x topk routes
+ * (device topk_ids, row-major) by destination bin = owner[e] * local +
+ * slot[e] (device int32 arrays over the num_experts experts; local = experts
+ * per rank, world x local <= 512).  Writes counts[bin] (routes per bin),
+ * src_row[p] (the token of the route at sorted position p) and route_pos[i]
+ * (the sorted position of route i).  Within a bin the routes keep their
+ * order, as a stable sort leaves them.  An expert id outside
+ * [0, num_experts) sets *bad and gets route_pos -1.  Replaces the plan half
+ * of `moe_gather_plan` (submission.py:843-895) and an argsort + bincount. */
+FGG_API int fgg_moe_plan(const int32_t* topk_ids, int32_t num_tokens, int32_t topk,
+                         const int32_t* owner, const int32_t* slot, int32_t num_experts,
+                         int32_t world, int32_t local, int32_t* counts, int32_t* src_row,
+                         int32_t* route_pos, int* bad, void* stream);
 /* Dispatch gather: out row r = source row src_row[r] of both NVFP4 tensors
  * (codes [rows_in, code_bytes], scales [rows_in, sf_bytes]).  Row sizes and
  * pointers must be multiples of 4 bytes (16 for the vector path).  A source

@@ -62,6 +62,8 @@ _SIGS = {
     "fgg_nvfp4_prepare": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_nvfp4_gemm": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_nvfp4_grouped_gemm_noalloc": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, _VOIDP]),
+    "fgg_moe_plan": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int32, _VOIDP, _VOIDP, ctypes.c_int32,
+                                    ctypes.c_int32, ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
     "fgg_moe_gather_rows": (ctypes.c_int, [_VOIDP, _VOIDP, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                            _VOIDP, ctypes.c_int64, _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
     "fgg_moe_combine": (ctypes.c_int, [_VOIDP, ctypes.c_int64, _VOIDP, _VOIDP, ctypes.c_int32, ctypes.c_int32,

@@ -1,6 +1,7 @@
-// fgg_moe.cu - the byte-moving kernels around the expert-parallel grouped
-// GEMM: the dispatch gather (token rows -> route order) and the combine
-// (route rows -> router-weighted sum per token).  Both are HBM-bound copies;
+// fgg_moe.cu - the kernels around the expert-parallel grouped GEMM: the
+// dispatch plan (a stable counting sort of the routes by destination), the
+// dispatch gather (token rows -> route order) and the combine (route rows ->
+// router-weighted sum per token).  Gather and combine are HBM-bound copies;
 // they move 16-byte vectors with coalesced row segments and touch every
 // byte once.
 //
@@ -14,8 +15,8 @@
 namespace fgg {
 namespace {
 
-// One block per destination row group: block (b, part) copies rows
-// b*ROWS .. b*ROWS+ROWS-1 of both tensors, each thread VEC bytes at a time.
+// One block per destination row: block r copies source row src_row[r] of
+// both tensors, each thread sizeof(V) bytes at a time.
 template <typename V>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint8_t* __restrict__ codes,
                                                           const uint8_t* __restrict__ sf,
@@ -80,6 +81,87 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
   *reinterpret_cast<uint4*>(out + int64_t(t) * n + col) = o;
 }
 
+// Dispatch plan: a stable counting sort of the routes by destination bin
+// (owner rank x slot of the expert on it).  One CTA of kPlanWarps warps; warp
+// w owns the contiguous route chunk [w*chunk, (w+1)*chunk) and walks it 32
+// routes at a time, so the order inside a bin is the route order, as a stable
+// sort would leave it.  Lanes holding the same bin in one step are grouped
+// with __match_any_sync: their count goes to the warp's histogram (phase A),
+// and their rank among themselves gives each one its slot (phase C).
+constexpr int kPlanWarps = 16;
+constexpr int kPlanMaxBins = 512;
+
+__global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(
+    const int32_t* __restrict__ ids, int32_t routes, int32_t topk,
+    const int32_t* __restrict__ owner, const int32_t* __restrict__ slot, int32_t num_experts,
+    int32_t local, int32_t bins, int32_t* __restrict__ counts, int32_t* __restrict__ src_row,
+    int32_t* __restrict__ route_pos, int* __restrict__ bad) {
+  extern __shared__ int32_t hist[];  // [kPlanWarps][bins], then bin totals [bins]
+  int32_t* total = hist + kPlanWarps * bins;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kPlanWarps * bins; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int chunk = (routes + kPlanWarps - 1) / kPlanWarps;
+  const int lo = min(routes, warp * chunk), hi = min(routes, lo + chunk);
+  auto bin_of = [&](int i) -> int {  // -1: an id or placement entry out of range
+    const int e = ids[i];
+    if (e < 0 || e >= num_experts) return -1;
+    const int b = owner[e] * local + slot[e];
+    return (slot[e] < 0 || slot[e] >= local || b < 0 || b >= bins) ? -1 : b;
+  };
+  // A: per-warp histogram
+  for (int base = lo; base < hi; base += 32) {
+    const int i = base + lane;
+    const int b = i < hi ? bin_of(i) : -2;
+    if (b == -1) atomicExch(bad, 1);
+    const unsigned same = __match_any_sync(0xffffffffu, b);
+    if (b >= 0 && lane == __ffs(same) - 1) hist[warp * bins + b] += __popc(same);
+    __syncwarp();
+  }
+  __syncthreads();
+  // B: bin totals, exclusive offsets over bins, per-warp bases within a bin
+  for (int b = threadIdx.x; b < bins; b += blockDim.x) {
+    int acc = 0;
+    for (int w = 0; w < kPlanWarps; ++w) acc += hist[w * bins + b];
+    total[b] = acc;
+    counts[b] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // bins <= kPlanMaxBins: a serial scan is a few microseconds
+    int run = 0;
+    for (int b = 0; b < bins; ++b) {
+      const int c = total[b];
+      total[b] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < bins; b += blockDim.x) {
+    int run = total[b];
+    for (int w = 0; w < kPlanWarps; ++w) {
+      const int c = hist[w * bins + b];
+      hist[w * bins + b] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  // C: positions, in the same walk order as A
+  for (int base = lo; base < hi; base += 32) {
+    const int i = base + lane;
+    const int b = i < hi ? bin_of(i) : -2;
+    const unsigned same = __match_any_sync(0xffffffffu, b);
+    int pos = -1;
+    if (b >= 0) pos = hist[warp * bins + b] + __popc(same & ((1u << lane) - 1u));
+    __syncwarp();
+    if (b >= 0 && lane == __ffs(same) - 1) hist[warp * bins + b] += __popc(same);
+    __syncwarp();
+    if (i < hi) {
+      route_pos[i] = pos;
+      if (pos >= 0) src_row[pos] = i / topk;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace fgg
 
@@ -114,6 +196,29 @@ int fgg_moe_gather_rows(const void* codes, const void* sf, int64_t rows_in, int3
         c, f, src_row, rows_in, num_rows, code_bytes, sf_bytes, oc, of, bad);
   else
     return set_error(FGG_EALIGN, "row sizes and pointers must be multiples of 4 bytes");
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+int fgg_moe_plan(const int32_t* topk_ids, int32_t num_tokens, int32_t topk,
+                 const int32_t* owner, const int32_t* slot, int32_t num_experts, int32_t world,
+                 int32_t local, int32_t* counts, int32_t* src_row, int32_t* route_pos, int* bad,
+                 void* stream) {
+  if (num_tokens < 0 || topk < 1 || num_experts < 1 || world < 1 || local < 1)
+    return set_error(FGG_EINVAL, "bad plan sizes");
+  const int64_t bins = int64_t(world) * local;
+  if (bins > kPlanMaxBins)
+    return set_error(FGG_EBADSHAPE, "world x local experts = %lld exceeds %d", (long long)bins,
+                     kPlanMaxBins);
+  const int64_t routes = int64_t(num_tokens) * topk;
+  if (routes > INT32_MAX) return set_error(FGG_EBADSHAPE, "too many routes");
+  if (topk_ids == nullptr || owner == nullptr || slot == nullptr || counts == nullptr ||
+      src_row == nullptr || route_pos == nullptr || bad == nullptr)
+    return set_error(FGG_EINVAL, "null pointer");
+  const size_t smem = size_t(kPlanWarps + 1) * size_t(bins) * sizeof(int32_t);
+  plan_kernel<<<1, kPlanWarps * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      topk_ids, int32_t(routes), topk, owner, slot, num_experts, local, int32_t(bins), counts,
+      src_row, route_pos, bad);
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }

@@ -147,14 +147,19 @@ class ExpertParallelMoE:
         self.gemm_fn = gemm_fn
         self.pack = None
         self.bad = None
+        self.ws = None
         if gemm_fn is None:
             # the product path: weights packed once and reused by every
             # forward; the gather / combine kernels raise this flag on an
             # out-of-range row index (see check())
             self.pack = ops.pack_weights(self.w_codes, self.w_sf)
             self.bad = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.owner_i32 = torch.from_numpy(owner).to(dev)
+            self.slot_i32 = torch.from_numpy(slot).to(dev)
+            self.ws = torch.empty(0, dtype=torch.uint8, device=dev)  # GEMM workspace, grown on demand
         # problem group g = (source rank, local slot), source-major
         self.b_index = [e for _ in range(self.world) for e in range(self.local)]
+        self.b_index_np = np.asarray(self.b_index, dtype=np.int32)
 
     # -------------------------------------------------------------- pieces
     def plan(self, topk_ids: torch.Tensor):
@@ -191,8 +196,21 @@ class ExpertParallelMoE:
                              f"T={T}, K={self.k}")
         dev = x_u8.device
         W, E = self.world, self.local
+        S = T * topk
+        L = _lib.lib() if self.gemm_fn is None else None
+        stream = torch.cuda.current_stream(dev).cuda_stream if L is not None else None
         # 1. plan
-        order, counts = self.plan(topk_ids)
+        if L is not None:
+            ids32 = topk_ids.to(dev, torch.int32).contiguous()
+            counts = torch.empty(W * E, dtype=torch.int32, device=dev)
+            src_row = torch.empty(S, dtype=torch.int32, device=dev)
+            route_pos = torch.empty(S, dtype=torch.int32, device=dev)
+            _lib.check(L.fgg_moe_plan(ids32.data_ptr(), T, topk, self.owner_i32.data_ptr(),
+                                      self.slot_i32.data_ptr(), self.num_experts, W, E,
+                                      counts.data_ptr(), src_row.data_ptr(), route_pos.data_ptr(),
+                                      self.bad.data_ptr(), stream), "fgg_moe_plan")
+        else:  # host-logic tests without a GPU
+            order, counts = self.plan(topk_ids)
         # 2. dispatch: counts first, then the rows they describe
         if W == 1:
             recv_counts = counts
@@ -203,17 +221,15 @@ class ExpertParallelMoE:
         send_ce, recv_ce = both[0].view(W, E), both[1].view(W, E)
         send_splits = send_ce.sum(1).tolist()
         recv_splits = recv_ce.sum(1).tolist()
-        rows = order // topk
-        if self.gemm_fn is None:
-            S = T * topk
+        if L is not None:
             send_codes = torch.empty((S, kh), dtype=torch.uint8, device=dev)
             send_sf = torch.empty((S, ks), dtype=torch.uint8, device=dev)
-            src = rows.to(torch.int32)
-            _lib.check(_lib.lib().fgg_moe_gather_rows(
-                x_u8.data_ptr(), s_u8.data_ptr(), T, kh, ks, src.data_ptr(), S,
-                send_codes.data_ptr(), send_sf.data_ptr(), self.bad.data_ptr(),
-                torch.cuda.current_stream(dev).cuda_stream), "fgg_moe_gather_rows")
-        else:  # host-logic tests without a GPU
+            _lib.check(L.fgg_moe_gather_rows(
+                x_u8.data_ptr(), s_u8.data_ptr(), T, kh, ks, src_row.data_ptr(), S,
+                send_codes.data_ptr(), send_sf.data_ptr(), self.bad.data_ptr(), stream),
+                "fgg_moe_gather_rows")
+        else:
+            rows = order // topk
             send_codes = x_u8.index_select(0, rows)
             send_sf = s_u8.index_select(0, rows)
         R = int(sum(recv_splits))
@@ -229,18 +245,17 @@ class ExpertParallelMoE:
             dist.all_gather(parts, xs, group=self.group)
             src_scale = torch.cat(parts)
         # 3. grouped GEMM over the (source, slot) chunks
-        ms = recv_ce.reshape(-1).tolist()
-        a_list = list(recv_codes.split(ms))
-        sf_list = [t.view(torch.float8_e4m3fn) for t in recv_sf.split(ms)]
         alpha = (src_scale[:, None] * self.w_scale[None, :]).reshape(-1).contiguous()
         out = torch.empty((R, self.n), dtype=torch.bfloat16, device=dev)
         if gemm_events is not None:
             gemm_events[0].record()
-        if self.gemm_fn is None:
+        if L is not None:
             if R > 0:
-                ops.nvfp4_grouped_gemm(a_list, sf_list, self.w_codes, self.w_sf, None, alpha,
-                                       pack=self.pack, out=out, b_index=self.b_index)
+                self._gemm(L, recv_ce, recv_codes, recv_sf, alpha, out, stream)
         else:
+            ms = recv_ce.reshape(-1).tolist()
+            a_list = list(recv_codes.split(ms))
+            sf_list = [t.view(torch.float8_e4m3fn) for t in recv_sf.split(ms)]
             self.gemm_fn(a_list, sf_list, self.b_index, alpha, out)
         if gemm_events is not None:
             gemm_events[1].record()
@@ -250,17 +265,16 @@ class ExpertParallelMoE:
         else:
             back = torch.empty((T * topk, self.n), dtype=torch.bfloat16, device=dev)
             self._a2a(back, out, send_splits, recv_splits)
-        if topk_weights is not None and self.gemm_fn is None:
+        if L is not None:
+            if topk_weights is None:
+                return back.index_select(0, route_pos.long()).view(T, topk, self.n)
             # one pass: each token reads its k rows where the dispatch order
             # left them and writes the weighted sum
-            route_row = torch.empty(T * topk, dtype=torch.int32, device=dev)
-            route_row[order] = torch.arange(T * topk, dtype=torch.int32, device=dev)
             w = topk_weights.to(dev, torch.float32).contiguous()
             res = torch.empty((T, self.n), dtype=torch.bfloat16, device=dev)
-            _lib.check(_lib.lib().fgg_moe_combine(
-                back.data_ptr(), T * topk, route_row.data_ptr(), w.data_ptr(), T, topk, self.n,
-                res.data_ptr(), self.bad.data_ptr(), torch.cuda.current_stream(dev).cuda_stream),
-                "fgg_moe_combine")
+            _lib.check(L.fgg_moe_combine(back.data_ptr(), S, route_pos.data_ptr(), w.data_ptr(), T,
+                                         topk, self.n, res.data_ptr(), self.bad.data_ptr(),
+                                         stream), "fgg_moe_combine")
             return res
         res = torch.empty_like(back)
         res.index_copy_(0, order, back)
@@ -270,9 +284,34 @@ class ExpertParallelMoE:
         w = topk_weights.to(dev, torch.float32).view(T, topk, 1)
         return (res.float() * w).sum(1).to(torch.bfloat16)
 
+    def _gemm(self, L, recv_ce, recv_codes, recv_sf, alpha, out, stream):
+        """The grouped GEMM through the C ABI directly: the group pointers are
+        offsets into the two receive buffers, so no per-group tensor views."""
+        kh, ks = self.k // 2, self.k // 16
+        ms = recv_ce.reshape(-1).numpy().astype(np.int32)
+        offs = np.zeros_like(ms, dtype=np.uint64)
+        offs[1:] = np.cumsum(ms[:-1], dtype=np.uint64)
+        a_ptrs = np.uint64(recv_codes.data_ptr()) + offs * np.uint64(kh)
+        sf_ptrs = np.uint64(recv_sf.data_ptr()) + offs * np.uint64(ks)
+        prob = _lib.FggNvfp4Problem(len(ms), self.n, self.k, ms.ctypes.data, a_ptrs.ctypes.data,
+                                    sf_ptrs.ctypes.data, alpha.data_ptr(), out.data_ptr(),
+                                    self.b_index_np.ctypes.data, self.local)
+        nbytes = int(L.fgg_nvfp4_workspace_bytes(prob))
+        if nbytes == 0:
+            _lib.check(L.fgg_nvfp4_grouped_gemm(prob, None, None, 0, None), "grouped GEMM")
+        if self.ws.numel() < nbytes:
+            self.ws = torch.empty(nbytes, dtype=torch.uint8, device=out.device)
+        _lib.check(L.fgg_nvfp4_grouped_gemm(prob, self.pack.buf.data_ptr(), self.ws.data_ptr(),
+                                            self.ws.numel(), stream), "grouped GEMM")
+
     def check(self) -> None:
-        """Raise if a gather or combine kernel met an out-of-range row index
-        (synchronises the device)."""
+        """Raise if a plan, gather or combine kernel met an out-of-range index,
+        or a bounded wait in the GEMM gave up (synchronises the device)."""
         if self.bad is not None and int(self.bad.item()) != 0:
             raise _lib.FggError(_lib.FGG_EINVAL, "ExpertParallelMoE",
-                                "a dispatch or combine row index was out of range")
+                                "an expert id or a dispatch / combine row index was out of range")
+        if self.ws is not None and self.ws.numel():
+            L = _lib.lib()
+            _lib.check(L.fgg_read_device_status(self.ws.data_ptr(),
+                                                torch.cuda.current_stream(self.device).cuda_stream),
+                       "grouped GEMM status")

@@ -100,6 +100,42 @@ def test_gather_rows_bitexact(cuda_device, kh, ks):
     assert int(bad.item()) == 1
 
 
+@pytest.mark.parametrize("world,T", [(1, 4096), (4, 333), (8, 1)])
+def test_plan_matches_stable_argsort(cuda_device, world, T):
+    """fgg_moe_plan is exactly the stable sort of the routes by (owner, slot):
+    integer work, bit-exact; an expert id out of range is flagged, skipped."""
+    from ratchet_b200 import _lib
+
+    L = _lib.lib()
+    Ex, topk = 64, 8
+    owner, slot = moe.place_experts(moe.expert_popularity(Ex, seed=4), world)
+    ids, _ = moe.zipf_routing(T, Ex, topk, seed=5)
+    key = torch.from_numpy((owner[ids] * (Ex // world) + slot[ids]).reshape(-1).astype(np.int64))
+    order = torch.argsort(key, stable=True)
+    dev = cuda_device
+    d_ids = torch.from_numpy(ids).to(dev)
+    o, s_ = torch.from_numpy(owner).to(dev), torch.from_numpy(slot).to(dev)
+    counts = torch.empty(Ex, dtype=torch.int32, device=dev)
+    src = torch.empty(T * topk, dtype=torch.int32, device=dev)
+    pos = torch.empty(T * topk, dtype=torch.int32, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(L.fgg_moe_plan(d_ids.data_ptr(), T, topk, o.data_ptr(), s_.data_ptr(), Ex, world,
+                              Ex // world, counts.data_ptr(), src.data_ptr(), pos.data_ptr(),
+                              bad.data_ptr(), st), "plan")
+    assert counts.cpu().tolist() == torch.bincount(key, minlength=Ex).tolist()
+    assert torch.equal(src.cpu().long(), order // topk)
+    inv = torch.empty_like(order)
+    inv[order] = torch.arange(order.numel())
+    assert torch.equal(pos.cpu().long(), inv)
+    assert int(bad.item()) == 0
+    d_ids.view(-1)[0] = Ex  # out of range: flagged, position -1
+    _lib.check(L.fgg_moe_plan(d_ids.data_ptr(), T, topk, o.data_ptr(), s_.data_ptr(), Ex, world,
+                              Ex // world, counts.data_ptr(), src.data_ptr(), pos.data_ptr(),
+                              bad.data_ptr(), st), "plan")
+    assert int(bad.item()) == 1 and int(pos[0].item()) == -1
+
+
 def test_combine_matches_fp32_reference(cuda_device):
     """fgg_moe_combine against plain PyTorch fp32: sum_k w[t,k] * rows[route[t,k]],
     rounded to bf16 once (tolerance: one bf16 ulp of the result)."""
