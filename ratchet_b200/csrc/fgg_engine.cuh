@@ -284,10 +284,8 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
     if constexpr (!C::MX) {
       // A pack built for a different problem is refused before any load.
       const PackHeader h = *p.pack;
-      if (h.magic != kPackMagic || h.g != p.wg || h.n != p.n || h.k != p.k) {
-        atomicCAS(p.status, 0, kStatusBadPack);
-        *abort_flag = 1;
-      }
+      // reported after griddep_wait: the prepare kernel resets the status word
+      if (h.magic != kPackMagic || h.g != p.wg || h.n != p.n || h.k != p.k) *abort_flag = 2;
     }
     fence_mbar_init();
   }
@@ -301,7 +299,13 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
     if (lane == 0) mbar_arrive(tmem_ready_bar);
   }
 
+  // Everything above (barriers, TMEM, the weight pack's header) is ready
+  // before this launch; the schedule, token descriptors and scale repack come
+  // from the prepare kernel just before it on the stream, which this launch
+  // may overlap (programmatic dependent launch).
+  griddep_wait();
   const bool aborted_early = (*abort_flag != 0);
+  if (threadIdx.x == 0 && *abort_flag == 2) atomicCAS(p.status, 0, kStatusBadPack);
 
   if (warp == 3) {
     // ------------------------------------------------------------ scheduler
@@ -667,10 +671,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     *abort_flag = 0;
     if constexpr (!C::MX) {
       const PackHeader h = *p.pack;
-      if (h.magic != kPackMagic || h.g != p.wg || h.n != p.n || h.k != p.k) {
-        atomicCAS(p.status, 0, kStatusBadPack);
-        *abort_flag = 1;
-      }
+      // reported after griddep_wait: the prepare kernel resets the status word
+      if (h.magic != kPackMagic || h.g != p.wg || h.n != p.n || h.k != p.k) *abort_flag = 2;
     }
     fence_mbar_init();
   }
@@ -685,7 +687,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     if (lane == 0) mbar_arrive(tmem_ready_bar);
   }
 
+  // Everything above (barriers, TMEM, the weight pack's header) is ready
+  // before this launch; the schedule, token descriptors and scale repack come
+  // from the prepare kernel just before it on the stream, which this launch
+  // may overlap (programmatic dependent launch).
+  griddep_wait();
   const bool aborted_early = (*abort_flag != 0);
+  if (threadIdx.x == 0 && *abort_flag == 2) atomicCAS(p.status, 0, kStatusBadPack);
   const uint32_t leader_schede0 = mapa_shared(schede_bar(0), 0);
   const uint32_t leader_acce0 = mapa_shared(acce_bar(0), 0);
   const uint32_t leader_full0 = mapa_shared(full_bar(0), 0);
@@ -958,6 +966,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   }
 }
 
+// Launch a GEMM kernel as a programmatic dependent of the preceding kernel on
+// the stream: it may start while that kernel (the prepare kernel) finishes,
+// and waits for its results at griddep_wait().  Host only.
+template <class Kernel>
+cudaError_t launch_dependent(Kernel kernel, int grid, uint32_t smem, cudaStream_t s,
+                             const GemmParams& gp) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, gp);
+}
+
 // Set the kernel's dynamic shared memory limit (once per device), then launch
 // one CTA pair per two SMs, or one per tile when there are fewer tiles.  Host only.
 template <class C>
@@ -974,8 +1001,7 @@ cudaError_t launch_pair(const GemmParams& gp, int sm_count, cudaStream_t s) {
   }
   const int pairs_avail = sm_count / 2;
   const int pairs = gp.num_tiles < pairs_avail ? (gp.num_tiles > 0 ? gp.num_tiles : 1) : pairs_avail;
-  fgg_gemm_pair_kernel<C><<<2 * pairs, 256, C::SMEM_BYTES, s>>>(gp);
-  return cudaGetLastError();
+  return launch_dependent(fgg_gemm_pair_kernel<C>, 2 * pairs, C::SMEM_BYTES, s, gp);
 }
 
 // Set the kernel's dynamic shared memory limit (once per device), then launch
@@ -993,8 +1019,7 @@ cudaError_t launch_engine(const GemmParams& gp, int sm_count, cudaStream_t s) {
     configured_device = dev;
   }
   const int grid = gp.num_tiles < sm_count ? (gp.num_tiles > 0 ? gp.num_tiles : 1) : sm_count;
-  fgg_gemm_kernel<C><<<grid, 256, C::SMEM_BYTES, s>>>(gp);
-  return cudaGetLastError();
+  return launch_dependent(fgg_gemm_kernel<C>, grid, C::SMEM_BYTES, s, gp);
 }
 
 }  // namespace fgg

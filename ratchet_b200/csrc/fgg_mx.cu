@@ -45,6 +45,9 @@ __device__ __forceinline__ uint32_t e8m0_byte(float v) {
 }
 
 __global__ void __launch_bounds__(256) mx_prepare_kernel(const __grid_constant__ MxPrepParams p) {
+  // every block is resident once it gets here: the GEMM grid behind this one
+  // may launch now (it waits for this grid's results before reading them)
+  griddep_launch_dependents();
   int blk = blockIdx.x;
   if (blk < p.blocks_tiles) {
     if (blk == 0 && threadIdx.x == 0) {

@@ -50,6 +50,9 @@ __device__ __forceinline__ int find_group(const int32_t* begin, int g_count, int
 }
 
 __global__ void __launch_bounds__(256) nvfp4_prepare_kernel(const __grid_constant__ PrepParams p) {
+  // every block is resident once it gets here: the GEMM grid behind this one
+  // may launch now (it waits for this grid's results before reading them)
+  griddep_launch_dependents();
   __shared__ alignas(128) CUtensorMap smap[8];
   __shared__ int32_t sbegin[FGG_MAX_GROUPS + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -190,6 +190,18 @@ __device__ __forceinline__ void tmap_publish(CUtensorMap* gdst, uint32_t smem_ma
       : "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch
+// Primary side: this block no longer holds back the launch of the next grid
+// on the stream (which must still wait for this grid's results, below).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Dependent side: wait until the preceding grid on the stream has completed
+// and its memory is visible.  Returns at once when no such dependency exists.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // --------------------------------------------------------------- clusters
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
