@@ -49,6 +49,14 @@ struct GroupInfo {
   int32_t wgroup;       // weight group (in the pack) this problem group multiplies with
 };
 
+// Byte offset, inside one replicated 4 KB token-scale block, of the copy of
+// line r0 of atom c that lane r0 + 32q receives (q = 0..3): the source layout
+// of one tcgen05.cp 128x256b (see desc_sf_pair_rep).
+__host__ __device__ __forceinline__ uint32_t sf_rep_offset(int c, int r0, int q) {
+  const int l = r0 + 32 * q;
+  return uint32_t((l >> 3) * 256 + c * 128 + (l & 7) * 16);
+}
+
 // A tile is packed into 32 bits: group (10) | weight tile (11) | token tile (11).
 __host__ __device__ __forceinline__ uint32_t pack_tile(int g, int nt, int xt) {
   return (uint32_t(g) << 22) | (uint32_t(nt) << 11) | uint32_t(xt);
@@ -202,7 +210,12 @@ struct EngineCfg {
   static constexpr uint32_t X_BYTES = BN * 128;
   // NVFP4: 4 atoms (one per K64 MMA); MX: one atom covers the 4 K32 MMAs.
   static constexpr uint32_t SFW_BYTES = MX ? 512 : 4 * 512;
-  static constexpr uint32_t SFX_BYTES = MX ? CH * 512 : 4 * CH * 512;
+  // Token scales of one scale slot: with two atoms (224-token tiles) they come
+  // in the replicated 4 KB layout that one 128x256b copy uploads; one atom
+  // (decode tiles) stays a plain 512-byte atom.
+  static constexpr bool SFX_REP = (CH == 2);
+  static constexpr uint32_t SFX_UNIT = SFX_REP ? 4096 : CH * 512;
+  static constexpr uint32_t SFX_BYTES = MX ? SFX_UNIT : 4 * SFX_UNIT;
   static constexpr uint32_t TX_BYTES = W_TX + X_BYTES + SFW_BYTES + SFX_BYTES;
   static constexpr uint32_t STAGE_BYTES =
       (W_BYTES + X_BYTES + SFW_BYTES + SFX_BYTES + 1023) / 1024 * 1024;
@@ -457,9 +470,13 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
           if constexpr (C::MX) {
             const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
             tc_cp_sf(tmem + col, desc_sf_atom(sSFW(stage)));
+            if constexpr (C::SFX_REP) {
+              tc_cp_sf2(tmem + col + 4, desc_sf_pair_rep(sSFX(stage)));
+            } else {
 #pragma unroll
-            for (int c = 0; c < C::CH; ++c)
-              tc_cp_sf(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(stage) + c * 512));
+              for (int c = 0; c < C::CH; ++c)
+                tc_cp_sf(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(stage) + c * 512));
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               // K step of 32 one-byte elements = 32 bytes = +2 in the start field;
@@ -476,10 +493,14 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
             for (int j = 0; j < 4; ++j) {
               const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
               tc_cp_sf(tmem + col, desc_sf_atom(sSFW(stage) + j * 512));
+              if constexpr (C::SFX_REP) {
+                tc_cp_sf2(tmem + col + 4, desc_sf_pair_rep(sSFX(stage) + j * C::SFX_UNIT));
+              } else {
 #pragma unroll
-              for (int c = 0; c < C::CH; ++c)
-                tc_cp_sf(tmem + col + 4 + 4 * c,
-                         desc_sf_atom(sSFX(stage) + (j * C::CH + c) * 512));
+                for (int c = 0; c < C::CH; ++c)
+                  tc_cp_sf(tmem + col + 4 + 4 * c,
+                           desc_sf_atom(sSFX(stage) + (j * C::CH + c) * 512));
+              }
               // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
               tc_mma_nvf4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col,
                           tmem + col + 4, (ks | j) != 0 ? 1u : 0u);
@@ -587,7 +608,10 @@ struct PairCfg {
   static constexpr uint32_t W_TX = MX ? 64 * 128 : 128 * 128;
   static constexpr uint32_t X_BYTES = BNH * 128;
   static constexpr uint32_t SFW_BYTES = MX ? 512 : 4 * 512;
-  static constexpr uint32_t SFX_BYTES = MX ? CH * 512 : 4 * CH * 512;
+  // token scales of one slot in the replicated layout of one 128x256b copy
+  static constexpr bool SFX_REP = true;
+  static constexpr uint32_t SFX_UNIT = 4096;
+  static constexpr uint32_t SFX_BYTES = MX ? SFX_UNIT : 4 * SFX_UNIT;
   // SF atoms travel as 2-D uint64 boxes {ROW_U64, BOX_ROWS}
   static constexpr uint32_t SFW_ROW_U64 = SFW_BYTES / 8 > 256 ? 256 : SFW_BYTES / 8;
   static constexpr uint32_t SFW_BOX_ROWS = SFW_BYTES / (8 * SFW_ROW_U64);
@@ -864,9 +888,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           if constexpr (C::MX) {
             const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
             tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(stage)));
-#pragma unroll
-            for (int c = 0; c < C::CH; ++c)
-              tc_cp_sf_pair(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(stage) + c * 512));
+            tc_cp_sf2_pair(tmem + col + 4, desc_sf_pair_rep(sSFX(stage)));
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const uint32_t idj =
@@ -881,10 +903,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             for (int j = 0; j < 4; ++j) {
               const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
               tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(stage) + j * 512));
-#pragma unroll
-              for (int c = 0; c < C::CH; ++c)
-                tc_cp_sf_pair(tmem + col + 4 + 4 * c,
-                              desc_sf_atom(sSFX(stage) + (j * C::CH + c) * 512));
+              tc_cp_sf2_pair(tmem + col + 4, desc_sf_pair_rep(sSFX(stage) + j * C::SFX_UNIT));
               tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col,
                                tmem + col + 4, (ks | j) != 0 ? 1u : 0u);
               sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;

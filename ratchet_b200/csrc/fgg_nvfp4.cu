@@ -121,9 +121,17 @@ __global__ void __launch_bounds__(256) nvfp4_prepare_kernel(const __grid_constan
     if (rr < p.bn && row < p.m[g] && 4 * j < kq)
       v[r1] = __ldg(reinterpret_cast<const uint32_t*>(p.a_sf[g] + size_t(row) * kq + 4 * j));
   }
-  uint4* dst = reinterpret_cast<uint4*>(p.sfx_out + (size_t(X) * p.nk64p + j) * (p.ch * 512u) +
-                                        size_t(c) * 512u + size_t(r0) * 16u);
-  *dst = make_uint4(v[0], v[1], v[2], v[3]);
+  const uint4 line16 = make_uint4(v[0], v[1], v[2], v[3]);
+  if (p.ch == 2) {
+    // 224-token tiles: the replicated block one 128x256b copy uploads
+    uint8_t* blk4k = p.sfx_out + (size_t(X) * p.nk64p + j) * 4096u;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(blk4k + sf_rep_offset(c, r0, q)) = line16;
+  } else {
+    *reinterpret_cast<uint4*>(p.sfx_out + (size_t(X) * p.nk64p + j) * (p.ch * 512u) +
+                              size_t(r0) * 16u) = line16;
+  }
 }
 
 struct PackParams {
@@ -186,9 +194,9 @@ __global__ void __launch_bounds__(256) nvfp4_pack_weights_kernel(const __grid_co
 }
 
 // ------------------------------------------------------------ host side
-using CfgPrefill = EngineCfg<false, 224, 4>;   // one CTA per tile (N % 256 != 0)
+using CfgPrefill = EngineCfg<false, 224, 3>;   // one CTA per tile (N % 256 != 0)
 using CfgDecode = EngineCfg<false, 16, 8>;     // every group has M <= 16
-using CfgPair = PairCfg<false, 6>;             // CTA pairs, 256 x 224 tiles
+using CfgPair = PairCfg<false, 4>;             // CTA pairs, 256 x 224 tiles
 
 struct PackLayout {
   size_t header, tmaps, sfw, total;
@@ -278,7 +286,9 @@ static int plan(const FggNvfp4Problem* p, WsLayout* L) {
   L->tmaps = cv.take(size_t(G) * sizeof(CUtensorMap), 128);
   L->ginfo = cv.take(size_t(G) * sizeof(GroupInfo), 256);
   L->tiles = cv.take(size_t(std::max<int64_t>(tiles, 1)) * 4, 256);
-  L->sfx = cv.take(size_t(std::max<int64_t>(xts, 1)) * L->nk64p * L->ch * 512, 256);
+  // token scales per (token tile, MMA): two atoms in the 4 KB replicated layout
+  // of one 128x256b copy, or one plain 512-byte atom for 16-token tiles
+  L->sfx = cv.take(size_t(std::max<int64_t>(xts, 1)) * L->nk64p * (L->ch == 2 ? 4096 : 512), 256);
   L->total = cv.off;
   return FGG_OK;
 }

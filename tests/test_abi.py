@@ -92,7 +92,7 @@ def _ws_bytes_py(ms, n, k):
     take(len(ms) * 128, 128)
     take(len(ms) * 16, 256)
     take(max(tiles, 1) * 4, 256)
-    take(max(xts, 1) * nk64p * ch * 512, 256)
+    take(max(xts, 1) * nk64p * (4096 if ch == 2 else 512), 256)  # 224-token tiles: replicated
     return off
 
 
