@@ -607,7 +607,10 @@ struct PairCfg {
   static constexpr uint32_t W_BYTES = 128 * 128;
   static constexpr uint32_t W_TX = MX ? 64 * 128 : 128 * 128;
   static constexpr uint32_t X_BYTES = BNH * 128;
-  static constexpr uint32_t SFW_BYTES = MX ? 512 : 4 * 512;
+  // Weight scales of a K step.  MX: one atom for the 4 MMAs.  NVFP4: the atoms
+  // of MMAs (0, 1) and (2, 3), each pair in the replicated 4 KB layout of one
+  // 128x256b copy, built by four TMA loads of 1 KB from the plain atoms.
+  static constexpr uint32_t SFW_BYTES = MX ? 512 : 2 * 4096;
   // token scales of one slot in the replicated layout of one 128x256b copy
   static constexpr bool SFX_REP = true;
   static constexpr uint32_t SFX_UNIT = 4096;
@@ -622,7 +625,9 @@ struct PairCfg {
       (W_BYTES + X_BYTES + SFW_BYTES + SFX_BYTES + 1023) / 1024 * 1024;
   static_assert((W_BYTES + X_BYTES) % 1024 == 0, "operand tiles must stay 1024 B aligned");
   static constexpr int SF_BASE = 2 * BN;          // 448
-  static constexpr int SF_SLOT = 4 + 4 * CH;      // 12 columns
+  // MX: [weights 4 | tokens 8] per K step.  NVFP4: per MMA pair,
+  // [weights a 4 | weights b 4 | tokens a 8 | tokens b 8].
+  static constexpr int SF_SLOT = MX ? 12 : 24;
   static constexpr int NSLOTS = (512 - SF_BASE) / SF_SLOT;
   static_assert(NSLOTS >= 2, "not enough TMEM for the scale ring");
   static_assert(SF_BASE + NSLOTS * SF_SLOT <= 512, "TMEM columns exceeded");
@@ -812,6 +817,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const int xrow = xti * C::BN + int(rank) * half;
         const int sfw_y =
             ((s.wgroup * p.nt128 + 2 * nti + int(rank)) * p.ksteps) * int(C::SFW_BOX_ROWS);
+        // NVFP4: index of this CTA's first weight atom of the tile (4 per K step)
+        const int sfw_atom0 = (s.wgroup * p.nt128 + 2 * nti + int(rank)) * p.ksteps * 4;
         const int sfx_y = (s.xtile_index * p.ksteps) * int(C::SFX_BOX_ROWS);
         bool ok = true;
         for (int ks = 0; ks < p.ksteps; ++ks) {
@@ -827,7 +834,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           else
             tma_load_2d_pair(sW(stage), tw, fb, ks * 128, wrow);
           tma_load_2d_pair(sX(stage), tx, fb, ks * 128, xrow);
-          tma_load_2d_pair(sSFW(stage), &p.sfw_map, fb, 0, sfw_y + ks * int(C::SFW_BOX_ROWS));
+          if constexpr (C::MX) {
+            tma_load_2d_pair(sSFW(stage), &p.sfw_map, fb, 0, sfw_y + ks * int(C::SFW_BOX_ROWS));
+          } else {
+            // MMA pairs (0, 1) and (2, 3): four identical 1 KB quarters each
+#pragma unroll
+            for (int pp = 0; pp < 2; ++pp)
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                tma_load_3d_pair(sSFW(stage) + pp * 4096 + q * 1024, &p.sfw_map, fb, 0,
+                                 sfw_atom0 + ks * 4 + 2 * pp, 0);
+          }
           tma_load_2d_pair(sSFX(stage), &p.sfx_map, fb, 0, sfx_y + ks * int(C::SFX_BOX_ROWS));
           ++arms;
           if (++stage == C::STAGES) {
@@ -900,12 +917,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
           } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int pp = 0; pp < 2; ++pp) {  // MMA pairs (2pp, 2pp+1) share one weight upload
               const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-              tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(stage) + j * 512));
-              tc_cp_sf2_pair(tmem + col + 4, desc_sf_pair_rep(sSFX(stage) + j * C::SFX_UNIT));
-              tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col,
-                               tmem + col + 4, (ks | j) != 0 ? 1u : 0u);
+              tc_cp_sf2_pair(tmem + col, desc_sf_pair_rep(sSFW(stage) + pp * 4096));
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int j = 2 * pp + h;
+                tc_cp_sf2_pair(tmem + col + 8 + 8 * h,
+                               desc_sf_pair_rep(sSFX(stage) + j * C::SFX_UNIT));
+                tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc,
+                                 tmem + col + 4 * h, tmem + col + 8 + 8 * h,
+                                 (ks | j) != 0 ? 1u : 0u);
+              }
               sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
             }
           }

@@ -466,10 +466,10 @@ int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uin
   gp.nt128 = L.nt128;
   cudaError_t e;
   if (L.pair) {
-    // scale-factor atoms as 2-D uint64 tensors: weights 2 KB per (group, 128-row
-    // tile, K step); tokens 4 KB per (token tile, K step) as two 2 KB rows
-    if (int rc = encode_u64_rows(&gp.sfw_map, gp.sfw, uint64_t(L.wg) * L.nt128 * L.nk256,
-                                 CfgPair::SFW_ROW_U64, CfgPair::SFW_BOX_ROWS))
+    // weight scale atoms as a 3-D uint64 tensor whose boxes build the replicated
+    // layout of two atoms; token scales (already replicated by the prepare
+    // kernel, 16 KB per token tile and K step) as 2 KB rows
+    if (int rc = encode_sf_pairs(&gp.sfw_map, gp.sfw, uint64_t(L.wg) * L.nt128 * L.nk64p))
       return rc;
     if (int rc = encode_u64_rows(&gp.sfx_map, gp.sfx,
                                  uint64_t(L.xt_total) * L.nk256 * CfgPair::SFX_BOX_ROWS,
