@@ -134,22 +134,6 @@ def pack_weights(b_list, b_sf_list) -> WeightPack:
     return _PACKS.get_or(key, lambda: WeightPack(b_list, b_sf_list))
 
 
-def _problem_sizes(problem_sizes, G, n, k, a_list):
-    if problem_sizes is None:
-        return [int(a.shape[0]) for a in a_list]
-    ps = problem_sizes.tolist() if isinstance(problem_sizes, torch.Tensor) else list(problem_sizes)
-    if len(ps) != G:
-        raise ValueError(f"problem_sizes has {len(ps)} entries for {G} groups")
-    ms = []
-    for g, row in enumerate(ps):
-        m_, n_, k_ = (int(v) for v in row)
-        if (n_, k_) != (n, k) or m_ != int(a_list[g].shape[0]):
-            raise ValueError(f"problem_sizes[{g}]={tuple(row)} disagrees with the tensors "
-                             f"(M={int(a_list[g].shape[0])}, N={n}, K={k})")
-        ms.append(m_)
-    return ms
-
-
 def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None, alpha=None,
                        *, pack: WeightPack | None = None, out: torch.Tensor | None = None,
                        b_index=None) -> list[torch.Tensor]:
@@ -182,21 +166,39 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
     if pack is None:
         pack = pack_weights(b_list, b_sf_list)
     n, k, dev = pack.n, pack.k, pack.device
-    ms = _problem_sizes(problem_sizes, G, n, k, a_list)
+    ps = None
+    if problem_sizes is not None:
+        ps = problem_sizes.tolist() if isinstance(problem_sizes, torch.Tensor) else problem_sizes
+        if len(ps) != G:
+            raise ValueError(f"problem_sizes has {len(ps)} entries for {G} groups")
     kh, ks = k // 2, k // 16
-    a_u8, sf_u8 = [], []
-    for g, (a, s, m) in enumerate(zip(a_list, a_sf_list, ms)):
-        if a.dtype is not torch.uint8:
-            a = _as_u8(a, f"a[{g}]")
-        if s.dtype is not torch.uint8:
-            s = _as_u8(s, f"a_sf[{g}]")
-        if a.shape != (m, kh) or s.shape != (m, ks):
-            raise ValueError(f"group {g}: a {tuple(a.shape)} / a_sf {tuple(s.shape)} do not match "
-                             f"M={m}, K={k}")
+    # One pass over the groups (decode calls carry hundreds), no per-group
+    # views: byte dtypes are read through their data pointers as they are.
+    ms = [0] * G
+    pa = np.empty(G, dtype=np.uint64)
+    psf = np.empty(G, dtype=np.uint64)
+    u8 = _U8_DTYPES
+    for g in range(G):
+        a, s = a_list[g], a_sf_list[g]
+        sa = a.shape
+        m = sa[0] if len(sa) == 2 else -1
+        if ps is not None:
+            row = ps[g]
+            if len(row) != 3 or row[0] != m or row[1] != n or row[2] != k:
+                raise ValueError(f"problem_sizes[{g}]={tuple(row)} disagrees with the tensors "
+                                 f"(M={m}, N={n}, K={k})")
+        if a.dtype not in u8:
+            _as_u8(a, f"a[{g}]")
+        if s.dtype not in u8:
+            _as_u8(s, f"a_sf[{g}]")
+        if m < 0 or sa[1] != kh or s.shape != (m, ks):
+            raise ValueError(f"group {g}: a {tuple(sa)} / a_sf {tuple(s.shape)} do not match "
+                             f"[M, {kh}] / [M, {ks}] for K={k}")
         if m and not (a.is_cuda and s.is_cuda and a.is_contiguous() and s.is_contiguous()):
             raise ValueError(f"group {g}: activations must be contiguous CUDA tensors")
-        a_u8.append(a)
-        sf_u8.append(s)
+        ms[g] = m
+        pa[g] = a.data_ptr()
+        psf[g] = s.data_ptr()
     if alpha is None:
         alpha_t = torch.ones(G, dtype=torch.float32, device=dev)
     elif isinstance(alpha, torch.Tensor):
@@ -213,7 +215,6 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
         raise ValueError(f"out must be a contiguous bf16 [{total}, {n}] tensor on {dev}")
     L = _lib.lib()
     m_arr = np.asarray(ms, dtype=np.int32)
-    pa, psf = _ptr_array(a_u8), _ptr_array(sf_u8)
     prob = _lib.FggNvfp4Problem(G, n, k, m_arr.ctypes.data, pa.ctypes.data, psf.ctypes.data,
                                 alpha_t.data_ptr(), out.data_ptr(),
                                 None if bidx is None else bidx.ctypes.data, len(b_list))

@@ -76,3 +76,30 @@ def test_lru_evicts_oldest():
 def test_quantize_rejects_cpu():
     with pytest.raises(ValueError):
         rb.quantize_nvfp4(torch.zeros((4, 32)))
+
+
+def test_problem_sizes_checked_against_tensors():
+    """problem_sizes rows (M_g, N, K) must agree with the activation tensors;
+    checked before any device work (a stand-in pack with no device buffer)."""
+    import types
+
+    fake = types.SimpleNamespace(n=256, k=128, device=torch.device("cpu"))
+    a = [torch.zeros((m, 64), dtype=torch.uint8) for m in (3, 0, 17)]
+    sf = [torch.zeros((m, 8), dtype=torch.uint8) for m in (3, 0, 17)]
+    b = [None] * 3
+
+    def call(ps):
+        return rb.nvfp4_grouped_gemm(a, sf, b, b, ps, pack=fake)
+
+    with pytest.raises(ValueError, match=r"problem_sizes\[0\]"):
+        call([(4, 256, 128), (0, 256, 128), (17, 256, 128)])
+    with pytest.raises(ValueError, match=r"problem_sizes\[0\]"):
+        call(torch.tensor([[3, 128, 128], [0, 256, 128], [17, 256, 128]]))
+    with pytest.raises(ValueError, match="3 groups"):
+        call([(3, 256, 128)])
+    # agreeing sizes pass the check and stop at the CPU tensors: no CPU fallback
+    with pytest.raises(ValueError, match="CUDA"):
+        call([(3, 256, 128), (0, 256, 128), (17, 256, 128)])
+    with pytest.raises(ValueError, match=r"group 0: a \(3, 32\)"):
+        rb.nvfp4_grouped_gemm([torch.zeros((3, 32), dtype=torch.uint8), a[1], a[2]], sf, b, b,
+                              pack=fake)
