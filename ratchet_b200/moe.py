@@ -10,9 +10,9 @@ per GPU) and the rows travel between ranks:
   1. plan      every (token, k) route gets its owner rank and the expert's
                slot on that rank; routes are ordered by (rank, slot) with one
                stable sort, and counted per (rank, slot)
-  2. dispatch  all-to-all of the counts, then of the NVFP4 rows (codes and
-               E4M3 scales) in that order, plus an all-gather of each rank's
-               activation decode scale
+  2. dispatch  all-to-all of the counts (with each rank's activation decode
+               scale), then of the NVFP4 rows (codes and E4M3 scales) in that
+               order
   3. GEMM      the received rows are source-major: the rows of one local
                expert arrive as one contiguous chunk per source rank.  Each
                (source, expert) chunk is one problem group of the grouped
@@ -185,8 +185,6 @@ class ExpertParallelMoE:
         weighted sum over k) when topk_weights [T, k] is given.
         gemm_events: optional (start, end) CUDA events recorded around the
         grouped GEMM on the current stream (for timing the kernel alone)."""
-        import torch.distributed as dist
-
         T, topk = int(topk_ids.shape[0]), int(topk_ids.shape[1])
         kh, ks = self.k // 2, self.k // 16
         x_u8 = x_codes.view(torch.uint8)
@@ -211,16 +209,19 @@ class ExpertParallelMoE:
                                       self.bad.data_ptr(), stream), "fgg_moe_plan")
         else:  # host-logic tests without a GPU
             order, counts = self.plan(topk_ids)
-        # 2. dispatch: counts first, then the rows they describe
+        # 2. to every rank: the counts of the routes it gets from here and
+        #    this rank's activation decode scale (its bits after the counts)
+        xs = torch.as_tensor(x_scale, dtype=torch.float32, device=dev).reshape(1)
+        info = torch.empty((W, E + 1), dtype=torch.int32, device=dev)
+        info[:, :E] = counts.view(W, E)
+        info[:, E] = xs.view(torch.int32)
         if W == 1:
-            recv_counts = counts
+            recv_info = info
         else:
-            recv_counts = torch.empty_like(counts)
-            self._a2a(recv_counts, counts)
-        both = torch.stack([counts, recv_counts]).cpu()  # one host sync per forward
-        send_ce, recv_ce = both[0].view(W, E), both[1].view(W, E)
-        send_splits = send_ce.sum(1).tolist()
-        recv_splits = recv_ce.sum(1).tolist()
+            recv_info = torch.empty_like(info)
+            self._a2a(recv_info, info)
+        # 3. the rows in (owner, slot) order: launched before the host waits
+        #    for the counts, so the device gathers while the host syncs
         if L is not None:
             send_codes = torch.empty((S, kh), dtype=torch.uint8, device=dev)
             send_sf = torch.empty((S, ks), dtype=torch.uint8, device=dev)
@@ -232,19 +233,20 @@ class ExpertParallelMoE:
             rows = order // topk
             send_codes = x_u8.index_select(0, rows)
             send_sf = s_u8.index_select(0, rows)
+        both = torch.stack([info, recv_info]).cpu()  # one host sync per forward
+        send_ce, recv_ce = both[0, :, :E], both[1, :, :E]
+        send_splits = send_ce.sum(1).tolist()
+        recv_splits = recv_ce.sum(1).tolist()
+        src_scale = recv_info[:, E].contiguous().view(torch.float32)
         R = int(sum(recv_splits))
-        xs = torch.as_tensor(x_scale, dtype=torch.float32, device=dev).reshape(1)
         if W == 1:  # nothing leaves the rank
-            recv_codes, recv_sf, src_scale = send_codes, send_sf, xs
+            recv_codes, recv_sf = send_codes, send_sf
         else:
             recv_codes = torch.empty((R, kh), dtype=torch.uint8, device=dev)
             recv_sf = torch.empty((R, ks), dtype=torch.uint8, device=dev)
             self._a2a(recv_codes, send_codes, recv_splits, send_splits)
             self._a2a(recv_sf, send_sf, recv_splits, send_splits)
-            parts = [torch.empty_like(xs) for _ in range(W)]
-            dist.all_gather(parts, xs, group=self.group)
-            src_scale = torch.cat(parts)
-        # 3. grouped GEMM over the (source, slot) chunks
+        # 4. grouped GEMM over the (source, slot) chunks
         alpha = (src_scale[:, None] * self.w_scale[None, :]).reshape(-1).contiguous()
         out = torch.empty((R, self.n), dtype=torch.bfloat16, device=dev)
         if gemm_events is not None:
@@ -259,7 +261,7 @@ class ExpertParallelMoE:
             self.gemm_fn(a_list, sf_list, self.b_index, alpha, out)
         if gemm_events is not None:
             gemm_events[1].record()
-        # 4. combine: rows go back along the dispatch splits, then to route order
+        # 5. combine: rows go back along the dispatch splits, then to route order
         if W == 1:
             back = out
         else:
