@@ -596,12 +596,16 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
 // schedule ring, whose slots the leader writes into the follower's shared
 // memory: those waits acquire at cluster scope.
 // ====================================================================
-template <bool MX_, int STAGES_>
+template <bool MX_, int STAGES_, int KSUB_ = 1>
 struct PairCfg {
   static constexpr bool MX = MX_;
   static constexpr int BN = 224;   // tokens per pair tile = MMA N
   static constexpr int BNH = 112;  // token rows one CTA loads
   static constexpr int STAGES = STAGES_;
+  // K steps per pipeline stage: one barrier wait and one commit on the MMA
+  // thread cover KSUB K steps
+  static constexpr int KSUB = KSUB_;
+  static_assert(KSUB == 1 || KSUB == 2, "one or two K steps per stage");
   static constexpr int CH = 2;     // 128-row token SF atoms per tile
   static constexpr int K_STEP = MX ? 128 : 256;
   static constexpr uint32_t W_BYTES = 128 * 128;
@@ -621,8 +625,10 @@ struct PairCfg {
   static constexpr uint32_t SFX_ROW_U64 = SFX_BYTES / 8 > 256 ? 256 : SFX_BYTES / 8;
   static constexpr uint32_t SFX_BOX_ROWS = SFX_BYTES / (8 * SFX_ROW_U64);
   static constexpr uint32_t TX_CTA = W_TX + X_BYTES + SFW_BYTES + SFX_BYTES;
-  static constexpr uint32_t STAGE_BYTES =
+  // bytes of one K step's tiles; a stage holds KSUB of them
+  static constexpr uint32_t SUB_BYTES =
       (W_BYTES + X_BYTES + SFW_BYTES + SFX_BYTES + 1023) / 1024 * 1024;
+  static constexpr uint32_t STAGE_BYTES = KSUB * SUB_BYTES;
   static_assert((W_BYTES + X_BYTES) % 1024 == 0, "operand tiles must stay 1024 B aligned");
   static constexpr int SF_BASE = 2 * BN;          // 448
   // MX: [weights 4 | tokens 8] per K step.  NVFP4: per MMA pair,
@@ -672,11 +678,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   const bool leader = (rank == 0);
   const uint32_t peer = rank ^ 1u;
 
-  auto sW = [&](int s) { return base + s * C::STAGE_BYTES; };
-  auto sX = [&](int s) { return base + s * C::STAGE_BYTES + C::W_BYTES; };
-  auto sSFW = [&](int s) { return base + s * C::STAGE_BYTES + C::W_BYTES + C::X_BYTES; };
-  auto sSFX = [&](int s) {
-    return base + s * C::STAGE_BYTES + C::W_BYTES + C::X_BYTES + C::SFW_BYTES;
+  // tiles of K-step slot q = stage * KSUB + (K step within the stage)
+  auto sW = [&](int q) { return base + q * C::SUB_BYTES; };
+  auto sX = [&](int q) { return base + q * C::SUB_BYTES + C::W_BYTES; };
+  auto sSFW = [&](int q) { return base + q * C::SUB_BYTES + C::W_BYTES + C::X_BYTES; };
+  auto sSFX = [&](int q) {
+    return base + q * C::SUB_BYTES + C::W_BYTES + C::X_BYTES + C::SFW_BYTES;
   };
   // MMA N of a tile: a multiple of 32 so that each CTA holds a multiple of 16 rows
   auto tile_ncols = [&](int rows) -> int { return min(C::BN, (rows + 31) & ~31); };
@@ -821,31 +828,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const int sfw_atom0 = (s.wgroup * p.nt128 + 2 * nti + int(rank)) * p.ksteps * 4;
         const int sfx_y = (s.xtile_index * p.ksteps) * int(C::SFX_BOX_ROWS);
         bool ok = true;
-        for (int ks = 0; ks < p.ksteps; ++ks) {
+        for (int ks0 = 0; ks0 < p.ksteps; ks0 += C::KSUB) {
           if (!mbar_wait1(empty_bar(stage), phase ^ 1, abort_flag, p.status,
                           kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
-          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2u * C::TX_CTA);
-          const uint32_t fb = leader_full0 + 8u * stage;
-          if constexpr (C::MX)
-            tma_load_3d_pair(sW(stage), tw, fb, ks * C::K_STEP, wrow, g);
-          else
-            tma_load_2d_pair(sW(stage), tw, fb, ks * 128, wrow);
-          tma_load_2d_pair(sX(stage), tx, fb, ks * 128, xrow);
-          if constexpr (C::MX) {
-            tma_load_2d_pair(sSFW(stage), &p.sfw_map, fb, 0, sfw_y + ks * int(C::SFW_BOX_ROWS));
-          } else {
-            // MMA pairs (0, 1) and (2, 3): four identical 1 KB quarters each
-#pragma unroll
-            for (int pp = 0; pp < 2; ++pp)
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-                tma_load_3d_pair(sSFW(stage) + pp * 4096 + q * 1024, &p.sfw_map, fb, 0,
-                                 sfw_atom0 + ks * 4 + 2 * pp, 0);
+          if (leader) {
+            if constexpr (C::KSUB == 1)
+              mbar_arrive_expect_tx(full_bar(stage), 2u * C::TX_CTA);
+            else
+              mbar_arrive_expect_tx(full_bar(stage),
+                                    2u * C::TX_CTA * uint32_t(min(C::KSUB, p.ksteps - ks0)));
           }
-          tma_load_2d_pair(sSFX(stage), &p.sfx_map, fb, 0, sfx_y + ks * int(C::SFX_BOX_ROWS));
+          const uint32_t fb = leader_full0 + 8u * stage;
+#pragma unroll
+          for (int sub = 0; sub < C::KSUB; ++sub) {
+            const int ks = ks0 + sub;
+            if constexpr (C::KSUB > 1) {
+              if (ks >= p.ksteps) break;
+            }
+            const int q = stage * C::KSUB + sub;
+            if constexpr (C::MX)
+              tma_load_3d_pair(sW(q), tw, fb, ks * C::K_STEP, wrow, g);
+            else
+              tma_load_2d_pair(sW(q), tw, fb, ks * 128, wrow);
+            tma_load_2d_pair(sX(q), tx, fb, ks * 128, xrow);
+            if constexpr (C::MX) {
+              tma_load_2d_pair(sSFW(q), &p.sfw_map, fb, 0, sfw_y + ks * int(C::SFW_BOX_ROWS));
+            } else {
+              // MMA pairs (0, 1) and (2, 3): four identical 1 KB quarters each
+#pragma unroll
+              for (int pp = 0; pp < 2; ++pp)
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq)
+                  tma_load_3d_pair(sSFW(q) + pp * 4096 + qq * 1024, &p.sfw_map, fb, 0,
+                                   sfw_atom0 + ks * 4 + 2 * pp, 0);
+            }
+            tma_load_2d_pair(sSFX(q), &p.sfx_map, fb, 0, sfx_y + ks * int(C::SFX_BOX_ROWS));
+          }
           ++arms;
           if (++stage == C::STAGES) {
             stage = 0;
@@ -894,42 +915,51 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const uint32_t d_tmem = tmem + b * C::BN;
         const uint32_t idesc =
             C::MX ? 0u : idesc_block_scaled(kFmtNvf4E2M1, kFmtNvf4E2M1, 0, 256, ncols, 0, 0);
-        for (int ks = 0; ks < p.ksteps; ++ks) {
+        for (int ks0 = 0; ks0 < p.ksteps; ks0 += C::KSUB) {
           if (!mbar_wait1(full_bar(stage), phase, abort_flag, p.status, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = desc_k_sw128(sW(stage));
-          const uint64_t bdesc = desc_k_sw128(sX(stage));
-          if constexpr (C::MX) {
-            const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-            tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(stage)));
-            tc_cp_sf2_pair(tmem + col + 4, desc_sf_pair_rep(sSFX(stage)));
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t idj =
-                  idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 256, ncols, j, j);
-              tc_mma_mxf8f6f4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
-                                   (tmem + col) | (uint32_t(j) << 30),
-                                   (tmem + col + 4) | (uint32_t(j) << 30), (ks | j) != 0 ? 1u : 0u);
+          for (int sub = 0; sub < C::KSUB; ++sub) {
+            const int ks = ks0 + sub;
+            if constexpr (C::KSUB > 1) {
+              if (ks >= p.ksteps) break;
             }
-            sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
-          } else {
-#pragma unroll
-            for (int pp = 0; pp < 2; ++pp) {  // MMA pairs (2pp, 2pp+1) share one weight upload
+            const int q = stage * C::KSUB + sub;  // this K step's slot in the stage
+            const uint64_t adesc = desc_k_sw128(sW(q));
+            const uint64_t bdesc = desc_k_sw128(sX(q));
+            if constexpr (C::MX) {
               const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-              tc_cp_sf2_pair(tmem + col, desc_sf_pair_rep(sSFW(stage) + pp * 4096));
+              tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(q)));
+              tc_cp_sf2_pair(tmem + col + 4, desc_sf_pair_rep(sSFX(q)));
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int j = 2 * pp + h;
-                tc_cp_sf2_pair(tmem + col + 8 + 8 * h,
-                               desc_sf_pair_rep(sSFX(stage) + j * C::SFX_UNIT));
-                tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc,
-                                 tmem + col + 4 * h, tmem + col + 8 + 8 * h,
-                                 (ks | j) != 0 ? 1u : 0u);
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t idj =
+                    idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 256, ncols, j, j);
+                tc_mma_mxf8f6f4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
+                                     (tmem + col) | (uint32_t(j) << 30),
+                                     (tmem + col + 4) | (uint32_t(j) << 30),
+                                     (ks | j) != 0 ? 1u : 0u);
               }
               sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+            } else {
+#pragma unroll
+              for (int pp = 0; pp < 2; ++pp) {  // MMA pairs (2pp, 2pp+1) share one weight upload
+                const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
+                tc_cp_sf2_pair(tmem + col, desc_sf_pair_rep(sSFW(q) + pp * 4096));
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int j = 2 * pp + h;
+                  tc_cp_sf2_pair(tmem + col + 8 + 8 * h,
+                                 desc_sf_pair_rep(sSFX(q) + j * C::SFX_UNIT));
+                  tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc,
+                                   tmem + col + 4 * h, tmem + col + 8 + 8 * h,
+                                   (ks | j) != 0 ? 1u : 0u);
+                }
+                sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+              }
             }
           }
           tc_commit_pair(empty_bar(stage), 0x3);
