@@ -371,7 +371,13 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
           slot = 0;
           sphase ^= 1;
         }
-        if (s.tile == kEndTile) break;
+        if (s.tile == kEndTile) {
+          // no new tiles for this CTA: the next kernel on the stream (the next
+          // call's prepare kernel) may launch; it waits for this grid's
+          // completion before it touches memory
+          griddep_launch_dependents();
+          break;
+        }
         const int g = int(s.tile >> 22);
         const int nti = int((s.tile >> 11) & 0x7FFu);
         const int xti = int(s.tile & 0x7FFu);
@@ -798,7 +804,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           slot = 0;
           sphase ^= 1;
         }
-        if (s.tile == kEndTile) break;
+        if (s.tile == kEndTile) {
+          griddep_launch_dependents();  // as in the single-CTA kernel
+          break;
+        }
         const int g = int(s.tile >> 22);
         const int nti = int((s.tile >> 11) & 0x7FFu);
         const int xti = int(s.tile & 0x7FFu);
@@ -1038,12 +1047,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   }
 }
 
-// Launch a GEMM kernel as a programmatic dependent of the preceding kernel on
-// the stream: it may start while that kernel (the prepare kernel) finishes,
+// Launch a kernel as a programmatic dependent of the preceding kernel on the
+// stream: it may start while that kernel finishes (the GEMM behind the
+// prepare kernel, the next call's prepare kernel behind a GEMM's last tiles),
 // and waits for its results at griddep_wait().  Host only.
-template <class Kernel>
+template <class Kernel, class Params>
 cudaError_t launch_dependent(Kernel kernel, int grid, uint32_t smem, cudaStream_t s,
-                             const GemmParams& gp) {
+                             const Params& gp) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(256);

@@ -48,6 +48,8 @@ __global__ void __launch_bounds__(256) mx_prepare_kernel(const __grid_constant__
   // every block is resident once it gets here: the GEMM grid behind this one
   // may launch now (it waits for this grid's results before reading them)
   griddep_launch_dependents();
+  // launched early behind the previous GEMM: touch no memory before it is done
+  griddep_wait();
   int blk = blockIdx.x;
   if (blk < p.blocks_tiles) {
     if (blk == 0 && threadIdx.x == 0) {
@@ -211,7 +213,7 @@ int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
     pp.blocks_sfx = int((int64_t(L.xblocks) * L.ksteps * 64 + 255) / 256);
     const int64_t sfw_lines = int64_t(p->num_groups) * L.nt128 * L.ksteps * 32;
     const int64_t blocks = int64_t(pp.blocks_tiles) + pp.blocks_sfx + (sfw_lines + 255) / 256;
-    mx_prepare_kernel<<<int(blocks), 256, 0, s>>>(pp);
+    FGG_CUDA_CHECK(launch_dependent(mx_prepare_kernel, int(blocks), 0, s, pp));
     FGG_CUDA_CHECK(cudaGetLastError());
   }
 

@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(256) nvfp4_prepare_kernel(const __grid_constan
   // every block is resident once it gets here: the GEMM grid behind this one
   // may launch now (it waits for this grid's results before reading them)
   griddep_launch_dependents();
+  // launched early behind the previous GEMM: touch no memory before it is done
+  griddep_wait();
   __shared__ alignas(128) CUtensorMap smap[8];
   __shared__ int32_t sbegin[FGG_MAX_GROUPS + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -430,7 +432,7 @@ int prepare_impl(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8_t
   const int64_t sf_lines = int64_t(L.xt_total) * L.nk64p * L.ch * 32;
   const int64_t blocks = int64_t(pp.blocks_tmap) + pp.blocks_tiles + (sf_lines + 255) / 256;
   if (blocks > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
-  nvfp4_prepare_kernel<<<int(blocks), 256, 0, s>>>(pp);
+  FGG_CUDA_CHECK(launch_dependent(nvfp4_prepare_kernel, int(blocks), 0, s, pp));
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }
