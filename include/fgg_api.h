@@ -119,6 +119,16 @@ FGG_API size_t fgg_nvfp4_workspace_bytes(const FggNvfp4Problem* p);
  * set). */
 FGG_API int fgg_nvfp4_grouped_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace,
                            size_t ws_bytes, void* stream);
+/* The same GEMM with the gated epilogue of a fused gate+up projection: the
+ * packed weight rows (N = 2I of them) come in 32-row chunks of 16 gate rows
+ * then the 16 up rows of the same outputs; out is bf16 [sum_g M_g, N/2] with
+ *   out[t, 16c + i] = bf16(silu(alpha_g * acc[t, 32c + i]) * alpha_g * acc[t, 32c + 16 + i]).
+ * N % 32 == 0; workspace as for fgg_nvfp4_grouped_gemm.  No counterpart in
+ * the reference operator: it is the SiLU * up epilogue of the gated expert
+ * GEMM in tasks/muse_prefill_boundary/reference/submission.py:31-33 (fused
+ * kernel) and :1096 (its self-test: silu(hh[:, :D]) * hh[:, D:]). */
+FGG_API int fgg_nvfp4_grouped_gemm_silu_mul(const FggNvfp4Problem* p, const void* pack,
+                                            void* workspace, size_t ws_bytes, void* stream);
 /* The two halves of fgg_nvfp4_grouped_gemm, for callers that replay one
  * problem (same pointers, same sizes) many times, e.g. inside a CUDA graph:
  * fgg_nvfp4_prepare fills `workspace` (descriptors, token-scale repack, tile

@@ -161,6 +161,22 @@ def grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, alpha, as_bf16: bool = Tr
     return outs
 
 
+def gated_grouped_gemm(a_list, a_sf_list, b13_list, b13_sf_list, alpha):
+    """Reference of the gated gate+up epilogue: per group, with b13 rows
+    [0, I) the gate projection and [I, 2I) the up projection,
+        hh = alpha_g * deq(A_g) @ deq(B13_g)^T          (fp32)
+        h  = bf16(silu(hh[:, :I]) * hh[:, I:])
+    (tasks/muse_prefill_boundary/reference/submission.py:1096, the reference's
+    own check of its fused SiLU * up epilogue)."""
+    import torch
+
+    outs = []
+    for c in grouped_gemm(a_list, a_sf_list, b13_list, b13_sf_list, alpha, as_bf16=False):
+        i = c.shape[1] // 2
+        outs.append((torch.nn.functional.silu(c[:, :i]) * c[:, i:]).to(torch.bfloat16))
+    return outs
+
+
 def random_problem(m_list, n: int, k: int, seed: int = 0, w_std: float = 1.0):
     """Seeded synthetic NVFP4 problem: N(0,1) activations, N(0, w_std) weights,
     each tensor quantised with its own global scale.  Returns a dict of numpy

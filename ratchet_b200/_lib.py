@@ -68,6 +68,7 @@ _SIGS = {
                                            _VOIDP, ctypes.c_int64, _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
     "fgg_moe_combine": (ctypes.c_int, [_VOIDP, ctypes.c_int64, _VOIDP, _VOIDP, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP]),
+    "fgg_nvfp4_grouped_gemm_silu_mul": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_mx_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(FggMxProblem)]),
     "fgg_mx_grouped_gemm": (ctypes.c_int, [ctypes.POINTER(FggMxProblem), _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_amax": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int64, _VOIDP, _VOIDP]),

@@ -107,7 +107,15 @@ struct GemmParams {
   int32_t ksteps;
   int32_t nt;     // weight tiles per group in the tile list (128 rows; 256 for pairs)
   int32_t nt128;  // 128-row weight tiles per group (the SF pack's unit)
+  int32_t epi;    // kEpiPlain or kEpiSiluMul (NVFP4 only)
 };
+
+// Epilogues.  kEpiPlain: out[t, n] = bf16(alpha * acc).  kEpiSiluMul: the
+// weight rows come in 32-row chunks of 16 gate rows then the 16 up rows of the
+// same outputs; out[t, 16c + i] = bf16(silu(alpha * gate) * (alpha * up)) with
+// row stride N/2.
+constexpr int32_t kEpiPlain = 0;
+constexpr int32_t kEpiSiluMul = 1;
 
 // Metadata of tile `tile` (scheduler warp, off the critical path).
 template <bool MX, int BN>
@@ -193,6 +201,29 @@ __device__ __forceinline__ void epilogue_tile(__nv_bfloat16* out, int ldn, int n
     for (int j = 0; j < 16; ++j) {
       if (c0 + j < rows)
         orow[size_t(c0 + j) * ldn] = __float2bfloat16_rn(alpha * __uint_as_float(r[j]));
+    }
+  }
+}
+
+// Gated epilogue of one tile for the calling warp (kEpiSiluMul): lanes 0-15
+// hold 16 gate rows, lanes 16-31 the up rows of the same 16 outputs; a
+// shuffle pairs them and lanes 0-15 store silu(gate) * up.  n0: the warp's
+// first weight row (a multiple of 32); out has N/2 columns.
+__device__ __forceinline__ void epilogue_tile_silu_mul(__nv_bfloat16* out, int ldn_half, int n0,
+                                                       size_t row0, int rows, int ncols,
+                                                       float alpha, uint32_t taddr) {
+  const int lane = threadIdx.x & 31;
+  __nv_bfloat16* orow = out + row0 * size_t(ldn_half) + size_t(n0 / 2 + lane);
+  for (int c0 = 0; c0 < ncols; c0 += 16) {
+    uint32_t r[16];
+    tmem_ld16(taddr + c0, r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float g = alpha * __uint_as_float(r[j]);
+      const float u = __shfl_down_sync(0xffffffffu, g, 16);
+      if (lane < 16 && c0 + j < rows)
+        orow[size_t(c0 + j) * ldn_half] = __float2bfloat16_rn(g / (1.0f + __expf(-g)) * u);
     }
   }
 }
@@ -558,8 +589,12 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
       if (!mbar_wait(accf_bar(b), (lt >> 1) & 1u, abort_flag, p.status, kStatusTimeoutEpilogue))
         break;
       tc_fence_after();
-      epilogue_tile(p.out, p.n, nti * 128 + q * 32 + lane, size_t(s.row0), s.rows, ncols,
-                    s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
+      if (p.epi == kEpiSiluMul)
+        epilogue_tile_silu_mul(p.out, p.n / 2, nti * 128 + q * 32, size_t(s.row0), s.rows, ncols,
+                               s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
+      else
+        epilogue_tile(p.out, p.n, nti * 128 + q * 32 + lane, size_t(s.row0), s.rows, ncols,
+                      s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(b));
@@ -1016,8 +1051,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       if (!mbar_wait(accf_bar(b), (lt >> 1) & 1u, abort_flag, p.status, kStatusTimeoutEpilogue))
         break;
       tc_fence_after();
-      epilogue_tile(p.out, p.n, nti * 256 + int(rank) * 128 + q * 32 + lane, size_t(s.row0),
-                    s.rows, ncols, s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
+      if (p.epi == kEpiSiluMul)
+        epilogue_tile_silu_mul(p.out, p.n / 2, nti * 256 + int(rank) * 128 + q * 32,
+                               size_t(s.row0), s.rows, ncols, s.alpha,
+                               tmem + (uint32_t(q * 32) << 16) + b * C::BN);
+      else
+        epilogue_tile(p.out, p.n, nti * 256 + int(rank) * 128 + q * 32 + lane, size_t(s.row0),
+                      s.rows, ncols, s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {

@@ -438,7 +438,7 @@ int prepare_impl(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8_t
 }
 
 int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uint8_t* ws,
-              const DeviceInfo& dev, cudaStream_t s) {
+              const DeviceInfo& dev, cudaStream_t s, int32_t epi = kEpiPlain) {
   if (L.num_tiles == 0) return FGG_OK;
   if (pack == nullptr) return set_error(FGG_EINVAL, "pack is null");
   if (!aligned16(pack)) return set_error(FGG_EALIGN, "pack must be 16-byte aligned");
@@ -460,6 +460,7 @@ int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uin
   gp.g = G;
   gp.wg = L.wg;
   gp.n = p->n;
+  gp.epi = epi;
   gp.k = p->k;
   gp.m_total = 0;
   gp.num_tiles = L.num_tiles;
@@ -528,6 +529,23 @@ int fgg_nvfp4_grouped_gemm(const FggNvfp4Problem* p, const void* pack, void* wor
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (int rc = prepare_impl(p, L, first, ws, s)) return rc;
   return gemm_impl(p, L, pack, ws, dev, s);
+}
+
+int fgg_nvfp4_grouped_gemm_silu_mul(const FggNvfp4Problem* p, const void* pack, void* workspace,
+                                    size_t ws_bytes, void* stream) {
+  WsLayout L;
+  if (int rc = plan(p, &L)) return rc;
+  if (p->n % 32 != 0)
+    return set_error(FGG_EBADSHAPE, "N=%d: gate and up rows come in chunks of 16 + 16", p->n);
+  int first = -1;
+  if (int rc = check_problem(p, L, workspace, ws_bytes, &first)) return rc;
+  if (L.num_tiles > 0 && pack == nullptr) return set_error(FGG_EINVAL, "pack is null");
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (int rc = prepare_impl(p, L, first, ws, s)) return rc;
+  return gemm_impl(p, L, pack, ws, dev, s, kEpiSiluMul);
 }
 
 }  // extern "C"

@@ -150,6 +150,69 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
                  b_index[g] (b_list then holds the weight groups, any count);
                  several problem groups may share one weight group
     """
+    return _nvfp4_grouped(a_list, a_sf_list, b_list, b_sf_list, problem_sizes, alpha, pack, out,
+                          b_index, silu_mul=False)
+
+
+def nvfp4_grouped_gemm_silu_mul(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
+                                alpha=None, *, pack: WeightPack | None = None,
+                                out: torch.Tensor | None = None, b_index=None) -> list[torch.Tensor]:
+    """Fused gate+up projection with the SiLU * up epilogue (the gated expert
+    path of tasks/muse_prefill_boundary/reference/submission.py:31-33, :1096).
+
+    b_list[g] [2I, K/2] / b_sf_list[g] [2I, K/16] hold the gate and up rows in
+    chunks of 16 gate rows followed by the 16 up rows of the same outputs
+    (interleave_gate_up builds that order from gate rows then up rows).
+    Returns per group h_g [M_g, I] bf16 with
+        h_g = silu(alpha_g * A_g B_gate^T) * (alpha_g * A_g B_up^T),
+    computed in fp32 from the accumulators and rounded once.  Everything else
+    as nvfp4_grouped_gemm; `out`, when given, is bf16 [sum M_g, I]."""
+    return _nvfp4_grouped(a_list, a_sf_list, b_list, b_sf_list, problem_sizes, alpha, pack, out,
+                          b_index, silu_mul=True)
+
+
+def interleave_gate_up(w13: torch.Tensor, w13_sf: torch.Tensor):
+    """Rows [0, I) gate, [I, 2I) up -> the row order of the silu_mul epilogue:
+    for each c, gate rows 16c..16c+15 then up rows I+16c..I+16c+15.  Works on
+    the codes [2I, K/2] and the scales [2I, K/16] alike (a row permutation)."""
+    rows = int(w13.shape[0])
+    if rows % 32 != 0 or int(w13_sf.shape[0]) != rows:
+        raise ValueError(f"gate+up weights need 2I rows with I % 16 == 0, got {rows}")
+    half = rows // 2
+    c = torch.arange(half // 16, device=w13.device).view(-1, 1)
+    i = torch.arange(16, device=w13.device).view(1, -1)
+    perm = torch.cat([16 * c + i, half + 16 * c + i], dim=1).reshape(-1)
+    # as bytes: index_select has no kernels for the fp8 / fp4 dtypes
+    return tuple(t.view(torch.uint8).index_select(0, perm).view(t.dtype) for t in (w13, w13_sf))
+
+
+def nvfp4_expert_mlp(a_list, a_sf_list, alpha13, w13_list, w13_sf_list, w2_list, w2_sf_list,
+                     w2_scale, *, pack13: WeightPack | None = None,
+                     pack2: WeightPack | None = None):
+    """Per group g, the gated expert MLP on NVFP4 operands:
+        h_g = silu(alpha13_g A_g W13_gate^T) * (alpha13_g A_g W13_up^T)   (bf16)
+        h -> NVFP4 (one decode scale s_h over all groups' rows)
+        y_g = (s_h * w2_scale_g) * deq(h_g) @ deq(W2_g)^T                 (bf16)
+    w13_list[g] in the interleave_gate_up row order ([2I, K/2]); w2_list[g]
+    [H, I/2]; w2_scale: G fp32 decode scales of W2.  Three launches after the
+    gate+up GEMM: amax, quantise, down GEMM.  Returns (y_list, h) with h the
+    bf16 [sum M_g, I] intermediate."""
+    ms = [int(a.shape[0]) for a in a_list]
+    inter = int(w13_list[0].shape[0]) // 2
+    h = torch.empty((sum(ms), inter), dtype=torch.bfloat16, device=w13_list[0].device)
+    nvfp4_grouped_gemm_silu_mul(a_list, a_sf_list, w13_list, w13_sf_list, alpha=alpha13,
+                                pack=pack13, out=h)
+    hc, hs, hg = quantize_nvfp4(h)
+    h_codes = list(hc.split(ms))
+    h_sf = list(hs.split(ms))
+    w2s = torch.as_tensor(w2_scale, dtype=torch.float32, device=h.device).reshape(-1)
+    y = nvfp4_grouped_gemm(h_codes, h_sf, w2_list, w2_sf_list, alpha=(hg * w2s).contiguous(),
+                           pack=pack2)
+    return y, h
+
+
+def _nvfp4_grouped(a_list, a_sf_list, b_list, b_sf_list, problem_sizes, alpha, pack, out,
+                   b_index, silu_mul: bool) -> list[torch.Tensor]:
     global _last_ws
     G = len(a_list)
     if G == 0 or G != len(a_sf_list) or len(b_list) != len(b_sf_list) or not b_list:
@@ -208,11 +271,14 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
     if alpha_t.numel() != G:
         raise ValueError(f"alpha has {alpha_t.numel()} entries for {G} groups")
     total = sum(ms)
+    n_out = n // 2 if silu_mul else n
+    if silu_mul and n % 32 != 0:
+        raise ValueError(f"N={n}: gate and up rows come in chunks of 16 + 16")
     if out is None:
-        out = torch.empty((total, n), dtype=torch.bfloat16, device=dev)
-    elif (out.dtype != torch.bfloat16 or out.shape != (total, n) or not out.is_contiguous()
+        out = torch.empty((total, n_out), dtype=torch.bfloat16, device=dev)
+    elif (out.dtype != torch.bfloat16 or out.shape != (total, n_out) or not out.is_contiguous()
           or out.device != dev):
-        raise ValueError(f"out must be a contiguous bf16 [{total}, {n}] tensor on {dev}")
+        raise ValueError(f"out must be a contiguous bf16 [{total}, {n_out}] tensor on {dev}")
     L = _lib.lib()
     m_arr = np.asarray(ms, dtype=np.int32)
     prob = _lib.FggNvfp4Problem(G, n, k, m_arr.ctypes.data, pa.ctypes.data, psf.ctypes.data,
@@ -222,9 +288,10 @@ def nvfp4_grouped_gemm(a_list, a_sf_list, b_list, b_sf_list, problem_sizes=None,
     if nbytes == 0:
         _lib.check(L.fgg_nvfp4_grouped_gemm(prob, None, None, 0, None), "nvfp4_grouped_gemm")
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    entry = L.fgg_nvfp4_grouped_gemm_silu_mul if silu_mul else L.fgg_nvfp4_grouped_gemm
     with torch.cuda.device(dev):
-        _lib.check(L.fgg_nvfp4_grouped_gemm(prob, pack.buf.data_ptr(), ws.data_ptr(), nbytes,
-                                            _stream_ptr(dev)), "nvfp4_grouped_gemm")
+        _lib.check(entry(prob, pack.buf.data_ptr(), ws.data_ptr(), nbytes, _stream_ptr(dev)),
+                   "nvfp4_grouped_gemm")
     _last_ws = ws
     return list(out.split(ms, dim=0))
 

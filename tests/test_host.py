@@ -103,3 +103,20 @@ def test_problem_sizes_checked_against_tensors():
     with pytest.raises(ValueError, match=r"group 0: a \(3, 32\)"):
         rb.nvfp4_grouped_gemm([torch.zeros((3, 32), dtype=torch.uint8), a[1], a[2]], sf, b, b,
                               pack=fake)
+
+
+def test_interleave_gate_up_order():
+    """Rows come out as 16 gate rows, then the 16 up rows of the same outputs."""
+    inter, k2 = 48, 4
+    w = torch.arange(2 * inter, dtype=torch.uint8).view(-1, 1).repeat(1, k2)
+    sf = w[:, :2].clone().view(torch.float8_e4m3fn)
+    wi, sfi = rb.interleave_gate_up(w, sf)
+    rows = wi[:, 0].tolist()
+    want = []
+    for c in range(inter // 16):
+        want += list(range(16 * c, 16 * c + 16)) + list(range(inter + 16 * c, inter + 16 * c + 16))
+    assert rows == want
+    assert sfi.dtype == torch.float8_e4m3fn
+    assert sfi.view(torch.uint8)[:, 0].tolist() == want
+    with pytest.raises(ValueError):
+        rb.interleave_gate_up(w[:40], sf[:40])
