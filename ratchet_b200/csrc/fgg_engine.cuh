@@ -228,11 +228,14 @@ __device__ __forceinline__ void epilogue_tile_silu_mul(__nv_bfloat16* out, int l
   }
 }
 
-template <bool MX_, int BN_, int STAGES_>
+template <bool MX_, int BN_, int STAGES_, int KSUB_ = 1>
 struct EngineCfg {
   static constexpr bool MX = MX_;
   static constexpr int BN = BN_;
   static constexpr int STAGES = STAGES_;
+  // K steps per pipeline stage (one barrier wait and one commit per stage)
+  static constexpr int KSUB = KSUB_;
+  static_assert(KSUB == 1 || KSUB == 2, "one or two K steps per stage");
   static constexpr int CH = (BN + 127) / 128;  // 128-row SF atoms per token tile
   // K elements per pipeline stage: one 128-byte swizzle row of each operand.
   static constexpr int K_STEP = MX ? 128 : 256;
@@ -248,8 +251,10 @@ struct EngineCfg {
   static constexpr uint32_t SFX_UNIT = SFX_REP ? 4096 : CH * 512;
   static constexpr uint32_t SFX_BYTES = MX ? SFX_UNIT : 4 * SFX_UNIT;
   static constexpr uint32_t TX_BYTES = W_TX + X_BYTES + SFW_BYTES + SFX_BYTES;
-  static constexpr uint32_t STAGE_BYTES =
+  // bytes of one K step's tiles; a stage holds KSUB of them
+  static constexpr uint32_t SUB_BYTES =
       (W_BYTES + X_BYTES + SFW_BYTES + SFX_BYTES + 1023) / 1024 * 1024;
+  static constexpr uint32_t STAGE_BYTES = KSUB * SUB_BYTES;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "BN must be a multiple of 16");
   static_assert((W_BYTES + X_BYTES) % 1024 == 0, "operand tiles must stay 1024 B aligned");
   // TMEM columns: two accumulators of BN fp32 columns, then a ring of scale
@@ -301,11 +306,12 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  auto sW = [&](int s) { return base + s * C::STAGE_BYTES; };
-  auto sX = [&](int s) { return base + s * C::STAGE_BYTES + C::W_BYTES; };
-  auto sSFW = [&](int s) { return base + s * C::STAGE_BYTES + C::W_BYTES + C::X_BYTES; };
-  auto sSFX = [&](int s) {
-    return base + s * C::STAGE_BYTES + C::W_BYTES + C::X_BYTES + C::SFW_BYTES;
+  // tiles of K-step slot q = stage * KSUB + (K step within the stage)
+  auto sW = [&](int q) { return base + q * C::SUB_BYTES; };
+  auto sX = [&](int q) { return base + q * C::SUB_BYTES + C::W_BYTES; };
+  auto sSFW = [&](int q) { return base + q * C::SUB_BYTES + C::W_BYTES + C::X_BYTES; };
+  auto sSFX = [&](int q) {
+    return base + q * C::SUB_BYTES + C::W_BYTES + C::X_BYTES + C::SFW_BYTES;
   };
 
   if (threadIdx.x == 0) {
@@ -433,23 +439,34 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
         const uint8_t* sfw =
             p.sfw + (size_t(s.wgroup) * p.nt + nti) * size_t(p.ksteps) * C::SFW_BYTES;
         bool ok = true;
-        for (int ks = 0; ks < p.ksteps; ++ks) {
+        for (int ks0 = 0; ks0 < p.ksteps; ks0 += C::KSUB) {
           if (!mbar_wait1(empty_bar(stage), phase ^ 1, abort_flag, p.status,
                           kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
           const uint32_t fb = full_bar(stage);
-          mbar_arrive_expect_tx(fb, C::TX_BYTES);
-          if constexpr (C::MX) {
-            tma_load_3d(sW(stage), tw, fb, ks * C::K_STEP, nti * 128, g);
-            tma_load_2d(sX(stage), tx, fb, ks * C::K_STEP, xti * C::BN);
-          } else {
-            tma_load_2d(sW(stage), tw, fb, ks * 128, nti * 128);
-            tma_load_2d(sX(stage), tx, fb, ks * 128, xti * C::BN);
+          if constexpr (C::KSUB == 1)
+            mbar_arrive_expect_tx(fb, C::TX_BYTES);
+          else
+            mbar_arrive_expect_tx(fb, C::TX_BYTES * uint32_t(min(C::KSUB, p.ksteps - ks0)));
+#pragma unroll
+          for (int sub = 0; sub < C::KSUB; ++sub) {
+            const int ks = ks0 + sub;
+            if constexpr (C::KSUB > 1) {
+              if (ks >= p.ksteps) break;
+            }
+            const int q = stage * C::KSUB + sub;
+            if constexpr (C::MX) {
+              tma_load_3d(sW(q), tw, fb, ks * C::K_STEP, nti * 128, g);
+              tma_load_2d(sX(q), tx, fb, ks * C::K_STEP, xti * C::BN);
+            } else {
+              tma_load_2d(sW(q), tw, fb, ks * 128, nti * 128);
+              tma_load_2d(sX(q), tx, fb, ks * 128, xti * C::BN);
+            }
+            bulk_g2s(sSFW(q), sfw + size_t(ks) * C::SFW_BYTES, C::SFW_BYTES, fb);
+            bulk_g2s(sSFX(q), sfx + size_t(ks) * C::SFX_BYTES, C::SFX_BYTES, fb);
           }
-          bulk_g2s(sSFW(stage), sfw + size_t(ks) * C::SFW_BYTES, C::SFW_BYTES, fb);
-          bulk_g2s(sSFX(stage), sfx + size_t(ks) * C::SFX_BYTES, C::SFX_BYTES, fb);
           ++arms;
           if (++stage == C::STAGES) {
             stage = 0;
@@ -496,52 +513,60 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
         const uint32_t d_tmem = tmem + b * C::BN;
         const uint32_t idesc =
             C::MX ? 0u : idesc_block_scaled(kFmtNvf4E2M1, kFmtNvf4E2M1, 0, 128, ncols, 0, 0);
-        for (int ks = 0; ks < p.ksteps; ++ks) {
+        for (int ks0 = 0; ks0 < p.ksteps; ks0 += C::KSUB) {
           if (!mbar_wait1(full_bar(stage), phase, abort_flag, p.status, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = desc_k_sw128(sW(stage));
-          const uint64_t bdesc = desc_k_sw128(sX(stage));
-          if constexpr (C::MX) {
-            const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-            tc_cp_sf(tmem + col, desc_sf_atom(sSFW(stage)));
-            if constexpr (C::SFX_REP) {
-              tc_cp_sf2(tmem + col + 4, desc_sf_pair_rep(sSFX(stage)));
-            } else {
 #pragma unroll
-              for (int c = 0; c < C::CH; ++c)
-                tc_cp_sf(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(stage) + c * 512));
+          for (int sub = 0; sub < C::KSUB; ++sub) {
+            const int ks = ks0 + sub;
+            if constexpr (C::KSUB > 1) {
+              if (ks >= p.ksteps) break;
             }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              // K step of 32 one-byte elements = 32 bytes = +2 in the start field;
-              // SF id j picks byte j of every scale column.
-              const uint32_t idj =
-                  idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 128, ncols, j, j);
-              tc_mma_mxf8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
-                              (tmem + col) | (uint32_t(j) << 30),
-                              (tmem + col + 4) | (uint32_t(j) << 30), (ks | j) != 0 ? 1u : 0u);
-            }
-            sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            const int q = stage * C::KSUB + sub;  // this K step's slot in the stage
+            const uint64_t adesc = desc_k_sw128(sW(q));
+            const uint64_t bdesc = desc_k_sw128(sX(q));
+            if constexpr (C::MX) {
               const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-              tc_cp_sf(tmem + col, desc_sf_atom(sSFW(stage) + j * 512));
+              tc_cp_sf(tmem + col, desc_sf_atom(sSFW(q)));
               if constexpr (C::SFX_REP) {
-                tc_cp_sf2(tmem + col + 4, desc_sf_pair_rep(sSFX(stage) + j * C::SFX_UNIT));
+                tc_cp_sf2(tmem + col + 4, desc_sf_pair_rep(sSFX(q)));
               } else {
 #pragma unroll
                 for (int c = 0; c < C::CH; ++c)
-                  tc_cp_sf(tmem + col + 4 + 4 * c,
-                           desc_sf_atom(sSFX(stage) + (j * C::CH + c) * 512));
+                  tc_cp_sf(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(q) + c * 512));
               }
-              // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
-              tc_mma_nvf4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col,
-                          tmem + col + 4, (ks | j) != 0 ? 1u : 0u);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                // K step of 32 one-byte elements = 32 bytes = +2 in the start field;
+                // SF id j picks byte j of every scale column.
+                const uint32_t idj =
+                    idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 128, ncols, j, j);
+                tc_mma_mxf8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
+                                (tmem + col) | (uint32_t(j) << 30),
+                                (tmem + col + 4) | (uint32_t(j) << 30), (ks | j) != 0 ? 1u : 0u);
+              }
               sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
+                tc_cp_sf(tmem + col, desc_sf_atom(sSFW(q) + j * 512));
+                if constexpr (C::SFX_REP) {
+                  tc_cp_sf2(tmem + col + 4, desc_sf_pair_rep(sSFX(q) + j * C::SFX_UNIT));
+                } else {
+#pragma unroll
+                  for (int c = 0; c < C::CH; ++c)
+                    tc_cp_sf(tmem + col + 4 + 4 * c,
+                             desc_sf_atom(sSFX(q) + (j * C::CH + c) * 512));
+                }
+                // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
+                tc_mma_nvf4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col,
+                            tmem + col + 4, (ks | j) != 0 ? 1u : 0u);
+                sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+              }
             }
           }
           tc_commit(empty_bar(stage));

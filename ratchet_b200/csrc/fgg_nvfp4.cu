@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(256) nvfp4_pack_weights_kernel(const __grid_co
 
 // ------------------------------------------------------------ host side
 using CfgPrefill = EngineCfg<false, 224, 3>;   // one CTA per tile (N % 256 != 0)
-using CfgDecode = EngineCfg<false, 16, 8>;     // every group has M <= 16
+using CfgDecode = EngineCfg<false, 16, 4, 2>;  // every group has M <= 16; 2 K steps per stage
 using CfgPair = PairCfg<false, 4>;             // CTA pairs, 256 x 224 tiles
 
 struct PackLayout {
