@@ -244,11 +244,13 @@ struct EngineCfg {
   static constexpr uint32_t X_BYTES = BN * 128;
   // NVFP4: 4 atoms (one per K64 MMA); MX: one atom covers the 4 K32 MMAs.
   static constexpr uint32_t SFW_BYTES = MX ? 512 : 4 * 512;
-  // Token scales of one scale slot: with two atoms (224-token tiles) they come
-  // in the replicated 4 KB layout that one 128x256b copy uploads; one atom
-  // (decode tiles) stays a plain 512-byte atom.
+  // Token scales.  Two atoms per MMA (224-token tiles): the replicated 4 KB
+  // layout that one 128x256b copy uploads, per MMA.  One atom per MMA
+  // (16-token decode tiles, NVFP4): the atoms of MMAs (0, 1) and (2, 3) in
+  // that layout, one copy per MMA pair (SFX_PAIR).
   static constexpr bool SFX_REP = (CH == 2);
-  static constexpr uint32_t SFX_UNIT = SFX_REP ? 4096 : CH * 512;
+  static constexpr bool SFX_PAIR = (CH == 1 && !MX);
+  static constexpr uint32_t SFX_UNIT = SFX_REP ? 4096 : SFX_PAIR ? 2048 : CH * 512;
   static constexpr uint32_t SFX_BYTES = MX ? SFX_UNIT : 4 * SFX_UNIT;
   static constexpr uint32_t TX_BYTES = W_TX + X_BYTES + SFW_BYTES + SFX_BYTES;
   // bytes of one K step's tiles; a stage holds KSUB of them
@@ -259,9 +261,10 @@ struct EngineCfg {
   static_assert((W_BYTES + X_BYTES) % 1024 == 0, "operand tiles must stay 1024 B aligned");
   // TMEM columns: two accumulators of BN fp32 columns, then a ring of scale
   // slots (4 columns of weight scales + 4 per token atom).  NVFP4 takes one
-  // slot per MMA, MX one per K step.
+  // slot per MMA, MX one per K step; with SFX_PAIR one slot per MMA pair,
+  // [weights a 4 | weights b 4 | tokens a 4 | tokens b 4].
   static constexpr int SF_BASE = ((2 * BN + 3) / 4) * 4;
-  static constexpr int SF_SLOT = 4 + 4 * CH;
+  static constexpr int SF_SLOT = SFX_PAIR ? 16 : 4 + 4 * CH;
   static constexpr int NSLOTS_FIT = (512 - SF_BASE) / SF_SLOT;
   static constexpr int NSLOTS = NSLOTS_FIT > 8 ? 8 : NSLOTS_FIT;
   static_assert(NSLOTS >= 2, "not enough TMEM for the scale ring");
@@ -549,6 +552,21 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
                                 (tmem + col + 4) | (uint32_t(j) << 30), (ks | j) != 0 ? 1u : 0u);
               }
               sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+            } else if constexpr (C::SFX_PAIR) {
+#pragma unroll
+              for (int pp = 0; pp < 2; ++pp) {  // MMAs (2pp, 2pp+1): one token-scale upload
+                const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
+                tc_cp_sf2(tmem + col + 8, desc_sf_pair_rep(sSFX(q) + pp * 4096));
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int j = 2 * pp + h;
+                  tc_cp_sf(tmem + col + 4 * h, desc_sf_atom(sSFW(q) + j * 512));
+                  // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
+                  tc_mma_nvf4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col + 4 * h,
+                              tmem + col + 8 + 4 * h, (ks | j) != 0 ? 1u : 0u);
+                }
+                sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+              }
             } else {
 #pragma unroll
               for (int j = 0; j < 4; ++j) {

@@ -124,15 +124,18 @@ __global__ void __launch_bounds__(256) nvfp4_prepare_kernel(const __grid_constan
       v[r1] = __ldg(reinterpret_cast<const uint32_t*>(p.a_sf[g] + size_t(row) * kq + 4 * j));
   }
   const uint4 line16 = make_uint4(v[0], v[1], v[2], v[3]);
-  if (p.ch == 2) {
+  if (p.ch == 1) {
+    // 16-token tiles: the atoms of MMAs (2i, 2i+1) in one replicated block
+    uint8_t* blk4k = p.sfx_out + (size_t(X) * p.nk64p + (j & ~1)) * 2048u;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(blk4k + sf_rep_offset(j & 1, r0, q)) = line16;
+  } else {
     // 224-token tiles: the replicated block one 128x256b copy uploads
     uint8_t* blk4k = p.sfx_out + (size_t(X) * p.nk64p + j) * 4096u;
 #pragma unroll
     for (int q = 0; q < 4; ++q)
       *reinterpret_cast<uint4*>(blk4k + sf_rep_offset(c, r0, q)) = line16;
-  } else {
-    *reinterpret_cast<uint4*>(p.sfx_out + (size_t(X) * p.nk64p + j) * (p.ch * 512u) +
-                              size_t(r0) * 16u) = line16;
   }
 }
 
@@ -288,9 +291,10 @@ static int plan(const FggNvfp4Problem* p, WsLayout* L) {
   L->tmaps = cv.take(size_t(G) * sizeof(CUtensorMap), 128);
   L->ginfo = cv.take(size_t(G) * sizeof(GroupInfo), 256);
   L->tiles = cv.take(size_t(std::max<int64_t>(tiles, 1)) * 4, 256);
-  // token scales per (token tile, MMA): two atoms in the 4 KB replicated layout
-  // of one 128x256b copy, or one plain 512-byte atom for 16-token tiles
-  L->sfx = cv.take(size_t(std::max<int64_t>(xts, 1)) * L->nk64p * (L->ch == 2 ? 4096 : 512), 256);
+  // token scales per (token tile, MMA) in the replicated layout of a 128x256b
+  // copy: two atoms per MMA (4 KB), or for 16-token tiles the atoms of two
+  // MMAs per 4 KB block (2 KB per MMA)
+  L->sfx = cv.take(size_t(std::max<int64_t>(xts, 1)) * L->nk64p * (L->ch == 2 ? 4096 : 2048), 256);
   L->total = cv.off;
   return FGG_OK;
 }

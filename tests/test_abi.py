@@ -92,7 +92,9 @@ def _ws_bytes_py(ms, n, k):
     take(len(ms) * 128, 128)
     take(len(ms) * 16, 256)
     take(max(tiles, 1) * 4, 256)
-    take(max(xts, 1) * nk64p * (4096 if ch == 2 else 512), 256)  # 224-token tiles: replicated
+    # token scales, replicated for 128x256b copies: 4 KB per MMA (224-token
+    # tiles, two atoms) or 4 KB per two MMAs (16-token tiles)
+    take(max(xts, 1) * nk64p * (4096 if ch == 2 else 2048), 256)
     return off
 
 
