@@ -57,6 +57,12 @@ def workload(name: str, seed: int = 0) -> dict:
                     "(Zipf s=1.1, seed 0), N=4096 (gate+up), K=7168, expert-parallel",
                     m=[4096 * 8], n=4096, k=7168, w_std=1.0, bound="tensor",
                     tokens=4096, experts=64, topk=8)
+    if name == "mlp":
+        ms = [int(v) for v in rng.integers(64, 1025, size=8)]
+        return dict(name="mlp", desc="gated expert MLP, 8 experts, M_g~U[64,1024] seed 0: "
+                    "gate+up N=4096 (I=2048) K=7168 with the SiLU*up epilogue, NVFP4 "
+                    "quantisation of the intermediate, down N=7168 K=2048",
+                    m=ms, n=2 * 2048, k=7168, inter=2048, w_std=1.0, bound="tensor")
     if name == "decode":
         ms = [int(v) for v in rng.integers(1, 17, size=256)]
         return dict(name="decode", desc="256 groups, M_g~U[1,16] seed 0, N=7168, K=2048",
@@ -65,6 +71,8 @@ def workload(name: str, seed: int = 0) -> dict:
 
 
 def flops(wl) -> float:
+    if wl["name"] == "mlp":  # gate+up GEMM, then the down projection
+        return 2.0 * sum(wl["m"]) * (wl["n"] * wl["k"] + wl["k"] * wl["inter"])
     return 2.0 * sum(wl["m"]) * wl["n"] * wl["k"]
 
 
@@ -660,22 +668,111 @@ def run_moe(args, wl):
 
 
 
+def run_mlp(args, wl):
+    """The gated expert MLP (nvfp4_expert_mlp) on one GPU, or as independent
+    replicas under torchrun.  A step = gate+up grouped GEMM with the SiLU*up
+    epilogue, amax + NVFP4 quantisation of the intermediate, down grouped
+    GEMM: the whole call is timed (it is the kernel time too)."""
+    ws, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import ratchet_b200 as rb
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 * rank + 5)
+    hid, inter = wl["k"], wl["inter"]
+    A, ASF, a13, W13, W13SF, W2, W2SF, w2g = [], [], [], [], [], [], [], []
+    for m in wl["m"]:
+        qa, sa, ga = rb.quantize_nvfp4(torch.randn((m, hid), generator=gen, device=dev))
+        q13, s13, g13 = rb.quantize_nvfp4(torch.randn((2 * inter, hid), generator=gen, device=dev))
+        q13, s13 = rb.interleave_gate_up(q13, s13)
+        q2, s2, g2 = rb.quantize_nvfp4(torch.randn((hid, inter), generator=gen, device=dev))
+        A.append(qa)
+        ASF.append(sa)
+        a13.append(ga * g13)
+        W13.append(q13)
+        W13SF.append(s13)
+        W2.append(q2)
+        W2SF.append(s2)
+        w2g.append(g2)
+    alpha13 = torch.stack(a13).float()
+    w2s = torch.stack(w2g).float()
+    call = lambda: rb.nvfp4_expert_mlp(A, ASF, alpha13, W13, W13SF, W2, W2SF, w2s)
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    rb.last_status()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws, dev)
+    fl = flops(wl)
+    value = fl * ws / (ms * 1e-3) / 1e12
+    pk = peaks()
+    achieved = fl / (ms * 1e-3) / 1e12
+    peak = 4.0 * pk["bf16"]
+    wbytes = sum(t.numel() for t in W13 + W13SF + W2 + W2SF)
+    if rank == 0:
+        line = {
+            "metric": "grouped-GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "nvfp4 (e2m1 x e2m1, e4m3/16 scales, fp32 acc, bf16 out)",
+            "data": "synthetic (seeded N(0,1) activations and weights, NVFP4-quantised)",
+            "config": {"workload": wl["desc"], "groups": len(wl["m"]), "sum_m": sum(wl["m"]),
+                       "hidden": hid, "inter": inter, "parallelism": f"replicas x{ws}",
+                       "l2": f"expert weights {wbytes / 1e6:.0f} MB read every step (> L2)"},
+            "clocks": clocks,
+            "e2e": None,
+            "gpu_launches": 6 * args.steps,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                         "peak_basis": f"4 x {pk['src']} dense bf16 ({pk['bf16']:.0f} TF/s)",
+                         "kernel_ms": ms,
+                         "kernel": "whole call: two prepare + two GEMM kernels, amax, quantise"},
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["grouped", "dense", "decode", "moe"], default="grouped")
+    ap.add_argument("--config", choices=["grouped", "dense", "decode", "moe", "mlp"],
+                    default="grouped")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = workload(args.config)
+    if args.impl == "reference" and wl["name"] == "mlp":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference operator has no "
+                          "gated expert MLP; its CPU arm covers the GEMM configs"}))
+        return 0
     if args.impl == "reference":
         return run_reference(args, wl)
     if wl["name"] == "moe":
         return run_moe(args, wl)
+    if wl["name"] == "mlp":
+        return run_mlp(args, wl)
     return run_ours(args, wl)
 
 

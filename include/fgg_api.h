@@ -253,9 +253,12 @@ FGG_API int fgg_amax(const void* x, int32_t x_dtype, int64_t count, float* amax_
  *   s    = e4m3_rn_satfinite((blockmax / 6) * gs)    per 16 elements
  *   q    = e2m1_rne(x * (gs / float(s)))             (0 where s == 0)
  * codes [rows, k/2] uint8 (element 2j in the low nibble), sf [rows, k/16] E4M3.
- * `amax` is a device fp32 scalar (from fgg_amax or supplied by the caller). */
+ * `amax` is a device fp32 scalar (from fgg_amax or supplied by the caller).
+ * decode_scale: optional device fp32 scalar that receives g = 1 / gs (the
+ * per-tensor decode scale, x ~ e2m1 * e4m3 * g); NULL to skip. */
 FGG_API int fgg_nvfp4_quantize(const void* x, int32_t x_dtype, int64_t rows, int32_t k,
-                       const float* amax, void* codes, void* sf, void* stream);
+                               const float* amax, void* codes, void* sf, float* decode_scale,
+                               void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Status                                                                    */

@@ -72,7 +72,7 @@ _SIGS = {
     "fgg_mx_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(FggMxProblem)]),
     "fgg_mx_grouped_gemm": (ctypes.c_int, [ctypes.POINTER(FggMxProblem), _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_amax": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int64, _VOIDP, _VOIDP]),
-    "fgg_nvfp4_quantize": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
+    "fgg_nvfp4_quantize": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
     "fgg_read_device_status": (ctypes.c_int, [_VOIDP, _VOIDP]),
 }
 

@@ -206,24 +206,37 @@ __device__ __forceinline__ void epilogue_tile(__nv_bfloat16* out, int ldn, int n
 }
 
 // Gated epilogue of one tile for the calling warp (kEpiSiluMul): lanes 0-15
-// hold 16 gate rows, lanes 16-31 the up rows of the same 16 outputs; a
-// shuffle pairs them and lanes 0-15 store silu(gate) * up.  n0: the warp's
+// hold 16 gate rows, lanes 16-31 the up rows of the same 16 outputs.  Two
+// token columns at a time: one shuffle across the half-warps gives lanes 0-15
+// the up values of column j and lanes 16-31 the gate values of column j + 1,
+// so every lane computes one silu(gate) * up (silu(x) = x * sigmoid(x),
+// sigmoid(x) = (1 + tanh(x / 2)) / 2 on the hardware tanh).  n0: the warp's
 // first weight row (a multiple of 32); out has N/2 columns.
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void epilogue_tile_silu_mul(__nv_bfloat16* out, int ldn_half, int n0,
                                                        size_t row0, int rows, int ncols,
                                                        float alpha, uint32_t taddr) {
   const int lane = threadIdx.x & 31;
-  __nv_bfloat16* orow = out + row0 * size_t(ldn_half) + size_t(n0 / 2 + lane);
+  const bool gate_half = lane < 16;
+  __nv_bfloat16* ocol = out + row0 * size_t(ldn_half) + size_t(n0 / 2 + (lane & 15));
   for (int c0 = 0; c0 < ncols; c0 += 16) {
     uint32_t r[16];
     tmem_ld16(taddr + c0, r);
     tmem_wait_ld();
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float g = alpha * __uint_as_float(r[j]);
-      const float u = __shfl_down_sync(0xffffffffu, g, 16);
-      if (lane < 16 && c0 + j < rows)
-        orow[size_t(c0 + j) * ldn_half] = __float2bfloat16_rn(g / (1.0f + __expf(-g)) * u);
+    for (int j = 0; j < 16; j += 2) {
+      const float v0 = alpha * __uint_as_float(r[j]);
+      const float v1 = alpha * __uint_as_float(r[j + 1]);
+      const float got = __shfl_xor_sync(0xffffffffu, gate_half ? v1 : v0, 16);
+      const float g = gate_half ? v0 : got;
+      const float u = gate_half ? got : v1;
+      const float h = g * fmaf(0.5f, tanh_approx(0.5f * g), 0.5f) * u;
+      const int t = c0 + j + (gate_half ? 0 : 1);
+      if (t < rows) ocol[size_t(t) * ldn_half] = __float2bfloat16_rn(h);
     }
   }
 }

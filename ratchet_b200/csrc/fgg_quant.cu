@@ -78,13 +78,17 @@ __device__ __forceinline__ uint32_t e2m1_code(float y) {
 }
 
 // One thread per 16-element block: 8 code bytes + 1 scale byte.
+// Thread 0 also writes the decode scale g = 1 / gs when asked (decode_scale
+// non-null), so the caller needs no host-side arithmetic on amax.
 template <typename T>
 __global__ void nvfp4_quant_kernel(const T* __restrict__ x, int64_t blocks, const float* amax_p,
-                                   uint8_t* __restrict__ codes, uint8_t* __restrict__ sf) {
+                                   uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
+                                   float* __restrict__ decode_scale) {
   const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (b >= blocks) return;
   const float amax = *amax_p;
   const float gs = amax > 0.0f ? 2688.0f / amax : 1.0f;
+  if (b == 0 && decode_scale != nullptr) *decode_scale = __fdiv_rn(1.0f, gs);
+  if (b >= blocks) return;
   float v[16];
   float bmax = 0.0f;
 #pragma unroll
@@ -113,7 +117,8 @@ using namespace fgg;
 extern "C" {
 
 int fgg_amax(const void* x, int32_t x_dtype, int64_t count, float* amax_out, void* stream) {
-  if (x == nullptr || amax_out == nullptr) return set_error(FGG_EINVAL, "null pointer");
+  if (amax_out == nullptr || (x == nullptr && count > 0))
+    return set_error(FGG_EINVAL, "null pointer");
   if (count < 0) return set_error(FGG_EINVAL, "negative count");
   if (x_dtype != 0 && x_dtype != 1) return set_error(FGG_EINVAL, "x_dtype must be 0 or 1");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -133,27 +138,28 @@ int fgg_amax(const void* x, int32_t x_dtype, int64_t count, float* amax_out, voi
 }
 
 int fgg_nvfp4_quantize(const void* x, int32_t x_dtype, int64_t rows, int32_t k, const float* amax,
-                       void* codes, void* sf, void* stream) {
-  if (x == nullptr || amax == nullptr || codes == nullptr || sf == nullptr)
-    return set_error(FGG_EINVAL, "null pointer");
+                       void* codes, void* sf, float* decode_scale, void* stream) {
   if (x_dtype != 0 && x_dtype != 1) return set_error(FGG_EINVAL, "x_dtype must be 0 or 1");
   if (rows < 0 || k <= 0 || k % 16 != 0)
     return set_error(FGG_EBADSHAPE, "need rows >= 0 and k a positive multiple of 16 (k=%d)", k);
+  // an empty tensor may come with null data pointers; amax is always read
+  if (amax == nullptr || (rows > 0 && (x == nullptr || codes == nullptr || sf == nullptr)))
+    return set_error(FGG_EINVAL, "null pointer");
   if ((reinterpret_cast<uintptr_t>(codes) & 7u) != 0)
     return set_error(FGG_EALIGN, "codes must be 8-byte aligned");
   const int64_t blocks = rows * (k / 16);
-  if (blocks == 0) return FGG_OK;
+  if (blocks == 0 && decode_scale == nullptr) return FGG_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int64_t grid = (blocks + 255) / 256;
+  const int64_t grid = blocks > 0 ? (blocks + 255) / 256 : 1;
   if (grid > INT32_MAX) return set_error(FGG_EBADSHAPE, "tensor too large");
   if (x_dtype == 0)
     nvfp4_quant_kernel<float><<<int(grid), 256, 0, s>>>(
         static_cast<const float*>(x), blocks, amax, static_cast<uint8_t*>(codes),
-        static_cast<uint8_t*>(sf));
+        static_cast<uint8_t*>(sf), decode_scale);
   else
     nvfp4_quant_kernel<__nv_bfloat16><<<int(grid), 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(x), blocks, amax, static_cast<uint8_t*>(codes),
-        static_cast<uint8_t*>(sf));
+        static_cast<uint8_t*>(sf), decode_scale);
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }

@@ -378,11 +378,10 @@ def quantize_nvfp4(x: torch.Tensor, amax: torch.Tensor | None = None):
             amax_t = amax.to(device=dev, dtype=torch.float32).reshape(()).contiguous()
         codes = torch.empty((rows, k // 2), dtype=torch.uint8, device=dev)
         sf = torch.empty((rows, k // 16), dtype=torch.uint8, device=dev)
+        g = torch.empty((), dtype=torch.float32, device=dev)  # written by the kernel
         _lib.check(L.fgg_nvfp4_quantize(x.data_ptr(), dt, rows, k, amax_t.data_ptr(),
-                                        codes.data_ptr(), sf.data_ptr(), s), "fgg_nvfp4_quantize")
-    gs = torch.where(amax_t > 0, torch.tensor(2688.0, device=dev) / amax_t,
-                     torch.ones((), device=dev))
-    g = torch.ones((), device=dev) / gs
+                                        codes.data_ptr(), sf.data_ptr(), g.data_ptr(), s),
+                   "fgg_nvfp4_quantize")
     return codes, sf.view(torch.float8_e4m3fn), g
 
 

@@ -143,7 +143,7 @@ def test_mx_shape_rules_follow_reference(L):
 
 
 def test_quantize_rejects_bad_k(L):
-    assert L.fgg_nvfp4_quantize(1, 0, 4, 24, 1, 8, 1, None) == _lib.FGG_EBADSHAPE
+    assert L.fgg_nvfp4_quantize(1, 0, 4, 24, 1, 8, 1, None, None) == _lib.FGG_EBADSHAPE
 
 
 def test_check_maps_codes_to_exceptions():

@@ -66,6 +66,18 @@ def test_quantizer_bf16_input(cuda_device):
     assert np.array_equal(sf.view(torch.uint8).cpu().numpy(), rs)
 
 
+def test_quantizer_decode_scale_of_zero_tensor(cuda_device):
+    """amax 0: gs = 1, so the decode scale written by the kernel is exactly 1,
+    and every code and scale byte is 0 (also for an empty tensor)."""
+    import ratchet_b200 as rb
+
+    codes, sf, g = rb.quantize_nvfp4(torch.zeros((8, 64), device=cuda_device))
+    assert float(g.item()) == 1.0
+    assert int(codes.sum()) == 0 and int(sf.view(torch.uint8).sum()) == 0
+    _, _, g0 = rb.quantize_nvfp4(torch.zeros((0, 64), device=cuda_device))
+    assert float(g0.item()) == 1.0
+
+
 def test_config1_single_group(cuda_device):
     """M=128, N=256, K=512, one group."""
     prob = ref.random_problem([128], 256, 512, seed=0)
