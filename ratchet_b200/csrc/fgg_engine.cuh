@@ -19,10 +19,16 @@
 //              in an 8-deep shared-memory ring, one tile ahead of the
 //              producer (the ring's depth covers the roles that lag behind)
 //   warps 4-7  epilogue: tcgen05.ld (each warp its 32-lane quadrant) -> fp32
-//              x alpha -> bf16 -> global, overlapped with the next tile's MMAs
+//              x alpha -> bf16 -> global (or the gated SiLU * up form),
+//              overlapped with the next tile's MMAs
 // The producer and MMA roles run on ONE thread each: between two K steps they
-// only test a barrier.  Every wait suspends in hardware (try_wait with a time
-// hint) so waiting warps do not steal issue slots from the MMA thread.
+// only test a barrier.  Every TMA or tcgen05 instruction holds its issuing
+// thread for about 60 cycles, so these two threads set the kernel's pace; the
+// layouts keep their instruction counts down (scale factors in the replicated
+// layout one 128x256b copy uploads, KSUB K steps per stage behind one barrier
+// test and one commit).  Every wait suspends in hardware (try_wait with a
+// time hint) so waiting warps do not steal issue slots from the MMA thread,
+// and the epilogue keeps its instruction stream short for the same reason.
 //
 // Two kernels:
 //   fgg_gemm_kernel       one CTA per tile, 128 weight rows x BN tokens
@@ -30,7 +36,8 @@
 //                         CTA loads half of the token tile
 // Two kinds (compile-time):
 //   NVFP4   .kind::mxf4nvf4 .scale_vec::4X: E2M1 x E2M1, one E4M3 scale per 16
-//           K; K step 256 = 4 MMAs of K 64, one SF slot per MMA.
+//           K; K step 256 = 4 MMAs of K 64, one SF slot per MMA (per MMA pair
+//           where one copy uploads the scales of two MMAs).
 //   MX      .kind::mxf8f6f4: weights E2M1 (4-bit codes unpacked to bytes by
 //           TMA), tokens E4M3, one UE8M0 scale per 32 K; K step 128 = 4 MMAs of
 //           K 32 that share one SF slot and pick their byte with the SF id.
