@@ -210,8 +210,8 @@ FGG_API int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t w
 
 /* Dispatch plan: a stable counting sort of the num_tokens x topk routes
  * (device topk_ids, row-major) by destination bin = owner[e] * local +
- * slot[e] (device int32 arrays over the num_experts experts; local = experts
- * per rank, world x local <= 512).  Writes counts[bin] (routes per bin),
+ * slot[e] (device int32 arrays over the num_experts <= 8192 experts; local =
+ * experts per rank, world x local <= 512).  Writes counts[bin] (routes per bin),
  * src_row[p] (the token of the route at sorted position p) and route_pos[i]
  * (the sorted position of route i).  Within a bin the routes keep their
  * order, as a stable sort leaves them.  An expert id outside

@@ -88,35 +88,55 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
 // sort would leave it.  Lanes holding the same bin in one step are grouped
 // with __match_any_sync: their count goes to the warp's histogram (phase A),
 // and their rank among themselves gives each one its slot (phase C).
+// The expert -> bin table sits in shared memory and each walk loads kPlanUnroll
+// steps of expert ids at once, so the walks are not a chain of dependent
+// global loads.
 constexpr int kPlanWarps = 16;
 constexpr int kPlanMaxBins = 512;
+constexpr int kPlanMaxExperts = 8192;
+constexpr int kPlanUnroll = 8;
 
 __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(
     const int32_t* __restrict__ ids, int32_t routes, int32_t topk,
     const int32_t* __restrict__ owner, const int32_t* __restrict__ slot, int32_t num_experts,
     int32_t local, int32_t bins, int32_t* __restrict__ counts, int32_t* __restrict__ src_row,
     int32_t* __restrict__ route_pos, int* __restrict__ bad) {
-  extern __shared__ int32_t hist[];  // [kPlanWarps][bins], then bin totals [bins]
+  // [kPlanWarps][bins] warp histograms, [bins] totals, [num_experts] bin of each expert
+  extern __shared__ int32_t hist[];
   int32_t* total = hist + kPlanWarps * bins;
+  int32_t* ebin = total + bins;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < kPlanWarps * bins; i += blockDim.x) hist[i] = 0;
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) {
+    const int sl = slot[e];
+    const int b = owner[e] * local + sl;
+    ebin[e] = (sl < 0 || sl >= local || b < 0 || b >= bins) ? -1 : b;  // -1: bad placement
+  }
   __syncthreads();
   const int chunk = (routes + kPlanWarps - 1) / kPlanWarps;
   const int lo = min(routes, warp * chunk), hi = min(routes, lo + chunk);
-  auto bin_of = [&](int i) -> int {  // -1: an id or placement entry out of range
-    const int e = ids[i];
+  // bin of route i given its expert id: -1 out of range (flagged), -2 past the chunk
+  auto bin_of = [&](int i, int e) -> int {
+    if (i >= hi) return -2;
     if (e < 0 || e >= num_experts) return -1;
-    const int b = owner[e] * local + slot[e];
-    return (slot[e] < 0 || slot[e] >= local || b < 0 || b >= bins) ? -1 : b;
+    return ebin[e];
   };
   // A: per-warp histogram
-  for (int base = lo; base < hi; base += 32) {
-    const int i = base + lane;
-    const int b = i < hi ? bin_of(i) : -2;
-    if (b == -1) atomicExch(bad, 1);
-    const unsigned same = __match_any_sync(0xffffffffu, b);
-    if (b >= 0 && lane == __ffs(same) - 1) hist[warp * bins + b] += __popc(same);
-    __syncwarp();
+  for (int base = lo; base < hi; base += 32 * kPlanUnroll) {
+    int e[kPlanUnroll];
+#pragma unroll
+    for (int u = 0; u < kPlanUnroll; ++u) {
+      const int i = base + 32 * u + lane;
+      e[u] = i < hi ? ids[i] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kPlanUnroll; ++u) {
+      const int b = bin_of(base + 32 * u + lane, e[u]);
+      if (b == -1) atomicExch(bad, 1);
+      const unsigned same = __match_any_sync(0xffffffffu, b);
+      if (b >= 0 && lane == __ffs(same) - 1) hist[warp * bins + b] += __popc(same);
+      __syncwarp();
+    }
   }
   __syncthreads();
   // B: bin totals, exclusive offsets over bins, per-warp bases within a bin
@@ -146,18 +166,27 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(
   }
   __syncthreads();
   // C: positions, in the same walk order as A
-  for (int base = lo; base < hi; base += 32) {
-    const int i = base + lane;
-    const int b = i < hi ? bin_of(i) : -2;
-    const unsigned same = __match_any_sync(0xffffffffu, b);
-    int pos = -1;
-    if (b >= 0) pos = hist[warp * bins + b] + __popc(same & ((1u << lane) - 1u));
-    __syncwarp();
-    if (b >= 0 && lane == __ffs(same) - 1) hist[warp * bins + b] += __popc(same);
-    __syncwarp();
-    if (i < hi) {
-      route_pos[i] = pos;
-      if (pos >= 0) src_row[pos] = i / topk;
+  for (int base = lo; base < hi; base += 32 * kPlanUnroll) {
+    int e[kPlanUnroll];
+#pragma unroll
+    for (int u = 0; u < kPlanUnroll; ++u) {
+      const int i = base + 32 * u + lane;
+      e[u] = i < hi ? ids[i] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kPlanUnroll; ++u) {
+      const int i = base + 32 * u + lane;
+      const int b = bin_of(i, e[u]);
+      const unsigned same = __match_any_sync(0xffffffffu, b);
+      int pos = -1;
+      if (b >= 0) pos = hist[warp * bins + b] + __popc(same & ((1u << lane) - 1u));
+      __syncwarp();
+      if (b >= 0 && lane == __ffs(same) - 1) hist[warp * bins + b] += __popc(same);
+      __syncwarp();
+      if (i < hi) {
+        route_pos[i] = pos;
+        if (pos >= 0) src_row[pos] = i / topk;
+      }
     }
   }
 }
@@ -210,12 +239,18 @@ int fgg_moe_plan(const int32_t* topk_ids, int32_t num_tokens, int32_t topk,
   if (bins > kPlanMaxBins)
     return set_error(FGG_EBADSHAPE, "world x local experts = %lld exceeds %d", (long long)bins,
                      kPlanMaxBins);
+  if (num_experts > kPlanMaxExperts)
+    return set_error(FGG_EBADSHAPE, "num_experts = %d exceeds %d", num_experts, kPlanMaxExperts);
   const int64_t routes = int64_t(num_tokens) * topk;
   if (routes > INT32_MAX) return set_error(FGG_EBADSHAPE, "too many routes");
   if (topk_ids == nullptr || owner == nullptr || slot == nullptr || counts == nullptr ||
       src_row == nullptr || route_pos == nullptr || bad == nullptr)
     return set_error(FGG_EINVAL, "null pointer");
-  const size_t smem = size_t(kPlanWarps + 1) * size_t(bins) * sizeof(int32_t);
+  const size_t smem =
+      (size_t(kPlanWarps + 1) * size_t(bins) + size_t(num_experts)) * sizeof(int32_t);
+  if (smem > 48 * 1024)
+    FGG_CUDA_CHECK(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(smem)));
   plan_kernel<<<1, kPlanWarps * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       topk_ids, int32_t(routes), topk, owner, slot, num_experts, local, int32_t(bins), counts,
       src_row, route_pos, bad);
