@@ -101,18 +101,6 @@ int encode_u64_rows(CUtensorMap* out, const void* base, uint64_t rows, uint32_t 
                 CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-// The weight scale atoms [num_atoms][512 B] seen as uint64 [chunk 4][atom][16]
-// with the chunk dimension (128 B apart) OUTSIDE the atom dimension (512 B
-// apart): a box {16, 2, 4} lands in shared memory as [chunk][atom][128 B],
-// one quarter of the replicated layout of a 128x256b scale copy of two atoms.
-int encode_sf_pairs(CUtensorMap* out, const void* base, uint64_t num_atoms) {
-  cuuint64_t dims[3] = {16, num_atoms, 4};
-  cuuint64_t strides[2] = {512, 128};
-  cuuint32_t box[3] = {16, 2, 4};
-  return encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, base, dims, strides, box,
-                CU_TENSOR_MAP_SWIZZLE_NONE);
-}
-
 int encode_3d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t d0,
               uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
               uint32_t b0, uint32_t b1, uint32_t b2) {

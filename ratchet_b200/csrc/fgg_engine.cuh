@@ -56,14 +56,6 @@ struct GroupInfo {
   int32_t wgroup;       // weight group (in the pack) this problem group multiplies with
 };
 
-// Byte offset, inside one replicated 4 KB token-scale block, of the copy of
-// line r0 of atom c that lane r0 + 32q receives (q = 0..3): the source layout
-// of one tcgen05.cp 128x256b (see desc_sf_pair_rep).
-__host__ __device__ __forceinline__ uint32_t sf_rep_offset(int c, int r0, int q) {
-  const int l = r0 + 32 * q;
-  return uint32_t((l >> 3) * 256 + c * 128 + (l & 7) * 16);
-}
-
 // A tile is packed into 32 bits: group (10) | weight tile (11) | token tile (11).
 __host__ __device__ __forceinline__ uint32_t pack_tile(int g, int nt, int xt) {
   return (uint32_t(g) << 22) | (uint32_t(nt) << 11) | uint32_t(xt);
@@ -264,14 +256,8 @@ struct EngineCfg {
   static constexpr uint32_t X_BYTES = BN * 128;
   // NVFP4: 4 atoms (one per K64 MMA); MX: one atom covers the 4 K32 MMAs.
   static constexpr uint32_t SFW_BYTES = MX ? 512 : 4 * 512;
-  // Token scales.  Two atoms per MMA (224-token tiles): the replicated 4 KB
-  // layout that one 128x256b copy uploads, per MMA.  One atom per MMA
-  // (16-token decode tiles, NVFP4): the atoms of MMAs (0, 1) and (2, 3) in
-  // that layout, one copy per MMA pair (SFX_PAIR).
-  static constexpr bool SFX_REP = (CH == 2);
-  static constexpr bool SFX_PAIR = (CH == 1 && !MX);
-  static constexpr uint32_t SFX_UNIT = SFX_REP ? 4096 : SFX_PAIR ? 2048 : CH * 512;
-  static constexpr uint32_t SFX_BYTES = MX ? SFX_UNIT : 4 * SFX_UNIT;
+  // token scales: CH atoms per MMA (NVFP4) or per K step (MX)
+  static constexpr uint32_t SFX_BYTES = MX ? CH * 512 : 4 * CH * 512;
   static constexpr uint32_t TX_BYTES = W_TX + X_BYTES + SFW_BYTES + SFX_BYTES;
   // bytes of one K step's tiles; a stage holds KSUB of them
   static constexpr uint32_t SUB_BYTES =
@@ -281,10 +267,9 @@ struct EngineCfg {
   static_assert((W_BYTES + X_BYTES) % 1024 == 0, "operand tiles must stay 1024 B aligned");
   // TMEM columns: two accumulators of BN fp32 columns, then a ring of scale
   // slots (4 columns of weight scales + 4 per token atom).  NVFP4 takes one
-  // slot per MMA, MX one per K step; with SFX_PAIR one slot per MMA pair,
-  // [weights a 4 | weights b 4 | tokens a 4 | tokens b 4].
+  // slot per MMA, MX one per K step.
   static constexpr int SF_BASE = ((2 * BN + 3) / 4) * 4;
-  static constexpr int SF_SLOT = SFX_PAIR ? 16 : 4 + 4 * CH;
+  static constexpr int SF_SLOT = 4 + 4 * CH;
   static constexpr int NSLOTS_FIT = (512 - SF_BASE) / SF_SLOT;
   static constexpr int NSLOTS = NSLOTS_FIT > 8 ? 8 : NSLOTS_FIT;
   static_assert(NSLOTS >= 2, "not enough TMEM for the scale ring");
@@ -411,40 +396,50 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
     __syncwarp();
   } else if (warp == 0) {
     // ------------------------------------------------------------- producer
-    if (lane == 0 && !aborted_early) {
+    // The whole warp runs the loop (operands warp-uniform), one elected lane
+    // issues the loads.
+    if (!aborted_early) {
       int stage = 0;
       uint32_t phase = 0;
       int slot = 0;
       uint32_t sphase = 0;
       uint32_t arms = 0;
       if constexpr (C::MX) {
-        prefetch_tensormap(&p.mx_tmap_w);
-        prefetch_tensormap(&p.mx_tmap_x);
+        if (lane == 0) {
+          prefetch_tensormap(&p.mx_tmap_w);
+          prefetch_tensormap(&p.mx_tmap_x);
+        }
       }
       while (true) {
-        if (!mbar_wait1(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutProducer))
+        if (!mbar_wait(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutProducer))
           break;
-        const SchedSlot s = read_slot(ring, slot);
-        mbar_arrive(schede_bar(slot));
-        mbar_arrive(taken_bar);
+        const uint32_t tile = __shfl_sync(kFullMask, ring[slot].tile, 0);
+        const int xtile_index = __shfl_sync(kFullMask, ring[slot].xtile_index, 0);
+        const int wgroup = __shfl_sync(kFullMask, ring[slot].wgroup, 0);
+        if (lane == 0) {
+          mbar_arrive(schede_bar(slot));
+          mbar_arrive(taken_bar);
+        }
         if (++slot == C::SCHED) {
           slot = 0;
           sphase ^= 1;
         }
-        if (s.tile == kEndTile) {
+        if (tile == kEndTile) {
           // no new tiles for this CTA: the next kernel on the stream (the next
           // call's prepare kernel) may launch; it waits for this grid's
           // completion before it touches memory
-          griddep_launch_dependents();
+          if (lane == 0) griddep_launch_dependents();
           break;
         }
-        const int g = int(s.tile >> 22);
-        const int nti = int((s.tile >> 11) & 0x7FFu);
-        const int xti = int(s.tile & 0x7FFu);
+        const int g = int(tile >> 22);
+        const int nti = int((tile >> 11) & 0x7FFu);
+        const int xti = int(tile & 0x7FFu);
         // the group and weight group index descriptor arrays: never trust them blindly
-        if (g >= p.g || unsigned(s.wgroup) >= unsigned(p.wg)) {
-          atomicCAS(p.status, 0, kStatusBadTile);
-          *abort_flag = 1;
+        if (g >= p.g || unsigned(wgroup) >= unsigned(p.wg)) {
+          if (lane == 0) {
+            atomicCAS(p.status, 0, kStatusBadTile);
+            *abort_flag = 1;
+          }
           break;
         }
         const CUtensorMap* tw;
@@ -453,43 +448,46 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
           tw = &p.mx_tmap_w;
           tx = &p.mx_tmap_x;
         } else {
-          tw = p.tmap_w + s.wgroup;
+          tw = p.tmap_w + wgroup;
           tx = p.tmap_x + g;
-          tensormap_acquire(tw);
+          tensormap_acquire(tw);  // every lane: the issuing one among them
           tensormap_acquire(tx);
         }
-        const uint8_t* sfx = p.sfx + size_t(s.xtile_index) * size_t(p.ksteps) * C::SFX_BYTES;
+        const uint8_t* sfx = p.sfx + size_t(xtile_index) * size_t(p.ksteps) * C::SFX_BYTES;
         const uint8_t* sfw =
-            p.sfw + (size_t(s.wgroup) * p.nt + nti) * size_t(p.ksteps) * C::SFW_BYTES;
+            p.sfw + (size_t(wgroup) * p.nt + nti) * size_t(p.ksteps) * C::SFW_BYTES;
         bool ok = true;
         for (int ks0 = 0; ks0 < p.ksteps; ks0 += C::KSUB) {
-          if (!mbar_wait1(empty_bar(stage), phase ^ 1, abort_flag, p.status,
-                          kStatusTimeoutProducer)) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.status,
+                         kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
           const uint32_t fb = full_bar(stage);
-          if constexpr (C::KSUB == 1)
-            mbar_arrive_expect_tx(fb, C::TX_BYTES);
-          else
-            mbar_arrive_expect_tx(fb, C::TX_BYTES * uint32_t(min(C::KSUB, p.ksteps - ks0)));
+          if (elect_one()) {
+            if constexpr (C::KSUB == 1)
+              mbar_arrive_expect_tx(fb, C::TX_BYTES);
+            else
+              mbar_arrive_expect_tx(fb, C::TX_BYTES * uint32_t(min(C::KSUB, p.ksteps - ks0)));
 #pragma unroll
-          for (int sub = 0; sub < C::KSUB; ++sub) {
-            const int ks = ks0 + sub;
-            if constexpr (C::KSUB > 1) {
-              if (ks >= p.ksteps) break;
+            for (int sub = 0; sub < C::KSUB; ++sub) {
+              const int ks = ks0 + sub;
+              if constexpr (C::KSUB > 1) {
+                if (ks >= p.ksteps) break;
+              }
+              const int q = stage * C::KSUB + sub;
+              if constexpr (C::MX) {
+                tma_load_3d(sW(q), tw, fb, ks * C::K_STEP, nti * 128, g);
+                tma_load_2d(sX(q), tx, fb, ks * C::K_STEP, xti * C::BN);
+              } else {
+                tma_load_2d(sW(q), tw, fb, ks * 128, nti * 128);
+                tma_load_2d(sX(q), tx, fb, ks * 128, xti * C::BN);
+              }
+              bulk_g2s(sSFW(q), sfw + size_t(ks) * C::SFW_BYTES, C::SFW_BYTES, fb);
+              bulk_g2s(sSFX(q), sfx + size_t(ks) * C::SFX_BYTES, C::SFX_BYTES, fb);
             }
-            const int q = stage * C::KSUB + sub;
-            if constexpr (C::MX) {
-              tma_load_3d(sW(q), tw, fb, ks * C::K_STEP, nti * 128, g);
-              tma_load_2d(sX(q), tx, fb, ks * C::K_STEP, xti * C::BN);
-            } else {
-              tma_load_2d(sW(q), tw, fb, ks * 128, nti * 128);
-              tma_load_2d(sX(q), tx, fb, ks * 128, xti * C::BN);
-            }
-            bulk_g2s(sSFW(q), sfw + size_t(ks) * C::SFW_BYTES, C::SFW_BYTES, fb);
-            bulk_g2s(sSFX(q), sfx + size_t(ks) * C::SFX_BYTES, C::SFX_BYTES, fb);
           }
+          __syncwarp();
           ++arms;
           if (++stage == C::STAGES) {
             stage = 0;
@@ -499,17 +497,22 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
         if (!ok) break;
       }
       // Every armed stage must land before the CTA may exit (normally already so).
-      const uint32_t first = arms > uint32_t(C::STAGES) ? arms - C::STAGES : 0u;
-      for (uint32_t a = first; a < arms; ++a)
-        mbar_wait_one(full_bar(int(a % C::STAGES)), (a / C::STAGES) & 1u, 200000000ull);
+      if (lane == 0) {
+        const uint32_t first = arms > uint32_t(C::STAGES) ? arms - C::STAGES : 0u;
+        for (uint32_t a = first; a < arms; ++a)
+          mbar_wait_one(full_bar(int(a % C::STAGES)), (a / C::STAGES) & 1u, 200000000ull);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0 && !aborted_early) {
-      bool ok = mbar_wait1(tmem_ready_bar, 0, abort_flag, p.status, kStatusTimeoutMma);
+    // The whole warp runs the loop; the scale uploads, MMAs and commits of a
+    // stage issue from one elect.sync region, with every operand (descriptors,
+    // TMEM columns) computed outside it and warp-uniform.
+    if (!aborted_early) {
+      bool ok = mbar_wait(tmem_ready_bar, 0, abort_flag, p.status, kStatusTimeoutMma);
       tc_fence_after();
-      const uint32_t tmem = *tmem_holder;
+      const uint32_t tmem = __shfl_sync(kFullMask, *tmem_holder, 0);
       int stage = 0;
       uint32_t phase = 0;
       int slot = 0;
@@ -518,96 +521,83 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
       int sfslot = 0;
       bool issued_any = false;
       while (ok) {
-        if (!mbar_wait1(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutMma))
-          break;
-        const SchedSlot s = read_slot(ring, slot);
-        mbar_arrive(schede_bar(slot));
+        if (!mbar_wait(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutMma)) break;
+        const uint32_t tile = __shfl_sync(kFullMask, ring[slot].tile, 0);
+        const int rows = __shfl_sync(kFullMask, ring[slot].rows, 0);
+        if (lane == 0) mbar_arrive(schede_bar(slot));
         if (++slot == C::SCHED) {
           slot = 0;
           sphase ^= 1;
         }
-        if (s.tile == kEndTile) break;
-        const int ncols = min(C::BN, (s.rows + 15) & ~15);
+        if (tile == kEndTile) break;
+        const int ncols = min(C::BN, (rows + 15) & ~15);
         const uint32_t b = lt & 1u;
-        if (!mbar_wait1(acce_bar(b), ((lt >> 1) & 1u) ^ 1u, abort_flag, p.status,
-                        kStatusTimeoutMma))
+        if (!mbar_wait(acce_bar(b), ((lt >> 1) & 1u) ^ 1u, abort_flag, p.status,
+                       kStatusTimeoutMma))
           break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + b * C::BN;
         const uint32_t idesc =
             C::MX ? 0u : idesc_block_scaled(kFmtNvf4E2M1, kFmtNvf4E2M1, 0, 128, ncols, 0, 0);
         for (int ks0 = 0; ks0 < p.ksteps; ks0 += C::KSUB) {
-          if (!mbar_wait1(full_bar(stage), phase, abort_flag, p.status, kStatusTimeoutMma)) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.status, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          // scale slots of this stage's MMAs (NVFP4: one per MMA; MX: one per K step)
+          constexpr int kSlots = C::KSUB * (C::MX ? 1 : 4);
+          uint32_t col[kSlots];
 #pragma unroll
-          for (int sub = 0; sub < C::KSUB; ++sub) {
-            const int ks = ks0 + sub;
-            if constexpr (C::KSUB > 1) {
-              if (ks >= p.ksteps) break;
-            }
-            const int q = stage * C::KSUB + sub;  // this K step's slot in the stage
-            const uint64_t adesc = desc_k_sw128(sW(q));
-            const uint64_t bdesc = desc_k_sw128(sX(q));
-            if constexpr (C::MX) {
-              const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-              tc_cp_sf(tmem + col, desc_sf_atom(sSFW(q)));
-              if constexpr (C::SFX_REP) {
-                tc_cp_sf2(tmem + col + 4, desc_sf_pair_rep(sSFX(q)));
-              } else {
+          for (int i = 0; i < kSlots; ++i) {
+            col[i] = tmem + C::SF_BASE + sfslot * C::SF_SLOT;
+            sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+          }
+          const bool last = ks0 + C::KSUB >= p.ksteps;
+          if (elect_one()) {
+#pragma unroll
+            for (int sub = 0; sub < C::KSUB; ++sub) {
+              const int ks = ks0 + sub;
+              if constexpr (C::KSUB > 1) {
+                if (ks >= p.ksteps) break;
+              }
+              const int q = stage * C::KSUB + sub;  // this K step's slot in the stage
+              const uint64_t adesc = desc_k_sw128(sW(q));
+              const uint64_t bdesc = desc_k_sw128(sX(q));
+              if constexpr (C::MX) {
+                const uint32_t c0 = col[sub];
+                tc_cp_sf(c0, desc_sf_atom(sSFW(q)));
 #pragma unroll
                 for (int c = 0; c < C::CH; ++c)
-                  tc_cp_sf(tmem + col + 4 + 4 * c, desc_sf_atom(sSFX(q) + c * 512));
-              }
+                  tc_cp_sf(c0 + 4 + 4 * c, desc_sf_atom(sSFX(q) + c * 512));
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                // K step of 32 one-byte elements = 32 bytes = +2 in the start field;
-                // SF id j picks byte j of every scale column.
-                const uint32_t idj =
-                    idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 128, ncols, j, j);
-                tc_mma_mxf8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
-                                (tmem + col) | (uint32_t(j) << 30),
-                                (tmem + col + 4) | (uint32_t(j) << 30), (ks | j) != 0 ? 1u : 0u);
-              }
-              sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
-            } else if constexpr (C::SFX_PAIR) {
-#pragma unroll
-              for (int pp = 0; pp < 2; ++pp) {  // MMAs (2pp, 2pp+1): one token-scale upload
-                const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-                tc_cp_sf2(tmem + col + 8, desc_sf_pair_rep(sSFX(q) + pp * 4096));
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const int j = 2 * pp + h;
-                  tc_cp_sf(tmem + col + 4 * h, desc_sf_atom(sSFW(q) + j * 512));
-                  // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
-                  tc_mma_nvf4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col + 4 * h,
-                              tmem + col + 8 + 4 * h, (ks | j) != 0 ? 1u : 0u);
+                for (int j = 0; j < 4; ++j) {
+                  // K step of 32 one-byte elements = 32 bytes = +2 in the start field;
+                  // SF id j picks byte j of every scale column.
+                  const uint32_t idj =
+                      idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 128, ncols, j, j);
+                  tc_mma_mxf8f6f4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
+                                  c0 | (uint32_t(j) << 30), (c0 + 4) | (uint32_t(j) << 30),
+                                  (ks | j) != 0 ? 1u : 0u);
                 }
-                sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
-              }
-            } else {
+              } else {
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-                tc_cp_sf(tmem + col, desc_sf_atom(sSFW(q) + j * 512));
-                if constexpr (C::SFX_REP) {
-                  tc_cp_sf2(tmem + col + 4, desc_sf_pair_rep(sSFX(q) + j * C::SFX_UNIT));
-                } else {
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t c0 = col[sub * 4 + j];
+                  tc_cp_sf(c0, desc_sf_atom(sSFW(q) + j * 512));
 #pragma unroll
                   for (int c = 0; c < C::CH; ++c)
-                    tc_cp_sf(tmem + col + 4 + 4 * c,
-                             desc_sf_atom(sSFX(q) + (j * C::CH + c) * 512));
+                    tc_cp_sf(c0 + 4 + 4 * c, desc_sf_atom(sSFX(q) + (j * C::CH + c) * 512));
+                  // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
+                  tc_mma_nvf4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, c0, c0 + 4,
+                              (ks | j) != 0 ? 1u : 0u);
                 }
-                // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
-                tc_mma_nvf4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, tmem + col,
-                            tmem + col + 4, (ks | j) != 0 ? 1u : 0u);
-                sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
               }
             }
+            tc_commit(empty_bar(stage));
+            if (last) tc_commit(accf_bar(b));
           }
-          tc_commit(empty_bar(stage));
+          __syncwarp();
           issued_any = true;
           if (++stage == C::STAGES) {
             stage = 0;
@@ -615,14 +605,15 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
           }
         }
         if (!ok) break;
-        tc_commit(accf_bar(b));
         ++lt;
       }
-      // Drain: every tcgen05 op this thread issued completes before TMEM is freed.
+      // Drain: every tcgen05 op the warp issued completes before TMEM is freed.
       if (issued_any) {
-        tc_commit(drain_bar);
-        if (!mbar_wait_one(drain_bar, 0, 200000000ull))
-          atomicCAS(p.status, 0, kStatusTimeoutDrain);
+        if (elect_one()) {
+          tc_commit(drain_bar);
+          if (!mbar_wait_one(drain_bar, 0, 200000000ull))
+            atomicCAS(p.status, 0, kStatusTimeoutDrain);
+        }
       }
     }
     __syncwarp();
@@ -715,14 +706,11 @@ struct PairCfg {
   static constexpr uint32_t W_BYTES = 128 * 128;
   static constexpr uint32_t W_TX = MX ? 64 * 128 : 128 * 128;
   static constexpr uint32_t X_BYTES = BNH * 128;
-  // Weight scales of a K step.  MX: one atom for the 4 MMAs.  NVFP4: the atoms
-  // of MMAs (0, 1) and (2, 3), each pair in the replicated 4 KB layout of one
-  // 128x256b copy, built by four TMA loads of 1 KB from the plain atoms.
-  static constexpr uint32_t SFW_BYTES = MX ? 512 : 2 * 4096;
-  // token scales of one slot in the replicated layout of one 128x256b copy
-  static constexpr bool SFX_REP = true;
-  static constexpr uint32_t SFX_UNIT = 4096;
-  static constexpr uint32_t SFX_BYTES = MX ? SFX_UNIT : 4 * SFX_UNIT;
+  // Weight scales of a K step (this CTA's 128 rows).  MX: one atom for the 4
+  // MMAs.  NVFP4: one atom per MMA.
+  static constexpr uint32_t SFW_BYTES = MX ? 512 : 4 * 512;
+  // token scales of all 224 tokens: two atoms per MMA (NVFP4) or per K step (MX)
+  static constexpr uint32_t SFX_BYTES = MX ? 2 * 512 : 4 * 2 * 512;
   // SF atoms travel as 2-D uint64 boxes {ROW_U64, BOX_ROWS}
   static constexpr uint32_t SFW_ROW_U64 = SFW_BYTES / 8 > 256 ? 256 : SFW_BYTES / 8;
   static constexpr uint32_t SFW_BOX_ROWS = SFW_BYTES / (8 * SFW_ROW_U64);
@@ -735,9 +723,8 @@ struct PairCfg {
   static constexpr uint32_t STAGE_BYTES = KSUB * SUB_BYTES;
   static_assert((W_BYTES + X_BYTES) % 1024 == 0, "operand tiles must stay 1024 B aligned");
   static constexpr int SF_BASE = 2 * BN;          // 448
-  // MX: [weights 4 | tokens 8] per K step.  NVFP4: per MMA pair,
-  // [weights a 4 | weights b 4 | tokens a 8 | tokens b 8].
-  static constexpr int SF_SLOT = MX ? 12 : 24;
+  // [weights 4 | tokens 8]: per MMA (NVFP4) or per K step (MX)
+  static constexpr int SF_SLOT = 12;
   static constexpr int NSLOTS = (512 - SF_BASE) / SF_SLOT;
   static_assert(NSLOTS >= 2, "not enough TMEM for the scale ring");
   static_assert(SF_BASE + NSLOTS * SF_SLOT <= 512, "TMEM columns exceeded");
@@ -879,101 +866,104 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     __syncwarp();
   } else if (warp == 0) {
     // ------------------------------------------------- producer (both CTAs)
-    if (lane == 0 && !aborted_early) {
+    // The whole warp runs the loop (operands warp-uniform), one elected lane
+    // issues the loads.
+    if (!aborted_early) {
       int stage = 0;
       uint32_t phase = 0;
       int slot = 0;
       uint32_t sphase = 0;
       uint32_t arms = 0;
-      if constexpr (C::MX) {
-        prefetch_tensormap(&p.mx_tmap_w);
-        prefetch_tensormap(&p.mx_tmap_x);
+      if (lane == 0) {
+        if constexpr (C::MX) {
+          prefetch_tensormap(&p.mx_tmap_w);
+          prefetch_tensormap(&p.mx_tmap_x);
+        }
+        prefetch_tensormap(&p.sfw_map);
+        prefetch_tensormap(&p.sfx_map);
       }
-      prefetch_tensormap(&p.sfw_map);
-      prefetch_tensormap(&p.sfx_map);
       while (true) {
-        if (!mbar_wait1<true>(schedf_bar(slot), sphase, abort_flag, p.status,
-                              kStatusTimeoutProducer))
+        if (!mbar_wait<true>(schedf_bar(slot), sphase, abort_flag, p.status,
+                             kStatusTimeoutProducer))
           break;
-        const SchedSlot s = read_slot(ring, slot);
-        release_slot(slot);
-        if (leader) mbar_arrive(taken_bar);
+        const uint32_t tile = __shfl_sync(kFullMask, ring[slot].tile, 0);
+        const int rows = __shfl_sync(kFullMask, ring[slot].rows, 0);
+        const int xtile_index = __shfl_sync(kFullMask, ring[slot].xtile_index, 0);
+        const int wgroup = __shfl_sync(kFullMask, ring[slot].wgroup, 0);
+        if (lane == 0) {
+          release_slot(slot);
+          if (leader) mbar_arrive(taken_bar);
+        }
         if (++slot == C::SCHED) {
           slot = 0;
           sphase ^= 1;
         }
-        if (s.tile == kEndTile) {
-          griddep_launch_dependents();  // as in the single-CTA kernel
+        if (tile == kEndTile) {
+          if (lane == 0) griddep_launch_dependents();  // as in the single-CTA kernel
           break;
         }
-        const int g = int(s.tile >> 22);
-        const int nti = int((s.tile >> 11) & 0x7FFu);
-        const int xti = int(s.tile & 0x7FFu);
+        const int g = int(tile >> 22);
+        const int nti = int((tile >> 11) & 0x7FFu);
+        const int xti = int(tile & 0x7FFu);
         // the group and weight group index descriptor arrays: never trust them blindly
-        if (g >= p.g || unsigned(s.wgroup) >= unsigned(p.wg)) {
-          atomicCAS(p.status, 0, kStatusBadTile);
-          *abort_flag = 1;
+        if (g >= p.g || unsigned(wgroup) >= unsigned(p.wg)) {
+          if (lane == 0) {
+            atomicCAS(p.status, 0, kStatusBadTile);
+            *abort_flag = 1;
+          }
           break;
         }
-        const int half = tile_ncols(s.rows) >> 1;
+        const int half = tile_ncols(rows) >> 1;
         const CUtensorMap* tw;
         const CUtensorMap* tx;
         if constexpr (C::MX) {
           tw = &p.mx_tmap_w;
           tx = &p.mx_tmap_x;
         } else {
-          tw = p.tmap_w + s.wgroup;
+          tw = p.tmap_w + wgroup;
           tx = p.tmap_x + g;
-          tensormap_acquire(tw);
+          tensormap_acquire(tw);  // every lane: the issuing one among them
           tensormap_acquire(tx);
         }
         const int wrow = nti * 256 + int(rank) * 128;
         const int xrow = xti * C::BN + int(rank) * half;
+        // this CTA's weight scale atoms of the tile: one row of SFW_BYTES per K step
         const int sfw_y =
-            ((s.wgroup * p.nt128 + 2 * nti + int(rank)) * p.ksteps) * int(C::SFW_BOX_ROWS);
-        // NVFP4: index of this CTA's first weight atom of the tile (4 per K step)
-        const int sfw_atom0 = (s.wgroup * p.nt128 + 2 * nti + int(rank)) * p.ksteps * 4;
-        const int sfx_y = (s.xtile_index * p.ksteps) * int(C::SFX_BOX_ROWS);
+            ((wgroup * p.nt128 + 2 * nti + int(rank)) * p.ksteps) * int(C::SFW_BOX_ROWS);
+        const int sfx_y = (xtile_index * p.ksteps) * int(C::SFX_BOX_ROWS);
         bool ok = true;
         for (int ks0 = 0; ks0 < p.ksteps; ks0 += C::KSUB) {
-          if (!mbar_wait1(empty_bar(stage), phase ^ 1, abort_flag, p.status,
-                          kStatusTimeoutProducer)) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.status,
+                         kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
-          if (leader) {
-            if constexpr (C::KSUB == 1)
-              mbar_arrive_expect_tx(full_bar(stage), 2u * C::TX_CTA);
-            else
-              mbar_arrive_expect_tx(full_bar(stage),
-                                    2u * C::TX_CTA * uint32_t(min(C::KSUB, p.ksteps - ks0)));
-          }
           const uint32_t fb = leader_full0 + 8u * stage;
-#pragma unroll
-          for (int sub = 0; sub < C::KSUB; ++sub) {
-            const int ks = ks0 + sub;
-            if constexpr (C::KSUB > 1) {
-              if (ks >= p.ksteps) break;
+          if (elect_one()) {
+            if (leader) {
+              if constexpr (C::KSUB == 1)
+                mbar_arrive_expect_tx(full_bar(stage), 2u * C::TX_CTA);
+              else
+                mbar_arrive_expect_tx(full_bar(stage),
+                                      2u * C::TX_CTA * uint32_t(min(C::KSUB, p.ksteps - ks0)));
             }
-            const int q = stage * C::KSUB + sub;
-            if constexpr (C::MX)
-              tma_load_3d_pair(sW(q), tw, fb, ks * C::K_STEP, wrow, g);
-            else
-              tma_load_2d_pair(sW(q), tw, fb, ks * 128, wrow);
-            tma_load_2d_pair(sX(q), tx, fb, ks * 128, xrow);
-            if constexpr (C::MX) {
+#pragma unroll
+            for (int sub = 0; sub < C::KSUB; ++sub) {
+              const int ks = ks0 + sub;
+              if constexpr (C::KSUB > 1) {
+                if (ks >= p.ksteps) break;
+              }
+              const int q = stage * C::KSUB + sub;
+              if constexpr (C::MX)
+                tma_load_3d_pair(sW(q), tw, fb, ks * C::K_STEP, wrow, g);
+              else
+                tma_load_2d_pair(sW(q), tw, fb, ks * 128, wrow);
+              tma_load_2d_pair(sX(q), tx, fb, ks * 128, xrow);
               tma_load_2d_pair(sSFW(q), &p.sfw_map, fb, 0, sfw_y + ks * int(C::SFW_BOX_ROWS));
-            } else {
-              // MMA pairs (0, 1) and (2, 3): four identical 1 KB quarters each
-#pragma unroll
-              for (int pp = 0; pp < 2; ++pp)
-#pragma unroll
-                for (int qq = 0; qq < 4; ++qq)
-                  tma_load_3d_pair(sSFW(q) + pp * 4096 + qq * 1024, &p.sfw_map, fb, 0,
-                                   sfw_atom0 + ks * 4 + 2 * pp, 0);
+              tma_load_2d_pair(sSFX(q), &p.sfx_map, fb, 0, sfx_y + ks * int(C::SFX_BOX_ROWS));
             }
-            tma_load_2d_pair(sSFX(q), &p.sfx_map, fb, 0, sfx_y + ks * int(C::SFX_BOX_ROWS));
           }
+          __syncwarp();
           ++arms;
           if (++stage == C::STAGES) {
             stage = 0;
@@ -983,7 +973,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         if (!ok) break;
       }
       // the leader's full barriers cover both CTAs' bytes: drain them before exit
-      if (leader) {
+      if (leader && lane == 0) {
         const uint32_t first = arms > uint32_t(C::STAGES) ? arms - C::STAGES : 0u;
         for (uint32_t a = first; a < arms; ++a)
           mbar_wait_one(full_bar(int(a % C::STAGES)), (a / C::STAGES) & 1u, 200000000ull);
@@ -992,10 +982,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     __syncwarp();
   } else if (warp == 1 && leader) {
     // ------------------------------------------------------- MMA issuer
-    if (lane == 0 && !aborted_early) {
-      bool ok = mbar_wait1(tmem_ready_bar, 0, abort_flag, p.status, kStatusTimeoutMma);
+    // The whole warp runs the loop; one elect.sync region per stage issues its
+    // scale uploads, MMAs and commits with warp-uniform operands.
+    if (!aborted_early) {
+      bool ok = mbar_wait(tmem_ready_bar, 0, abort_flag, p.status, kStatusTimeoutMma);
       tc_fence_after();
-      const uint32_t tmem = *tmem_holder;
+      const uint32_t tmem = __shfl_sync(kFullMask, *tmem_holder, 0);
       int stage = 0;
       uint32_t phase = 0;
       int slot = 0;
@@ -1004,72 +996,79 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       int sfslot = 0;
       bool issued_any = false;
       while (ok) {
-        if (!mbar_wait1<true>(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutMma))
+        if (!mbar_wait<true>(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutMma))
           break;
-        const SchedSlot s = read_slot(ring, slot);
-        mbar_arrive(schede_bar(slot));
+        const uint32_t tile = __shfl_sync(kFullMask, ring[slot].tile, 0);
+        const int rows = __shfl_sync(kFullMask, ring[slot].rows, 0);
+        if (lane == 0) mbar_arrive(schede_bar(slot));
         if (++slot == C::SCHED) {
           slot = 0;
           sphase ^= 1;
         }
-        if (s.tile == kEndTile) break;
-        const int ncols = tile_ncols(s.rows);
+        if (tile == kEndTile) break;
+        const int ncols = tile_ncols(rows);
         const uint32_t b = lt & 1u;
-        if (!mbar_wait1(acce_bar(b), ((lt >> 1) & 1u) ^ 1u, abort_flag, p.status,
-                        kStatusTimeoutMma))
+        if (!mbar_wait(acce_bar(b), ((lt >> 1) & 1u) ^ 1u, abort_flag, p.status,
+                       kStatusTimeoutMma))
           break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + b * C::BN;
         const uint32_t idesc =
             C::MX ? 0u : idesc_block_scaled(kFmtNvf4E2M1, kFmtNvf4E2M1, 0, 256, ncols, 0, 0);
         for (int ks0 = 0; ks0 < p.ksteps; ks0 += C::KSUB) {
-          if (!mbar_wait1(full_bar(stage), phase, abort_flag, p.status, kStatusTimeoutMma)) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.status, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          // scale slots of this stage's MMAs (NVFP4: one per MMA; MX: one per K step)
+          constexpr int kSlots = C::KSUB * (C::MX ? 1 : 4);
+          uint32_t col[kSlots];
 #pragma unroll
-          for (int sub = 0; sub < C::KSUB; ++sub) {
-            const int ks = ks0 + sub;
-            if constexpr (C::KSUB > 1) {
-              if (ks >= p.ksteps) break;
-            }
-            const int q = stage * C::KSUB + sub;  // this K step's slot in the stage
-            const uint64_t adesc = desc_k_sw128(sW(q));
-            const uint64_t bdesc = desc_k_sw128(sX(q));
-            if constexpr (C::MX) {
-              const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-              tc_cp_sf_pair(tmem + col, desc_sf_atom(sSFW(q)));
-              tc_cp_sf2_pair(tmem + col + 4, desc_sf_pair_rep(sSFX(q)));
+          for (int i = 0; i < kSlots; ++i) {
+            col[i] = tmem + C::SF_BASE + sfslot * C::SF_SLOT;
+            sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
+          }
+          const bool last = ks0 + C::KSUB >= p.ksteps;
+          if (elect_one()) {
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint32_t idj =
-                    idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 256, ncols, j, j);
-                tc_mma_mxf8f6f4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
-                                     (tmem + col) | (uint32_t(j) << 30),
-                                     (tmem + col + 4) | (uint32_t(j) << 30),
-                                     (ks | j) != 0 ? 1u : 0u);
+            for (int sub = 0; sub < C::KSUB; ++sub) {
+              const int ks = ks0 + sub;
+              if constexpr (C::KSUB > 1) {
+                if (ks >= p.ksteps) break;
               }
-              sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
-            } else {
+              const int q = stage * C::KSUB + sub;  // this K step's slot in the stage
+              const uint64_t adesc = desc_k_sw128(sW(q));
+              const uint64_t bdesc = desc_k_sw128(sX(q));
+              if constexpr (C::MX) {
+                const uint32_t c0 = col[sub];
+                tc_cp_sf_pair(c0, desc_sf_atom(sSFW(q)));
+                tc_cp_sf_pair(c0 + 4, desc_sf_atom(sSFX(q)));
+                tc_cp_sf_pair(c0 + 8, desc_sf_atom(sSFX(q) + 512));
 #pragma unroll
-              for (int pp = 0; pp < 2; ++pp) {  // MMA pairs (2pp, 2pp+1) share one weight upload
-                const uint32_t col = C::SF_BASE + sfslot * C::SF_SLOT;
-                tc_cp_sf2_pair(tmem + col, desc_sf_pair_rep(sSFW(q) + pp * 4096));
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t idj =
+                      idesc_block_scaled(kFmtF8E2M1, kFmtF8E4M3, 1, 256, ncols, j, j);
+                  tc_mma_mxf8f6f4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idj,
+                                       c0 | (uint32_t(j) << 30), (c0 + 4) | (uint32_t(j) << 30),
+                                       (ks | j) != 0 ? 1u : 0u);
+                }
+              } else {
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const int j = 2 * pp + h;
-                  tc_cp_sf2_pair(tmem + col + 8 + 8 * h,
-                                 desc_sf_pair_rep(sSFX(q) + j * C::SFX_UNIT));
-                  tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc,
-                                   tmem + col + 4 * h, tmem + col + 8 + 8 * h,
+                for (int j = 0; j < 4; ++j) {
+                  const uint32_t c0 = col[sub * 4 + j];
+                  tc_cp_sf_pair(c0, desc_sf_atom(sSFW(q) + j * 512));
+                  tc_cp_sf_pair(c0 + 4, desc_sf_atom(sSFX(q) + (2 * j) * 512));
+                  tc_cp_sf_pair(c0 + 8, desc_sf_atom(sSFX(q) + (2 * j + 1) * 512));
+                  tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, c0, c0 + 4,
                                    (ks | j) != 0 ? 1u : 0u);
                 }
-                sfslot = (sfslot + 1 == C::NSLOTS) ? 0 : sfslot + 1;
               }
             }
+            tc_commit_pair(empty_bar(stage), 0x3);
+            if (last) tc_commit_pair(accf_bar(b), 0x3);
           }
-          tc_commit_pair(empty_bar(stage), 0x3);
+          __syncwarp();
           issued_any = true;
           if (++stage == C::STAGES) {
             stage = 0;
@@ -1077,13 +1076,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           }
         }
         if (!ok) break;
-        tc_commit_pair(accf_bar(b), 0x3);
         ++lt;
       }
       if (issued_any) {
-        tc_commit_pair(drain_bar, 0x1);
-        if (!mbar_wait_one(drain_bar, 0, 200000000ull))
-          atomicCAS(p.status, 0, kStatusTimeoutDrain);
+        if (elect_one()) {
+          tc_commit_pair(drain_bar, 0x1);
+          if (!mbar_wait_one(drain_bar, 0, 200000000ull))
+            atomicCAS(p.status, 0, kStatusTimeoutDrain);
+        }
       }
     }
     __syncwarp();

@@ -48,10 +48,6 @@ int encode_3d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uin
               uint32_t b0, uint32_t b1, uint32_t b2);
 int encode_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t d0,
               uint64_t d1, uint64_t stride1_bytes, uint32_t b0, uint32_t b1);
-// The weight scale atoms [num_atoms][512 B] as a 3-D uint64 tensor whose
-// {16, 2, 4} boxes land as one quarter of the replicated two-atom layout of a
-// 128x256b scale copy.
-int encode_sf_pairs(CUtensorMap* out, const void* base, uint64_t num_atoms);
 // A contiguous byte buffer viewed as `rows` rows of `row_u64` uint64 values,
 // unswizzled, box {row_u64, box_rows}: how packed scale-factor atoms travel.
 int encode_u64_rows(CUtensorMap* out, const void* base, uint64_t rows, uint32_t row_u64,

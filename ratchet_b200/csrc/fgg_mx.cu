@@ -25,13 +25,13 @@ namespace {
 constexpr int kMxBlockM = 224;  // token tile = the reference's ALIGN (kernel.py:274)
 
 using CfgMx = EngineCfg<true, kMxBlockM, 4>;  // one CTA per tile (N % 256 != 0)
-using CfgMxPair = PairCfg<true, 3, 2>;       // CTA pairs, 256 x 224 tiles, 2 K steps per stage
+using CfgMxPair = PairCfg<true, 6>;          // CTA pairs, 256 x 224 tiles
 
 struct MxPrepParams {
   const float* a_sf;        // [M_total, K/128]
   const float* b_sf;        // [G, N, K/32]
   const int32_t* m_indices; // [M_total]
-  uint8_t* sfx_out;         // [XB][KS][4 KB replicated pair of atoms]
+  uint8_t* sfx_out;         // [XB][KS][2][512]
   uint8_t* sfw_out;         // [G][NT][KS][512]
   uint32_t* tiles_out;      // [XB * NT]
   int* status;
@@ -88,12 +88,8 @@ __global__ void __launch_bounds__(256) mx_prepare_kernel(const __grid_constant__
       if (rr < kMxBlockM && row < p.m_total)
         v[r1] = e8m0_byte(__ldg(p.a_sf + size_t(row) * kq + ks)) * 0x01010101u;
     }
-    // the replicated 4 KB block one 128x256b copy uploads
-    const uint4 line16 = make_uint4(v[0], v[1], v[2], v[3]);
-    uint8_t* blk4k = p.sfx_out + (size_t(xb) * p.ksteps + ks) * 4096u;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      *reinterpret_cast<uint4*>(blk4k + sf_rep_offset(c, r0, q)) = line16;
+    *reinterpret_cast<uint4*>(p.sfx_out + ((size_t(xb) * p.ksteps + ks) * 2 + c) * 512u +
+                              size_t(r0) * 16u) = make_uint4(v[0], v[1], v[2], v[3]);
     return;
   }
   blk -= p.blocks_sfx;
@@ -148,7 +144,7 @@ int mx_plan(const FggMxProblem* p, MxLayout* L) {
   Carver cv;
   L->status = cv.take(kStatusBytes, 256);
   L->tiles = cv.take(size_t(std::max(L->num_tiles, 1)) * 4, 256);
-  L->sfx = cv.take(size_t(std::max(L->xblocks, 1)) * L->ksteps * 4096, 256);
+  L->sfx = cv.take(size_t(std::max(L->xblocks, 1)) * L->ksteps * 1024, 256);
   L->sfw = cv.take(size_t(p->num_groups) * L->nt128 * L->ksteps * 512, 256);
   L->total = cv.off;
   return FGG_OK;

@@ -123,20 +123,8 @@ __global__ void __launch_bounds__(256) nvfp4_prepare_kernel(const __grid_constan
     if (rr < p.bn && row < p.m[g] && 4 * j < kq)
       v[r1] = __ldg(reinterpret_cast<const uint32_t*>(p.a_sf[g] + size_t(row) * kq + 4 * j));
   }
-  const uint4 line16 = make_uint4(v[0], v[1], v[2], v[3]);
-  if (p.ch == 1) {
-    // 16-token tiles: the atoms of MMAs (2i, 2i+1) in one replicated block
-    uint8_t* blk4k = p.sfx_out + (size_t(X) * p.nk64p + (j & ~1)) * 2048u;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      *reinterpret_cast<uint4*>(blk4k + sf_rep_offset(j & 1, r0, q)) = line16;
-  } else {
-    // 224-token tiles: the replicated block one 128x256b copy uploads
-    uint8_t* blk4k = p.sfx_out + (size_t(X) * p.nk64p + j) * 4096u;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      *reinterpret_cast<uint4*>(blk4k + sf_rep_offset(c, r0, q)) = line16;
-  }
+  *reinterpret_cast<uint4*>(p.sfx_out + ((size_t(X) * p.nk64p + j) * p.ch + c) * 512u +
+                            size_t(r0) * 16u) = make_uint4(v[0], v[1], v[2], v[3]);
 }
 
 struct PackParams {
@@ -199,9 +187,9 @@ __global__ void __launch_bounds__(256) nvfp4_pack_weights_kernel(const __grid_co
 }
 
 // ------------------------------------------------------------ host side
-using CfgPrefill = EngineCfg<false, 224, 3>;   // one CTA per tile (N % 256 != 0)
+using CfgPrefill = EngineCfg<false, 224, 4>;   // one CTA per tile (N % 256 != 0)
 using CfgDecode = EngineCfg<false, 16, 4, 2>;  // every group has M <= 16; 2 K steps per stage
-using CfgPair = PairCfg<false, 4>;             // CTA pairs, 256 x 224 tiles
+using CfgPair = PairCfg<false, 6>;             // CTA pairs, 256 x 224 tiles
 
 struct PackLayout {
   size_t header, tmaps, sfw, total;
@@ -291,10 +279,8 @@ static int plan(const FggNvfp4Problem* p, WsLayout* L) {
   L->tmaps = cv.take(size_t(G) * sizeof(CUtensorMap), 128);
   L->ginfo = cv.take(size_t(G) * sizeof(GroupInfo), 256);
   L->tiles = cv.take(size_t(std::max<int64_t>(tiles, 1)) * 4, 256);
-  // token scales per (token tile, MMA) in the replicated layout of a 128x256b
-  // copy: two atoms per MMA (4 KB), or for 16-token tiles the atoms of two
-  // MMAs per 4 KB block (2 KB per MMA)
-  L->sfx = cv.take(size_t(std::max<int64_t>(xts, 1)) * L->nk64p * (L->ch == 2 ? 4096 : 2048), 256);
+  // token scales per (token tile, MMA): ch atoms of 512 B
+  L->sfx = cv.take(size_t(std::max<int64_t>(xts, 1)) * L->nk64p * L->ch * 512, 256);
   L->total = cv.off;
   return FGG_OK;
 }
@@ -473,10 +459,11 @@ int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uin
   gp.nt128 = L.nt128;
   cudaError_t e;
   if (L.pair) {
-    // weight scale atoms as a 3-D uint64 tensor whose boxes build the replicated
-    // layout of two atoms; token scales (already replicated by the prepare
-    // kernel, 16 KB per token tile and K step) as 2 KB rows
-    if (int rc = encode_sf_pairs(&gp.sfw_map, gp.sfw, uint64_t(L.wg) * L.nt128 * L.nk64p))
+    // scale atoms as rows of uint64: a CTA's 4 weight atoms of a K step are one
+    // 2 KB row of the pack, the 8 token atoms of a K step two 2 KB rows
+    if (int rc = encode_u64_rows(&gp.sfw_map, gp.sfw,
+                                 uint64_t(L.wg) * L.nt128 * L.nk256 * CfgPair::SFW_BOX_ROWS,
+                                 CfgPair::SFW_ROW_U64, CfgPair::SFW_BOX_ROWS))
       return rc;
     if (int rc = encode_u64_rows(&gp.sfx_map, gp.sfx,
                                  uint64_t(L.xt_total) * L.nk256 * CfgPair::SFX_BOX_ROWS,

@@ -24,6 +24,21 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// One lane of a converged warp (elect.sync over the full mask).  The producer
+// and MMA roles run their loops on the whole warp, so every operand of a TMA or
+// tcgen05 instruction is warp-uniform, and issue from the elected lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -281,13 +296,6 @@ __device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
                : "memory");
 }
-// 128 lanes x 256 bit from shared memory (no replication): with a source whose
-// lane l holds line l%32 of two scale atoms, this leaves TMEM exactly as two
-// 32x128b.warpx4 copies of those atoms would, in one instruction.
-__device__ __forceinline__ void tc_cp_sf2(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc)
-               : "memory");
-}
 // D[tmem] (+)= A[smem] * B[smem]^T with per-16-element E4M3 block scales read from TMEM.
 __device__ __forceinline__ void tc_mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                             uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
@@ -339,10 +347,6 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t cta_mask) 
 }
 __device__ __forceinline__ void tc_cp_sf_pair(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
-               : "memory");
-}
-__device__ __forceinline__ void tc_cp_sf2_pair(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::2.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc)
                : "memory");
 }
 __device__ __forceinline__ void tc_mma_nvf4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
@@ -405,12 +409,6 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t saddr) {
 // Scale-factor atom (512 B = 32 rows x 16 B, core matrices of 8 x 16 B).
 __device__ __forceinline__ uint64_t desc_sf_atom(uint32_t saddr) {
   return smem_desc(saddr, 128, 128, kLayoutNone);
-}
-// Two scale atoms laid out for one 128x256b copy (4 KB): lane l's 32 bytes are
-// line l%32 of atom 0 then of atom 1, as core matrices of 8 lanes x 16 B:
-// byte (l/8)*256 + h*128 + (l%8)*16 holds line l%32 of atom h.
-__device__ __forceinline__ uint64_t desc_sf_pair_rep(uint32_t saddr) {
-  return smem_desc(saddr, 128, 256, kLayoutNone);
 }
 
 // Instruction descriptor, block-scaled kinds (bit fields from the PTX ISA

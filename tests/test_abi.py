@@ -92,9 +92,8 @@ def _ws_bytes_py(ms, n, k):
     take(len(ms) * 128, 128)
     take(len(ms) * 16, 256)
     take(max(tiles, 1) * 4, 256)
-    # token scales, replicated for 128x256b copies: 4 KB per MMA (224-token
-    # tiles, two atoms) or 4 KB per two MMAs (16-token tiles)
-    take(max(xts, 1) * nk64p * (4096 if ch == 2 else 2048), 256)
+    # token scales: ch atoms of 512 B per (token tile, MMA)
+    take(max(xts, 1) * nk64p * ch * 512, 256)
     return off
 
 
