@@ -19,15 +19,18 @@
 namespace fgg {
 
 // ------------------------------------------------------- prepare kernels
+// The per-group arrays travel as kernel parameters; CAP groups of room (a
+// small instance for the common few-group call keeps the launch light).
+template <int CAP>
 struct PrepParams {
   CUtensorMap tmpl;  // token descriptor template (group 0's geometry)
-  const uint8_t* a[FGG_MAX_GROUPS];
-  const uint8_t* a_sf[FGG_MAX_GROUPS];
-  int32_t m[FGG_MAX_GROUPS];
-  int32_t xtile_begin[FGG_MAX_GROUPS + 1];
-  int32_t tile_begin[FGG_MAX_GROUPS + 1];
-  int32_t out_row[FGG_MAX_GROUPS];
-  int32_t wgroup[FGG_MAX_GROUPS];  // weight group of each problem group
+  const uint8_t* a[CAP];
+  const uint8_t* a_sf[CAP];
+  int32_t m[CAP];
+  int32_t xtile_begin[CAP + 1];
+  int32_t tile_begin[CAP + 1];
+  int32_t out_row[CAP];
+  int32_t wgroup[CAP];  // weight group of each problem group
   CUtensorMap* tmap_out;
   GroupInfo* ginfo_out;
   uint32_t* tiles_out;
@@ -49,14 +52,16 @@ __device__ __forceinline__ int find_group(const int32_t* begin, int g_count, int
   return lo;
 }
 
-__global__ void __launch_bounds__(256) nvfp4_prepare_kernel(const __grid_constant__ PrepParams p) {
+template <int CAP>
+__global__ void __launch_bounds__(256)
+    nvfp4_prepare_kernel(const __grid_constant__ PrepParams<CAP> p) {
   // every block is resident once it gets here: the GEMM grid behind this one
   // may launch now (it waits for this grid's results before reading them)
   griddep_launch_dependents();
   // launched early behind the previous GEMM: touch no memory before it is done
   griddep_wait();
   __shared__ alignas(128) CUtensorMap smap[8];
-  __shared__ int32_t sbegin[FGG_MAX_GROUPS + 1];
+  __shared__ int32_t sbegin[CAP + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int blk = blockIdx.x;
   if (blk < p.blocks_tmap) {
@@ -381,14 +386,11 @@ int check_problem(const FggNvfp4Problem* p, const WsLayout& L, void* workspace, 
   return FGG_OK;
 }
 
-int prepare_impl(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8_t* ws,
-                 cudaStream_t s) {
+template <int CAP>
+int prepare_launch(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8_t* ws,
+                   cudaStream_t s) {
   const int G = p->num_groups;
-  if (L.num_tiles == 0) {
-    FGG_CUDA_CHECK(cudaMemsetAsync(ws + L.status, 0, kStatusBytes, s));
-    return FGG_OK;
-  }
-  static thread_local PrepParams pp;  // ~17 KB: keep it off the stack
+  static thread_local PrepParams<CAP> pp;  // up to ~17 KB: keep it off the stack
   memset(&pp, 0, sizeof(pp));
   if (int rc = encode_u8_2d(&pp.tmpl, p->a[first], uint64_t(p->k) / 2, uint64_t(p->m[first]), 128,
                             uint32_t(L.box_rows)))
@@ -422,9 +424,21 @@ int prepare_impl(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8_t
   const int64_t sf_lines = int64_t(L.xt_total) * L.nk64p * L.ch * 32;
   const int64_t blocks = int64_t(pp.blocks_tmap) + pp.blocks_tiles + (sf_lines + 255) / 256;
   if (blocks > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
-  FGG_CUDA_CHECK(launch_dependent(nvfp4_prepare_kernel, int(blocks), 0, s, pp));
+  FGG_CUDA_CHECK(launch_dependent(nvfp4_prepare_kernel<CAP>, int(blocks), 0, s, pp));
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
+}
+
+constexpr int kPrepSmallCap = 32;
+
+int prepare_impl(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8_t* ws,
+                 cudaStream_t s) {
+  if (L.num_tiles == 0) {
+    FGG_CUDA_CHECK(cudaMemsetAsync(ws + L.status, 0, kStatusBytes, s));
+    return FGG_OK;
+  }
+  if (p->num_groups <= kPrepSmallCap) return prepare_launch<kPrepSmallCap>(p, L, first, ws, s);
+  return prepare_launch<FGG_MAX_GROUPS>(p, L, first, ws, s);
 }
 
 int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uint8_t* ws,

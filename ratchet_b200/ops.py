@@ -46,8 +46,53 @@ def _as_u8(t: torch.Tensor, name: str) -> torch.Tensor:
     return t if t.dtype == torch.uint8 else t.view(torch.uint8)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_get_device = getattr(torch._C, "_cuda_getDevice", None)
+_capturing = getattr(torch._C, "_cuda_isCurrentStreamCapturing", None)
+
+
 def _stream_ptr(device: torch.device) -> int:
+    if _raw_stream is not None and device.index is not None:
+        return int(_raw_stream(device.index))
     return int(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _is_current(device: torch.device) -> bool:
+    """True when `device` is the current CUDA device (no context switch needed)."""
+    cur = _get_device() if _get_device is not None else torch.cuda.current_device()
+    return device.index is None or device.index == cur
+
+
+# Workspaces reused per (device, stream): calls on one stream are ordered, so
+# the next call's prepare kernel (which waits for the previous GEMM before it
+# touches memory) may overwrite the previous call's workspace.  Not used while
+# the stream is being captured into a CUDA graph (the graph keeps its own).
+_WS: dict = {}
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    if _capturing is not None and _capturing():
+        return torch.empty(nbytes, dtype=torch.uint8, device=device)
+    key = (device.index, stream)
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WS[key] = ws
+    return ws
+
+
+# Host arrays for the per-group problem description, reused per group count
+# (the C ABI reads them during the call only).
+_SCRATCH: dict = {}
+
+
+def _scratch(G: int):
+    sc = _SCRATCH.get(G)
+    if sc is None:
+        sc = (np.empty(G, dtype=np.int32), np.empty(G, dtype=np.uint64),
+              np.empty(G, dtype=np.uint64))
+        _SCRATCH[G] = sc
+    return sc
 
 
 def _ptr_array(tensors) -> np.ndarray:
@@ -238,11 +283,11 @@ def _nvfp4_grouped(a_list, a_sf_list, b_list, b_sf_list, problem_sizes, alpha, p
     # One pass over the groups (decode calls carry hundreds), no per-group
     # views: byte dtypes are read through their data pointers as they are.
     ms = [0] * G
-    pa = np.empty(G, dtype=np.uint64)
-    psf = np.empty(G, dtype=np.uint64)
+    m_arr, pa, psf = _scratch(G)
     u8 = _U8_DTYPES
     for g in range(G):
-        a, s = a_list[g], a_sf_list[g]
+        a = a_list[g]
+        s = a_sf_list[g]
         sa = a.shape
         m = sa[0] if len(sa) == 2 else -1
         if ps is not None:
@@ -262,10 +307,13 @@ def _nvfp4_grouped(a_list, a_sf_list, b_list, b_sf_list, problem_sizes, alpha, p
         ms[g] = m
         pa[g] = a.data_ptr()
         psf[g] = s.data_ptr()
+    m_arr[:] = ms
     if alpha is None:
         alpha_t = torch.ones(G, dtype=torch.float32, device=dev)
     elif isinstance(alpha, torch.Tensor):
-        alpha_t = alpha.to(device=dev, dtype=torch.float32).contiguous()
+        alpha_t = alpha
+        if alpha_t.dtype != torch.float32 or alpha_t.device != dev or not alpha_t.is_contiguous():
+            alpha_t = alpha_t.to(device=dev, dtype=torch.float32).contiguous()
     else:
         alpha_t = torch.tensor([float(x) for x in alpha], dtype=torch.float32, device=dev)
     if alpha_t.numel() != G:
@@ -280,20 +328,25 @@ def _nvfp4_grouped(a_list, a_sf_list, b_list, b_sf_list, problem_sizes, alpha, p
           or out.device != dev):
         raise ValueError(f"out must be a contiguous bf16 [{total}, {n_out}] tensor on {dev}")
     L = _lib.lib()
-    m_arr = np.asarray(ms, dtype=np.int32)
     prob = _lib.FggNvfp4Problem(G, n, k, m_arr.ctypes.data, pa.ctypes.data, psf.ctypes.data,
                                 alpha_t.data_ptr(), out.data_ptr(),
                                 None if bidx is None else bidx.ctypes.data, len(b_list))
     nbytes = int(L.fgg_nvfp4_workspace_bytes(prob))
     if nbytes == 0:
         _lib.check(L.fgg_nvfp4_grouped_gemm(prob, None, None, 0, None), "nvfp4_grouped_gemm")
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     entry = L.fgg_nvfp4_grouped_gemm_silu_mul if silu_mul else L.fgg_nvfp4_grouped_gemm
-    with torch.cuda.device(dev):
-        _lib.check(entry(prob, pack.buf.data_ptr(), ws.data_ptr(), nbytes, _stream_ptr(dev)),
-                   "nvfp4_grouped_gemm")
+    if _is_current(dev):
+        stream = _stream_ptr(dev)
+        ws = _workspace(dev, stream, nbytes)
+        rc = entry(prob, pack.buf.data_ptr(), ws.data_ptr(), nbytes, stream)
+    else:
+        with torch.cuda.device(dev):
+            stream = _stream_ptr(dev)
+            ws = _workspace(dev, stream, nbytes)
+            rc = entry(prob, pack.buf.data_ptr(), ws.data_ptr(), nbytes, stream)
+    _lib.check(rc, "nvfp4_grouped_gemm")
     _last_ws = ws
-    return list(out.split(ms, dim=0))
+    return list(out.split_with_sizes(ms))
 
 
 class _MxPrepared:
@@ -346,9 +399,12 @@ def fp4_grouped_gemm(a: torch.Tensor, a_sf: torch.Tensor, b: torch.Tensor, b_sf:
     prep = _MX_PREP.get_or(key, lambda: _MxPrepared(
         torch.empty(nbytes, dtype=torch.uint8, device=dev), (a_sf, b_sf, m_indices)))
     prob.reuse_prepared = 1 if prep.ready else 0
-    with torch.cuda.device(dev):
-        _lib.check(L.fgg_mx_grouped_gemm(prob, prep.ws.data_ptr(), nbytes, _stream_ptr(dev)),
-                   "fp4_grouped_gemm")
+    if _is_current(dev):
+        rc = L.fgg_mx_grouped_gemm(prob, prep.ws.data_ptr(), nbytes, _stream_ptr(dev))
+    else:
+        with torch.cuda.device(dev):
+            rc = L.fgg_mx_grouped_gemm(prob, prep.ws.data_ptr(), nbytes, _stream_ptr(dev))
+    _lib.check(rc, "fp4_grouped_gemm")
     prep.ready = True
     _last_ws = prep.ws
     return c
@@ -367,21 +423,27 @@ def quantize_nvfp4(x: torch.Tensor, amax: torch.Tensor | None = None):
     if k % 16 != 0:
         raise ValueError(f"K={k} must be a multiple of 16")
     dev = x.device
+    if _is_current(dev):
+        return _quantize_on(x, amax, dev, rows, k)
+    with torch.cuda.device(dev):
+        return _quantize_on(x, amax, dev, rows, k)
+
+
+def _quantize_on(x, amax, dev, rows, k):
     dt = 0 if x.dtype == torch.float32 else 1
     L = _lib.lib()
-    with torch.cuda.device(dev):
-        s = _stream_ptr(dev)
-        if amax is None:
-            amax_t = torch.empty((), dtype=torch.float32, device=dev)
-            _lib.check(L.fgg_amax(x.data_ptr(), dt, x.numel(), amax_t.data_ptr(), s), "fgg_amax")
-        else:
-            amax_t = amax.to(device=dev, dtype=torch.float32).reshape(()).contiguous()
-        codes = torch.empty((rows, k // 2), dtype=torch.uint8, device=dev)
-        sf = torch.empty((rows, k // 16), dtype=torch.uint8, device=dev)
-        g = torch.empty((), dtype=torch.float32, device=dev)  # written by the kernel
-        _lib.check(L.fgg_nvfp4_quantize(x.data_ptr(), dt, rows, k, amax_t.data_ptr(),
-                                        codes.data_ptr(), sf.data_ptr(), g.data_ptr(), s),
-                   "fgg_nvfp4_quantize")
+    s = _stream_ptr(dev)
+    if amax is None:
+        amax_t = torch.empty((), dtype=torch.float32, device=dev)
+        _lib.check(L.fgg_amax(x.data_ptr(), dt, x.numel(), amax_t.data_ptr(), s), "fgg_amax")
+    else:
+        amax_t = amax.to(device=dev, dtype=torch.float32).reshape(()).contiguous()
+    codes = torch.empty((rows, k // 2), dtype=torch.uint8, device=dev)
+    sf = torch.empty((rows, k // 16), dtype=torch.uint8, device=dev)
+    g = torch.empty((), dtype=torch.float32, device=dev)  # written by the kernel
+    _lib.check(L.fgg_nvfp4_quantize(x.data_ptr(), dt, rows, k, amax_t.data_ptr(),
+                                    codes.data_ptr(), sf.data_ptr(), g.data_ptr(), s),
+               "fgg_nvfp4_quantize")
     return codes, sf.view(torch.float8_e4m3fn), g
 
 
