@@ -31,7 +31,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 from pathlib import Path
 
@@ -63,6 +62,11 @@ def workload(name: str, seed: int = 0) -> dict:
                     "gate+up N=4096 (I=2048) K=7168 with the SiLU*up epilogue, NVFP4 "
                     "quantisation of the intermediate, down N=7168 K=2048",
                     m=ms, n=2 * 2048, k=7168, inter=2048, w_std=1.0, bound="tensor")
+    if name == "mx":
+        return dict(name="mx", desc="the reference operator fp4_grouped_gemm (MXFP8 x MXFP4) at "
+                    "its campaign point: 8 experts x 4096 rows (segments padded to 224, "
+                    "M_total=34048), N=K=4096", m=[4096] * 8, n=4096, k=4096, w_std=1.0,
+                    bound="tensor", ref_us=375.6)
     if name == "decode":
         ms = [int(v) for v in rng.integers(1, 17, size=256)]
         return dict(name="decode", desc="256 groups, M_g~U[1,16] seed 0, N=7168, K=2048",
@@ -98,10 +102,31 @@ def peaks() -> dict:
     return {"bf16": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "src": "fallback"}
 
 
+_SAMPLER_SRC = r"""
+import json, select, sys, time
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByUUID(sys.argv[1])
+print("ready", flush=True)
+out, err = [], None
+while not select.select([sys.stdin], [], [], 0)[0]:
+    try:
+        out.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                    pynvml.nvmlDeviceGetCurrentClocksEventReasons(h),
+                    pynvml.nvmlDeviceGetPowerUsage(h)))
+    except Exception as e:
+        err = str(e)
+        break
+    time.sleep(0.001)
+print(json.dumps({"samples": out, "err": err}), flush=True)
+"""
+
+
 class ClockSampler:
     """SM clock, power and throttle reasons sampled through NVML (the source
-    nvidia-smi reads) every ~1 ms on a thread while the timed region runs.
-    The GPU is found by UUID, so CUDA_VISIBLE_DEVICES remapping is harmless."""
+    nvidia-smi reads) every ~1 ms while the timed region runs.  The sampler is
+    a child process, so the timed loop's Python work cannot starve it.  The
+    GPU is found by UUID, so CUDA_VISIBLE_DEVICES remapping is harmless."""
 
     REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
                ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
@@ -111,57 +136,58 @@ class ClockSampler:
 
     def __init__(self, device: int):
         self.device = device
-        self.samples: list[tuple[int, int, int]] = []
         self.err = None
         self.nv = None
         self.max_mhz = None
+        self.proc = None
         try:
             import pynvml
 
             pynvml.nvmlInit()
             uuid = str(torch.cuda.get_device_properties(device).uuid)
-            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            h = pynvml.nvmlDeviceGetHandleByUUID(self.uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
             self.nv = pynvml
         except Exception as e:  # no NVML: report why instead of clocks
             self.err = f"nvml unavailable: {e}"
 
     def start(self):
-        self.stop_flag = threading.Event()
         if self.nv is None:
             return
-        self.t = threading.Thread(target=self._run, daemon=True)
-        self.t.start()
+        import subprocess
 
-    def _run(self):
-        nv, h = self.nv, self.h
-        while not self.stop_flag.is_set():
-            try:
-                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
-                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h),
-                                     nv.nvmlDeviceGetPowerUsage(h)))
-            except Exception as e:
-                self.err = str(e)
-                return
-            time.sleep(0.001)
+        self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_SRC, self.uuid],
+                                     stdin=subprocess.PIPE, stdout=subprocess.PIPE, text=True)
+        if self.proc.stdout.readline().strip() != "ready":
+            self.err = "clock sampler did not start"
+            self.proc.kill()
+            self.proc = None
 
     def stop(self) -> dict:
-        self.stop_flag.set()
-        if self.nv is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+        samples = []
+        if self.proc is not None:
+            try:
+                out, _ = self.proc.communicate(input="x", timeout=30)
+                d = json.loads(out.strip().splitlines()[-1])
+                samples = d["samples"]
+                self.err = d["err"] or self.err
+            except Exception as e:
+                self.proc.kill()
+                self.err = f"clock sampler failed: {e}"
+        if self.nv is None or not samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
                     "note": self.err}
-        self.t.join(timeout=5)
         reasons = set()
-        for _, bits, _ in self.samples:
+        for _, bits, _ in samples:
             for name, attr in self.REASONS:
                 if bits & getattr(self.nv, attr, 0):
                     reasons.add(name)
-        sm = [c for c, _, _ in self.samples]
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(reasons), "samples": len(sm),
-                "power_w_max": max(p for _, _, p in self.samples) / 1000.0 if sm else None,
-                "source": "NVML, ~1 ms polling during the timed region"}
+        sm = [c for c, _, _ in samples]
+        return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm),
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(p for _, _, p in samples) / 1000.0,
+                "source": "NVML in a child process, ~1 ms polling during the timed region"}
 
 
 def dist_init():
@@ -394,6 +420,47 @@ def cpu_sample(wl, budget_s: float = 10.0, seed: int = 1234):
                       f"K={k}): torch-CPU dequantise + fp32 matmul + bf16, {t_total:.1f} s timed"}
 
 
+def mx_inputs(wl, dev, seed: int = 0):
+    """The MX campaign inputs in the reference's layout: per-expert row
+    segments padded to 224 rows (m_indices = -1 on padding), E4M3 activations
+    with power-of-two 1x128 scales, packed E2M1 weights with 1x32 scales."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    n, k, G = wl["n"], wl["k"], len(wl["m"])
+    idx = []
+    for e, r in enumerate(wl["m"]):
+        idx += [e] * r + [-1] * ((-r) % 224)
+    m_total = len(idx)
+    mi = torch.tensor(idx, dtype=torch.int32, device=dev)
+    a = torch.randint(0, 256, (m_total, k), dtype=torch.uint8, device=dev, generator=gen)
+    a = torch.where((a & 0x7F) == 0x7F, a ^ 1, a).view(torch.float8_e4m3fn)  # no NaN codes
+    a_sf = torch.exp2(torch.randint(-3, 4, (m_total, k // 128), device=dev, generator=gen).float())
+    b = torch.randint(0, 256, (G, n, k // 2), dtype=torch.uint8, device=dev, generator=gen)
+    b_sf = torch.exp2(torch.randint(-4, 3, (G, n, k // 32), device=dev, generator=gen).float())
+    return a, a_sf, b, b_sf, mi
+
+
+def mx_cpu_sample(wl, budget_s: float = 10.0, seed: int = 1234):
+    """The MX oracle (oracle/mx.py) on a bounded sample: one expert segment
+    of 224 rows per step, dequantise + fp32 matmul + bf16 on the host cores."""
+    from oracle import mx as mref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    n, k = wl["n"], wl["k"]
+    prob = mref.random_problem([224], n, k, seed=seed)
+    t_total, f_total, done = 0.0, 0.0, 0
+    while t_total < budget_s and done < 64:
+        t0 = time.perf_counter()
+        mref.fp4_grouped_gemm(prob["a"], prob["a_sf"], prob["b"], prob["b_sf"], prob["m_indices"])
+        t_total += time.perf_counter() - t0
+        f_total += 2.0 * 224 * n * k
+        done += 1
+    return {"value": f_total / t_total / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{done} expert segments of 224 rows (N={n}, K={k}): numpy dequantise + "
+                      f"torch-CPU fp32 matmul + bf16, {t_total:.1f} s timed"}
+
+
 def _random_codes(rng, m, n, k):
     """Random NVFP4 codes and E4M3 scales (bytes 0x30..0x5F, values 0.75..28)."""
     qa = torch.from_numpy(rng.integers(0, 256, size=(m, k // 2), dtype=np.uint8))
@@ -419,6 +486,8 @@ def run_reference(args, wl):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    if wl["name"] == "mx":
+        return run_reference_mx(args, wl)
     from oracle import nvfp4 as ref
 
     torch.set_num_threads(os.cpu_count() or 1)
@@ -461,6 +530,107 @@ def run_reference(args, wl):
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_reference_mx(args, wl):
+    """The reference arm at the MX campaign point: the oracle's restatement of
+    kernel.py:2788 on the host cores, a bounded sample per step."""
+    from oracle import mx as mref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    n, k = wl["n"], wl["k"]
+    prob = mref.random_problem([224], n, k, seed=0)
+    step = lambda: mref.fp4_grouped_gemm(prob["a"], prob["a_sf"], prob["b"], prob["b_sf"],
+                                         prob["m_indices"])
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    val = 2.0 * 224 * n * k * args.steps / dt / 1e12
+    line = {
+        "impl": "reference", "metric": "grouped-GEMM TFLOPS", "value": val, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (dequantised MXFP8 x MXFP4)", "data": "synthetic",
+        "config": {"workload": wl["desc"], "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": "each step one expert segment of 224 rows: numpy dequantise "
+                                   "+ torch-CPU fp32 matmul + bf16"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_mx(args, wl):
+    """fp4_grouped_gemm, the reference's own operator, at its campaign point
+    (kernel.py:213, :286-288: 0.3756 ms on the reference's B200).  One GPU, or
+    independent replicas under torchrun.  A step is one call; the scale repack
+    is cached on tensor identity as the reference caches it, so a step is the
+    GEMM kernel."""
+    ws, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import ratchet_b200 as rb
+
+    a, a_sf, b, b_sf, mi = mx_inputs(wl, dev, seed=1000 * rank)
+    call = lambda: rb.fp4_grouped_gemm(a, a_sf, b, b_sf, mi)
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    rb.last_status()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws, dev)
+    fl = flops(wl)  # the 32768 real rows; padding rows are not counted
+    value = fl * ws / (ms * 1e-3) / 1e12
+    pk = peaks()
+    achieved = fl / (ms * 1e-3) / 1e12
+    peak = 2.0 * pk["bf16"]  # .kind::mxf8f6f4 runs at the FP8 rate, twice bf16
+    ref_value = fl / (wl["ref_us"] * 1e-6) / 1e12
+    if rank == 0:
+        line = {
+            "metric": "grouped-GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": achieved / ref_value,
+            "vs_baseline_basis": "the reference's published 0.3756 ms device time at this "
+                                 "config (kernels/gemm/fp4_grouped_gemm/b200/kernel.py:213, "
+                                 ":286), on its own B200",
+            "dtype": "mxf8f6f4 (e4m3 x e2m1, ue8m0 scales 1x128 / 1x32, fp32 acc, bf16 out)",
+            "data": "synthetic (seeded random E4M3 / E2M1 codes, power-of-two scales)",
+            "config": {"workload": wl["desc"], "m_total": int(a.shape[0]), "n": wl["n"],
+                       "k": wl["k"], "experts": len(wl["m"]), "parallelism": f"replicas x{ws}",
+                       "l2": "back-to-back calls on one 0.5 GB input set (> L2)"},
+            "clocks": clocks,
+            "e2e": None,
+            "gpu_launches": args.steps,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                         "peak_basis": f"2 x {pk['src']} dense bf16 ({pk['bf16']:.0f} TF/s)",
+                         "kernel_ms": ms, "kernel": "fgg_gemm_pair_kernel<PairCfg<MX>>"},
+            "cpu_baseline": (mx_cpu_sample(wl) if (ws == 1 and not args.no_cpu) else None),
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
     return 0
 
 
@@ -756,7 +926,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["grouped", "dense", "decode", "moe", "mlp"],
+    ap.add_argument("--config", choices=["grouped", "dense", "decode", "moe", "mlp", "mx"],
                     default="grouped")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
@@ -773,6 +943,8 @@ def main():
         return run_moe(args, wl)
     if wl["name"] == "mlp":
         return run_mlp(args, wl)
+    if wl["name"] == "mx":
+        return run_mx(args, wl)
     return run_ours(args, wl)
 
 

@@ -8,11 +8,11 @@
 // 16 (32 for pairs), and the epilogue's lanes walk consecutive output columns.
 //
 // Warp roles (256 threads, one CTA per SM):
-//   warp 0     producer: one thread issues the TMA loads of every K step into
-//              a STAGES-deep shared-memory ring
-//   warp 1     MMA issuer: one thread issues tcgen05.cp (scale factors ->
-//              TMEM) and the block-scaled tcgen05.mma chain into a
-//              double-buffered TMEM accumulator
+//   warp 0     producer: the TMA loads of every K step into a STAGES-deep
+//              shared-memory ring
+//   warp 1     MMA issuer: tcgen05.cp (scale factors -> TMEM) and the
+//              block-scaled tcgen05.mma chain into a double-buffered TMEM
+//              accumulator
 //   warp 2     TMEM allocator
 //   warp 3     scheduler: claims tiles from a global atomic counter (dynamic
 //              persistent schedule) and publishes each tile with its metadata
@@ -21,14 +21,18 @@
 //   warps 4-7  epilogue: tcgen05.ld (each warp its 32-lane quadrant) -> fp32
 //              x alpha -> bf16 -> global (or the gated SiLU * up form),
 //              overlapped with the next tile's MMAs
-// The producer and MMA roles run on ONE thread each: between two K steps they
-// only test a barrier.  Every TMA or tcgen05 instruction holds its issuing
-// thread for about 60 cycles, so these two threads set the kernel's pace; the
-// layouts keep their instruction counts down (scale factors in the replicated
-// layout one 128x256b copy uploads, KSUB K steps per stage behind one barrier
-// test and one commit).  Every wait suspends in hardware (try_wait with a
-// time hint) so waiting warps do not steal issue slots from the MMA thread,
-// and the epilogue keeps its instruction stream short for the same reason.
+// The producer and MMA roles run their loops on the whole warp, so that every
+// operand of a TMA or tcgen05 instruction (smem descriptors, TMEM columns,
+// coordinates) is computed warp-uniformly, and issue from one elect.sync
+// region per stage.  Issued that way a 32x128b.warpx4 scale copy costs the
+// issuing thread under 10 cycles; from a lone lane with per-thread operands
+// each TMA or tcgen05 instruction held it for 45-60, which bounded the kernel.
+// Scale factors therefore travel as plain 512-byte atoms, one small copy each
+// (a 128x256b copy would take one instruction for two atoms, but costs the
+// tensor pipe 50-64 cycles that do not overlap the MMAs).  Every wait
+// suspends in hardware (try_wait with a time hint) so waiting warps do not
+// steal issue slots, and the epilogue keeps its instruction stream short for
+// the same reason.
 //
 // Two kernels:
 //   fgg_gemm_kernel       one CTA per tile, 128 weight rows x BN tokens
@@ -36,8 +40,7 @@
 //                         CTA loads half of the token tile
 // Two kinds (compile-time):
 //   NVFP4   .kind::mxf4nvf4 .scale_vec::4X: E2M1 x E2M1, one E4M3 scale per 16
-//           K; K step 256 = 4 MMAs of K 64, one SF slot per MMA (per MMA pair
-//           where one copy uploads the scales of two MMAs).
+//           K; K step 256 = 4 MMAs of K 64, one SF slot per MMA.
 //   MX      .kind::mxf8f6f4: weights E2M1 (4-bit codes unpacked to bytes by
 //           TMA), tokens E4M3, one UE8M0 scale per 32 K; K step 128 = 4 MMAs of
 //           K 32 that share one SF slot and pick their byte with the SF id.

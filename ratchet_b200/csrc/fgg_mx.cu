@@ -25,7 +25,7 @@ namespace {
 constexpr int kMxBlockM = 224;  // token tile = the reference's ALIGN (kernel.py:274)
 
 using CfgMx = EngineCfg<true, kMxBlockM, 4>;  // one CTA per tile (N % 256 != 0)
-using CfgMxPair = PairCfg<true, 6>;          // CTA pairs, 256 x 224 tiles
+using CfgMxPair = PairCfg<true, 7>;          // CTA pairs, 256 x 224 tiles
 
 struct MxPrepParams {
   const float* a_sf;        // [M_total, K/128]

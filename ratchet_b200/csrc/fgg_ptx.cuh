@@ -116,9 +116,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   return true;
 }
 
-// Bounded wait executed by ONE thread (the producer and MMA roles run on a
-// single elected lane so that nothing but the barrier test sits between two
-// K steps).  Checks the clock and the abort word after every poll.
+// Bounded wait executed by ONE thread (the tile scheduler, which runs on a
+// single lane).  Checks the clock and the abort word after every poll.
 template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait1(uint32_t bar, uint32_t parity,
                                            volatile int* abort_flag, int* status, int code) {
