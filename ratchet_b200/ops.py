@@ -67,7 +67,8 @@ def _is_current(device: torch.device) -> bool:
 # the next call's prepare kernel (which waits for the previous GEMM before it
 # touches memory) may overwrite the previous call's workspace.  Not used while
 # the stream is being captured into a CUDA graph (the graph keeps its own).
-_WS: dict = {}
+_WS: OrderedDict = OrderedDict()
+_WS_MAX = 8
 
 
 def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
@@ -78,6 +79,10 @@ def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WS[key] = ws
+        while len(_WS) > _WS_MAX:  # the oldest stream's buffer returns to torch's allocator
+            _WS.popitem(last=False)
+    else:
+        _WS.move_to_end(key)
     return ws
 
 

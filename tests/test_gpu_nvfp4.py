@@ -123,6 +123,32 @@ def test_repeat_calls_bitwise_identical(cuda_device):
         assert torch.equal(x, y)
 
 
+def test_streams_and_workspace_reuse(cuda_device):
+    """Back-to-back calls of different shapes on two streams, no host sync in
+    between: each (device, stream) reuses one workspace, so every call must
+    see only its own tile list and scales."""
+    import ratchet_b200 as rb
+
+    probs = [ref.random_problem([300, 17, 64], 512, 1024, seed=21),
+             ref.random_problem([5, 230], 256, 512, seed=22),
+             ref.random_problem([9, 16, 3, 12], 256, 768, seed=23)]
+    dev_inputs = [_dev_problem(p, cuda_device) for p in probs]
+    streams = [torch.cuda.Stream(cuda_device), torch.cuda.Stream(cuda_device)]
+    torch.cuda.synchronize()
+    outs = []
+    for rep in range(3):
+        for i, (p, (a, a_sf, b, b_sf, alpha)) in enumerate(zip(probs, dev_inputs)):
+            with torch.cuda.stream(streams[(i + rep) % 2]):
+                outs.append((i, rb.nvfp4_grouped_gemm(a, a_sf, b, b_sf, None, alpha)))
+    torch.cuda.synchronize()
+    rb.last_status()
+    refs = [ref.grouped_gemm(p["a"], p["a_sf"], p["b"], p["b_sf"], p["alpha"]) for p in probs]
+    for i, o in outs:
+        for g, (x, r) in enumerate(zip(o, refs[i])):
+            ok, st = ref.check_close(x.cpu(), r)
+            assert ok, f"problem {i} group {g}: {st}"
+
+
 def test_alpha_applied_per_group(cuda_device):
     import ratchet_b200 as rb
 
