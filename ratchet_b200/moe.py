@@ -148,6 +148,7 @@ class ExpertParallelMoE:
         self.pack = None
         self.bad = None
         self.ws = None
+        self._host_counts = None  # pinned landing buffer of the per-forward count exchange
         if gemm_fn is None:
             # the product path: weights packed once and reused by every
             # forward; the gather / combine kernels raise this flag on an
@@ -196,7 +197,7 @@ class ExpertParallelMoE:
         W, E = self.world, self.local
         S = T * topk
         L = _lib.lib() if self.gemm_fn is None else None
-        stream = torch.cuda.current_stream(dev).cuda_stream if L is not None else None
+        stream = ops._stream_ptr(dev) if L is not None else None
         # 1. plan
         if L is not None:
             ids32 = topk_ids.to(dev, torch.int32).contiguous()
@@ -220,8 +221,21 @@ class ExpertParallelMoE:
         else:
             recv_info = torch.empty_like(info)
             self._a2a(recv_info, info)
-        # 3. the rows in (owner, slot) order: launched before the host waits
-        #    for the counts, so the device gathers while the host syncs
+        # the counts travel to the host ahead of the row gather: the host waits
+        # for this copy alone (one host sync per forward) and plans the GEMM
+        # while the device still gathers
+        both_d = torch.stack([info, recv_info])
+        counts_ready = None
+        if both_d.is_cuda:
+            if self._host_counts is None or self._host_counts.shape != both_d.shape:
+                self._host_counts = torch.empty(both_d.shape, dtype=torch.int32, pin_memory=True)
+            both = self._host_counts
+            both.copy_(both_d, non_blocking=True)
+            counts_ready = torch.cuda.Event()
+            counts_ready.record()
+        else:
+            both = both_d
+        # 3. the rows in (owner, slot) order
         if L is not None:
             send_codes = torch.empty((S, kh), dtype=torch.uint8, device=dev)
             send_sf = torch.empty((S, ks), dtype=torch.uint8, device=dev)
@@ -233,11 +247,17 @@ class ExpertParallelMoE:
             rows = order // topk
             send_codes = x_u8.index_select(0, rows)
             send_sf = s_u8.index_select(0, rows)
-        both = torch.stack([info, recv_info]).cpu()  # one host sync per forward
+        # alpha of problem group (source, slot) = source's activation scale x
+        # the slot's weight scale: device work, queued before the host waits
+        src_scale = recv_info[:, E].contiguous().view(torch.float32)
+        alpha = (src_scale[:, None] * self.w_scale[None, :]).reshape(-1).contiguous()
+        # on one rank every route stays: the GEMM output size is known up front
+        out = torch.empty((S, self.n), dtype=torch.bfloat16, device=dev) if W == 1 else None
+        if counts_ready is not None:
+            counts_ready.synchronize()
         send_ce, recv_ce = both[0, :, :E], both[1, :, :E]
         send_splits = send_ce.sum(1).tolist()
         recv_splits = recv_ce.sum(1).tolist()
-        src_scale = recv_info[:, E].contiguous().view(torch.float32)
         R = int(sum(recv_splits))
         if W == 1:  # nothing leaves the rank
             recv_codes, recv_sf = send_codes, send_sf
@@ -247,8 +267,8 @@ class ExpertParallelMoE:
             self._a2a(recv_codes, send_codes, recv_splits, send_splits)
             self._a2a(recv_sf, send_sf, recv_splits, send_splits)
         # 4. grouped GEMM over the (source, slot) chunks
-        alpha = (src_scale[:, None] * self.w_scale[None, :]).reshape(-1).contiguous()
-        out = torch.empty((R, self.n), dtype=torch.bfloat16, device=dev)
+        if out is None:
+            out = torch.empty((R, self.n), dtype=torch.bfloat16, device=dev)
         if gemm_events is not None:
             gemm_events[0].record()
         if L is not None:
