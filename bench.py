@@ -920,7 +920,18 @@ def run_mlp(args, wl):
     return 0
 
 
+def _one_line_stdout():
+    """Keep the process's stdout for the JSON line alone: file descriptor 1
+    (where native libraries print, e.g. NCCL's version banner) goes to stderr,
+    and Python's print writes to the original stdout."""
+    real = os.dup(1)
+    sys.stdout.flush()
+    os.dup2(2, 1)
+    sys.stdout = os.fdopen(real, "w", buffering=1)
+
+
 def main():
+    _one_line_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
