@@ -38,6 +38,7 @@ struct PrepParams {
   int* status;
   int32_t g, k, bn, ch, nk64p, nt, num_tiles, xt_total;
   int32_t blocks_tmap, blocks_tiles;
+  int32_t across_groups;  // tile order: 1 weight-tile-major over all groups, 0 group-major
 };
 
 __device__ __forceinline__ int find_group(const int32_t* begin, int g_count, int x) {
@@ -92,14 +93,32 @@ __global__ void __launch_bounds__(256)
   }
   blk -= p.blocks_tmap;
   if (blk < p.blocks_tiles) {
-    for (int i = threadIdx.x; i <= p.g; i += blockDim.x) sbegin[i] = p.tile_begin[i];
-    __syncthreads();
-    const int t = blk * blockDim.x + threadIdx.x;
-    if (t < p.num_tiles) {
-      const int g = find_group(sbegin, p.g, t);
-      const int local = t - sbegin[g];
-      const int xts = p.xtile_begin[g + 1] - p.xtile_begin[g];
-      p.tiles_out[t] = pack_tile(g, local / xts, local % xts);
+    if (p.across_groups) {
+      // Weight-tile-major over all groups: tile t pairs weight tile
+      // t / xt_total with token tile t % xt_total of the groups' concatenated
+      // token tiles.  The tiles running at any moment span every group, so
+      // the groups whose weights serve one token tile (read from DRAM for it
+      // alone) spread over the whole kernel instead of gathering at its end.
+      for (int i = threadIdx.x; i <= p.g; i += blockDim.x) sbegin[i] = p.xtile_begin[i];
+      __syncthreads();
+      const int t = blk * blockDim.x + threadIdx.x;
+      if (t < p.num_tiles) {
+        const int nti = t / p.xt_total;
+        const int X = t - nti * p.xt_total;
+        const int g = find_group(sbegin, p.g, X);
+        p.tiles_out[t] = pack_tile(g, nti, X - sbegin[g]);
+      }
+    } else {
+      // group-major: each group's weight tiles in turn, its token tiles fastest
+      for (int i = threadIdx.x; i <= p.g; i += blockDim.x) sbegin[i] = p.tile_begin[i];
+      __syncthreads();
+      const int t = blk * blockDim.x + threadIdx.x;
+      if (t < p.num_tiles) {
+        const int g = find_group(sbegin, p.g, t);
+        const int local = t - sbegin[g];
+        const int xts = p.xtile_begin[g + 1] - p.xtile_begin[g];
+        p.tiles_out[t] = pack_tile(g, local / xts, local % xts);
+      }
     }
     return;
   }
@@ -210,6 +229,10 @@ static PackLayout pack_layout(int g, int n, int k) {
   return L;
 }
 
+// activation bytes up to which the tile list runs weight-tile-major over all
+// groups (a quarter of the 126 MB L2: the weights in flight need the rest)
+constexpr int64_t kAcrossGroupsMaxBytes = 32ll << 20;
+
 struct WsLayout {
   int bn = 0, ch = 0, stages = 0;
   bool pair = false;
@@ -221,6 +244,13 @@ struct WsLayout {
   int32_t tile_begin[FGG_MAX_GROUPS + 1];
   int32_t out_row[FGG_MAX_GROUPS];
   int wg = 0;  // weight groups the problem groups index into
+  // Tile order.  Weight-tile-major over all groups re-reads every token tile
+  // once per weight tile, which pays while the activations stay in L2 (they
+  // are re-read from there) and spreads the single-use weights of small groups
+  // over the kernel; with more activation bytes than kAcrossGroupsMaxBytes the
+  // order stays group-major, so a group's token tiles share each weight tile
+  // while it is hot.  Decode tiles stream their weights once in either order.
+  bool across_groups = false;
   size_t status = 0, tmaps = 0, ginfo = 0, tiles = 0, sfx = 0, total = 0;
 };
 
@@ -276,6 +306,8 @@ static int plan(const FggNvfp4Problem* p, WsLayout* L) {
   }
   if (rows > INT32_MAX || tiles > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
   L->xtile_begin[G] = int32_t(xts);
+  L->across_groups = !decode && G > 1 &&
+                     rows * (p->k / 2 + p->k / 16) <= int64_t(kAcrossGroupsMaxBytes);
   L->tile_begin[G] = int32_t(tiles);
   L->num_tiles = int(tiles);
   L->xt_total = int(xts);
@@ -421,6 +453,7 @@ int prepare_launch(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8
   pp.xt_total = L.xt_total;
   pp.blocks_tmap = (G + 7) / 8;
   pp.blocks_tiles = (L.num_tiles + 255) / 256;
+  pp.across_groups = L.across_groups ? 1 : 0;
   const int64_t sf_lines = int64_t(L.xt_total) * L.nk64p * L.ch * 32;
   const int64_t blocks = int64_t(pp.blocks_tmap) + pp.blocks_tiles + (sf_lines + 255) / 256;
   if (blocks > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
