@@ -693,8 +693,9 @@ def run_ours(args, wl):
                        "n": wl["n"], "k": wl["k"], "parallelism": f"replicas x{ws}",
                        "l2": f"{R} rotating input sets of {per_set / 1e6:.0f} MB (> L2 in total)"},
             "clocks": clocks,
-            "e2e": {"value": fl * ws / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "e2e": None if args.no_e2e else {
+                "value": fl * ws / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "gpu_launches": 2 * args.steps,
             "roofline": roof,
             "cpu_baseline": cpu,
