@@ -38,7 +38,8 @@ struct PrepParams {
   int* status;
   int32_t g, k, bn, ch, nk64p, nt, num_tiles, xt_total;
   int32_t blocks_tmap, blocks_tiles;
-  int32_t across_groups;  // tile order: 1 weight-tile-major over all groups, 0 group-major
+  int32_t across_groups;
+  int32_t sf_vec;  // 1: K % 256 == 0 and every a_sf[g] 16-byte aligned (vector repack)  // tile order: 1 weight-tile-major over all groups, 0 group-major
 };
 
 __device__ __forceinline__ int find_group(const int32_t* begin, int g_count, int x) {
@@ -123,10 +124,44 @@ __global__ void __launch_bounds__(256)
     return;
   }
   blk -= p.blocks_tiles;
-  // Token scales -> SF atoms.  One thread writes one 16-byte atom row:
+  // Token scales -> SF atoms:
   //   atom byte (r % 32) * 16 + (r / 32) * 4 + b  <-  sf[row r][4 j + b]
   for (int i = threadIdx.x; i <= p.g; i += blockDim.x) sbegin[i] = p.xtile_begin[i];
   __syncthreads();
+  if (p.sf_vec) {
+    // K % 256 == 0 and 16-byte aligned scale rows: one thread loads 16 bytes
+    // (the scales of one K step of 4 MMAs) from each of its 4 rows and writes
+    // the 16-byte atom row of every MMA of that K step.
+    const int64_t quad = int64_t(blk) * blockDim.x + threadIdx.x;
+    const int nk256 = p.nk64p / 4;
+    const int64_t quads_per_xt = int64_t(nk256) * p.ch * 32;
+    if (quad >= int64_t(p.xt_total) * quads_per_xt) return;
+    const int X = int(quad / quads_per_xt);
+    const int rem = int(quad - int64_t(X) * quads_per_xt);
+    const int s4 = rem / (p.ch * 32);
+    const int c = (rem / 32) % p.ch;
+    const int r0 = rem & 31;
+    const int g = find_group(sbegin, p.g, X);
+    const int xt = X - sbegin[g];
+    const int kq = p.k / 16;
+    uint4 v[4];
+#pragma unroll
+    for (int r1 = 0; r1 < 4; ++r1) {
+      const int rr = c * 128 + r1 * 32 + r0;
+      const int row = xt * p.bn + rr;
+      v[r1] = make_uint4(0u, 0u, 0u, 0u);
+      if (rr < p.bn && row < p.m[g])
+        v[r1] = __ldg(reinterpret_cast<const uint4*>(p.a_sf[g] + size_t(row) * kq + 16 * s4));
+    }
+    uint8_t* dst = p.sfx_out + ((size_t(X) * p.nk64p + 4 * s4) * p.ch + c) * 512u + size_t(r0) * 16u;
+    const size_t jstride = size_t(p.ch) * 512u;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(v[0].x, v[1].x, v[2].x, v[3].x);
+    *reinterpret_cast<uint4*>(dst + jstride) = make_uint4(v[0].y, v[1].y, v[2].y, v[3].y);
+    *reinterpret_cast<uint4*>(dst + 2 * jstride) = make_uint4(v[0].z, v[1].z, v[2].z, v[3].z);
+    *reinterpret_cast<uint4*>(dst + 3 * jstride) = make_uint4(v[0].w, v[1].w, v[2].w, v[3].w);
+    return;
+  }
+  // general case: one thread writes one 16-byte atom row
   const int64_t line = int64_t(blk) * blockDim.x + threadIdx.x;
   const int64_t lines_per_xt = int64_t(p.nk64p) * p.ch * 32;
   if (line >= int64_t(p.xt_total) * lines_per_xt) return;
@@ -454,7 +489,12 @@ int prepare_launch(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8
   pp.blocks_tmap = (G + 7) / 8;
   pp.blocks_tiles = (L.num_tiles + 255) / 256;
   pp.across_groups = L.across_groups ? 1 : 0;
-  const int64_t sf_lines = int64_t(L.xt_total) * L.nk64p * L.ch * 32;
+  bool vec = p->k % 256 == 0;
+  for (int g = 0; g < G && vec; ++g)
+    vec = p->m[g] == 0 || aligned16(p->a_sf[g]);
+  pp.sf_vec = vec ? 1 : 0;
+  // threads of the scale repack: one per atom row, or per 4 atom rows (vector)
+  const int64_t sf_lines = int64_t(L.xt_total) * L.nk64p * L.ch * 32 / (vec ? 4 : 1);
   const int64_t blocks = int64_t(pp.blocks_tmap) + pp.blocks_tiles + (sf_lines + 255) / 256;
   if (blocks > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
   FGG_CUDA_CHECK(launch_dependent(nvfp4_prepare_kernel<CAP>, int(blocks), 0, s, pp));
