@@ -149,6 +149,32 @@ def test_streams_and_workspace_reuse(cuda_device):
             assert ok, f"problem {i} group {g}: {st}"
 
 
+def test_scale_rows_not_16_byte_aligned(cuda_device):
+    """K % 256 == 0 normally takes the prepare kernel's 16-byte scale loads;
+    scale tensors that start 4 bytes into a buffer must take the 4-byte path
+    and give the same results."""
+    import ratchet_b200 as rb
+
+    prob = ref.random_problem([200, 37, 5], 256, 512, seed=31)
+    a, a_sf, b, b_sf, alpha = _dev_problem(prob, cuda_device)
+    shifted = []
+    for s in a_sf:
+        raw = torch.empty(s.numel() + 4, dtype=torch.uint8, device=cuda_device)
+        view = raw[4:].view(s.shape)
+        view.copy_(s.view(torch.uint8))
+        assert view.data_ptr() % 16 == 4
+        shifted.append(view.view(torch.float8_e4m3fn))
+    outs = rb.nvfp4_grouped_gemm(a, shifted, b, b_sf, None, alpha)
+    rb.last_status()
+    refs = ref.grouped_gemm(prob["a"], prob["a_sf"], prob["b"], prob["b_sf"], prob["alpha"])
+    for g, (o, r) in enumerate(zip(outs, refs)):
+        ok, st = ref.check_close(o.cpu(), r)
+        assert ok, f"group {g}: {st}"
+    aligned = rb.nvfp4_grouped_gemm(a, a_sf, b, b_sf, None, alpha)
+    for x, y in zip(outs, aligned):
+        assert torch.equal(x, y)
+
+
 def test_alpha_applied_per_group(cuda_device):
     import ratchet_b200 as rb
 
