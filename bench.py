@@ -117,7 +117,7 @@ while not select.select([sys.stdin], [], [], 0)[0]:
     except Exception as e:
         err = str(e)
         break
-    time.sleep(0.001)
+    time.sleep(0.0002)
 print(json.dumps({"samples": out, "err": err}), flush=True)
 """
 
@@ -707,6 +707,37 @@ def run_ours(args, wl):
         dist.destroy_process_group()
     return 0
 
+def moe_setup(wl, ws: int, rank: int, dev) -> dict:
+    """Config 3's seeded inputs for one rank of an ws-way expert-parallel run:
+    Zipf(1.1) top-8 routing of all tokens (seed 0), LPT placement of the
+    experts, this rank's experts' weights (each drawn from its own seed, so
+    they do not depend on ws) and this rank's share of the tokens, quantised
+    to NVFP4 on the device."""
+    import ratchet_b200 as rb
+    from ratchet_b200 import moe
+
+    T, E, topk, n, k = wl["tokens"], wl["experts"], wl["topk"], wl["n"], wl["k"]
+    tl = T // ws
+    ids_all, w_all = moe.zipf_routing(T, E, topk, s=1.1, seed=0)
+    owner, slot = moe.place_experts(moe.expert_popularity(E, s=1.1, seed=0), ws)
+    mine = sorted(np.flatnonzero(owner == rank).tolist(), key=lambda e: slot[e])
+    wc, wsf, wg = [], [], []
+    for e in mine:
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(7000 + e)
+        q, sf, g = rb.quantize_nvfp4(torch.randn((n, k), generator=gen, device=dev))
+        wc.append(q)
+        wsf.append(sf)
+        wg.append(g)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(9000 + rank)
+    xc, xs, xg = rb.quantize_nvfp4(torch.randn((tl, k), generator=gen, device=dev))
+    ids = torch.from_numpy(ids_all[rank * tl:(rank + 1) * tl]).to(dev)
+    wts = torch.from_numpy(w_all[rank * tl:(rank + 1) * tl]).to(dev)
+    return dict(tl=tl, ids_all=ids_all, w_all=w_all, owner=owner, slot=slot, mine=mine,
+                wc=wc, wsf=wsf, wg=wg, xc=xc, xs=xs, xg=xg, ids=ids, wts=wts)
+
+
 def run_moe(args, wl):
     """one expert-parallel MoE projection over N ranks.
     The 4096 tokens are split evenly over the ranks (each rank routes its own
@@ -724,24 +755,10 @@ def run_moe(args, wl):
     T, E, topk, n, k = wl["tokens"], wl["experts"], wl["topk"], wl["n"], wl["k"]
     if T % ws or E % ws:
         raise SystemExit(f"--gpus {ws} must divide {T} tokens and {E} experts")
-    tl = T // ws
-    ids_all, w_all = moe.zipf_routing(T, E, topk, s=1.1, seed=0)
-    owner, slot = moe.place_experts(moe.expert_popularity(E, s=1.1, seed=0), ws)
-    mine = sorted(np.flatnonzero(owner == rank).tolist(), key=lambda e: slot[e])
-    wc, wsf, wg = [], [], []
-    for e in mine:  # each expert's weights depend only on its id, not on N
-        gen = torch.Generator(device=dev)
-        gen.manual_seed(7000 + e)
-        q, sf, g = rb.quantize_nvfp4(torch.randn((n, k), generator=gen, device=dev))
-        wc.append(q)
-        wsf.append(sf)
-        wg.append(g)
-    layer = moe.ExpertParallelMoE(wc, wsf, wg, owner, slot)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(9000 + rank)
-    xc, xs, xg = rb.quantize_nvfp4(torch.randn((tl, k), generator=gen, device=dev))
-    ids = torch.from_numpy(ids_all[rank * tl:(rank + 1) * tl]).to(dev)
-    wts = torch.from_numpy(w_all[rank * tl:(rank + 1) * tl]).to(dev)
+    d = moe_setup(wl, ws, rank, dev)
+    tl, ids_all, mine = d["tl"], d["ids_all"], d["mine"]
+    xc, xs, xg, ids, wts = d["xc"], d["xs"], d["xg"], d["ids"], d["wts"]
+    layer = moe.ExpertParallelMoE(d["wc"], d["wsf"], d["wg"], d["owner"], d["slot"])
     torch.cuda.synchronize()
     fl = 2.0 * T * topk * n * k
 

@@ -144,8 +144,9 @@ FGG_API int fgg_nvfp4_gemm(const FggNvfp4Problem* p, const void* pack, void* wor
  * fixed memory budget, or a host without an allocator on the call path.  The
  * call runs the same kernels with its scratch in a fixed device array inside
  * this library (FGG_NOALLOC_SCRATCH_BYTES per device) instead of a caller
- * workspace; it allocates nothing: no cudaMalloc / cudaFree and no allocating
- * library call, and its host-side bookkeeping lives in fixed arrays.
+ * workspace; after its set-up (below) it allocates nothing: no cudaMalloc /
+ * cudaFree and no allocating library call, and its host-side bookkeeping
+ * lives in fixed arrays.
  *   - Limit: a problem whose fgg_nvfp4_workspace_bytes exceeds
  *     FGG_NOALLOC_SCRATCH_BYTES is refused with FGG_EWORKSPACE before any
  *     device work (use fgg_nvfp4_grouped_gemm with a caller workspace).
@@ -156,10 +157,16 @@ FGG_API int fgg_nvfp4_gemm(const FggNvfp4Problem* p, const void* pack, void* wor
  *     whose device work overlaps in time (different streams, or host threads
  *     without ordering between them) corrupt each other.  Issue them on one
  *     stream, or order them with events.
- *   - The first call on each device performs one-time set-up (the scratch
- *     array's address via cudaGetSymbolAddress, which also loads its module,
- *     and the kernels' shared-memory attribute); make that first call before
- *     any stream capture.
+ *   - The first call on each device (more exactly, on each CUDA context: the
+ *     array's address belongs to the context that loaded it, so a context
+ *     created after cudaDeviceReset repeats this) performs one-time set-up:
+ *     the scratch array's address via cudaGetSymbolAddress, which also loads
+ *     its module and so reserves the array's device memory, and the kernels'
+ *     shared-memory attribute.  The first call on each host thread also sets
+ *     up that thread's parameter block (thread-local storage, which the C
+ *     library may allocate on a thread's first use).  Make one warm-up call
+ *     per device and per calling thread at initialisation, before any stream
+ *     capture; later calls allocate nothing.
  *   - status_out: optional device pointer to one int32; when non-null the call
  *     ends with a stream-ordered copy of the device status word there
  *     (0 = clean; non-zero = a bounded wait gave up), since the scratch that
@@ -269,6 +276,15 @@ FGG_API int fgg_nvfp4_quantize(const void* x, int32_t x_dtype, int64_t rows, int
  * (a device wait ran out; the kernel stopped early and its output is
  * incomplete) or FGG_ECUDA. */
 FGG_API int fgg_read_device_status(const void* workspace, void* stream);
+
+/* Test hook, no counterpart in the reference: flags applied to every GEMM
+ * launch until changed (process-wide).  FGG_DEBUG_NO_LOADS makes the
+ * producer arm no pipeline stage and issue no load, so the MMA role's bounded
+ * wait on its first stage runs out (after about one second) and the kernel
+ * ends early with a non-zero status word: a way to exercise the device error
+ * path without a fault.  Returns the previous flags.  0 in normal use. */
+#define FGG_DEBUG_NO_LOADS 1
+FGG_API int32_t fgg_debug_set_flags(int32_t flags);
 
 #ifdef __cplusplus
 }

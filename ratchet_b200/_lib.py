@@ -21,6 +21,7 @@ FGG_ETIMEOUT = 6
 FGG_EARCH = 7
 FGG_MAX_GROUPS = 512
 FGG_NOALLOC_SCRATCH_BYTES = 32 << 20
+FGG_DEBUG_NO_LOADS = 1
 
 _VOIDP = ctypes.c_void_p
 _PTRS = ctypes.POINTER(ctypes.c_void_p)
@@ -74,6 +75,7 @@ _SIGS = {
     "fgg_amax": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int64, _VOIDP, _VOIDP]),
     "fgg_nvfp4_quantize": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
     "fgg_read_device_status": (ctypes.c_int, [_VOIDP, _VOIDP]),
+    "fgg_debug_set_flags": (ctypes.c_int32, [ctypes.c_int32]),
 }
 
 _lock = threading.Lock()

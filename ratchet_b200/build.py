@@ -15,6 +15,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -58,13 +59,18 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
               "-I", str(ROOT / "include"), "--expt-relaxed-constexpr"]
     if ptxas_verbose:
         common += ["-Xptxas", "-v"]
+    jobs = []
     for src in _sources():
         obj = out_dir / (src.stem + ".o")
         cmd = common + ["-c", str(src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        jobs.append(cmd)
         objs.append(str(obj))
+    # one nvcc per translation unit, in parallel
+    with ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 1)) as pool:
+        for r in pool.map(lambda c: subprocess.run(c, check=True), jobs):
+            pass
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *objs, "-cudart", "static"]
     if verbose:

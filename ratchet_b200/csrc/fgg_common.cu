@@ -2,6 +2,7 @@
 // status read-back shared by all entry points.
 #include "fgg_host.cuh"
 
+#include <atomic>
 #include <mutex>
 
 namespace fgg {
@@ -26,7 +27,69 @@ void load_encoder() {
 
 DeviceInfo g_devs[64];
 std::mutex g_dev_mu;
+
+// Driver entry points for the current context and its unique id (fetched
+// through the runtime, like the tensor-map encoder).
+using PfnCtxGetCurrent = CUresult (*)(CUcontext*);
+using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long*);
+PfnCtxGetCurrent g_ctx_current = nullptr;
+PfnCtxGetId g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
+
+void load_ctx_entry_points() {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+  if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_ctx_current = reinterpret_cast<PfnCtxGetCurrent>(fn);
+  fn = nullptr;
+  if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_ctx_id = reinterpret_cast<PfnCtxGetId>(fn);
+}
+
+// Kernels whose dynamic shared-memory limit was raised, per context.
+struct AttrEntry {
+  const void* func = nullptr;
+  uint64_t ctx = 0;
+};
+constexpr int kAttrSlots = 64;
+AttrEntry g_attr[kAttrSlots];
+int g_attr_next = 0;
+std::mutex g_attr_mu;
 }  // namespace
+
+namespace {
+std::atomic<int32_t> g_debug_flags{0};
+}  // namespace
+
+int32_t debug_flags() { return g_debug_flags.load(std::memory_order_relaxed); }
+
+uint64_t current_context_id() {
+  std::call_once(g_ctx_once, load_ctx_entry_points);
+  if (g_ctx_current == nullptr || g_ctx_id == nullptr) return 0;
+  CUcontext c = nullptr;
+  if (g_ctx_current(&c) != CUDA_SUCCESS || c == nullptr) return 0;
+  unsigned long long id = 0;
+  if (g_ctx_id(c, &id) != CUDA_SUCCESS) return 0;
+  return uint64_t(id) + 1;  // never 0 for a live context
+}
+
+int ensure_max_dynamic_smem(const void* func, int bytes) {
+  const uint64_t ctx = current_context_id();
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  if (ctx != 0)
+    for (const AttrEntry& e : g_attr)
+      if (e.func == func && e.ctx == ctx) return FGG_OK;
+  FGG_CUDA_CHECK(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  // the call above initialises the context if nothing had yet
+  const uint64_t now = ctx != 0 ? ctx : current_context_id();
+  if (now != 0) {
+    g_attr[g_attr_next] = AttrEntry{func, now};
+    g_attr_next = (g_attr_next + 1) % kAttrSlots;
+  }
+  return FGG_OK;
+}
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -130,7 +193,11 @@ const char* fgg_error_string(int code) {
 
 const char* fgg_last_error_detail(void) { return fgg::g_detail; }
 
-const char* fgg_version(void) { return "fgg 0.1.0 sm_100a"; }
+const char* fgg_version(void) { return "fgg 0.2.0 sm_100a"; }
+
+int32_t fgg_debug_set_flags(int32_t flags) {
+  return fgg::g_debug_flags.exchange(flags, std::memory_order_relaxed);
+}
 
 int fgg_read_device_status(const void* workspace, void* stream) {
   if (workspace == nullptr) return fgg::set_error(FGG_EINVAL, "workspace is null");

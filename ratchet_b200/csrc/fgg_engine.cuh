@@ -48,6 +48,7 @@
 
 #include <cuda_bf16.h>
 
+#include "fgg_host.cuh"
 #include "fgg_ptx.cuh"
 
 namespace fgg {
@@ -110,7 +111,13 @@ struct GemmParams {
   int32_t nt;     // weight tiles per group in the tile list (128 rows; 256 for pairs)
   int32_t nt128;  // 128-row weight tiles per group (the SF pack's unit)
   int32_t epi;    // kEpiPlain or kEpiSiluMul (NVFP4 only)
+  int32_t debug_flags;  // test hooks (kDebugNoLoads); 0 in normal use
 };
+
+// Test hook: the producer arms no stage and issues no load, so the MMA role's
+// wait on the first full barrier runs out (a barrier nothing completes) and the
+// kernel ends through its bounded-wait path with a non-zero status word.
+constexpr int32_t kDebugNoLoads = 1;
 
 // Epilogues.  kEpiPlain: out[t, n] = bf16(alpha * acc).  kEpiSiluMul: the
 // weight rows come in 32-row chunks of 16 gate rows then the 16 up rows of the
@@ -467,7 +474,8 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
             break;
           }
           const uint32_t fb = full_bar(stage);
-          if (elect_one()) {
+          const bool arm = (p.debug_flags & kDebugNoLoads) == 0;
+          if (arm && elect_one()) {
             if constexpr (C::KSUB == 1)
               mbar_arrive_expect_tx(fb, C::TX_BYTES);
             else
@@ -491,7 +499,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
             }
           }
           __syncwarp();
-          ++arms;
+          if (arm) ++arms;
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
@@ -942,7 +950,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             break;
           }
           const uint32_t fb = leader_full0 + 8u * stage;
-          if (elect_one()) {
+          const bool arm = (p.debug_flags & kDebugNoLoads) == 0;
+          if (arm && elect_one()) {
             if (leader) {
               if constexpr (C::KSUB == 1)
                 mbar_arrive_expect_tx(full_bar(stage), 2u * C::TX_CTA);
@@ -967,7 +976,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
             }
           }
           __syncwarp();
-          ++arms;
+          if (arm) ++arms;
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
@@ -1173,39 +1182,25 @@ cudaError_t launch_dependent(Kernel kernel, int grid, uint32_t smem, cudaStream_
   return cudaLaunchKernelEx(&cfg, kernel, gp);
 }
 
-// Set the kernel's dynamic shared memory limit (once per device), then launch
+// Raise the kernel's dynamic shared memory limit (once per context), then launch
 // one CTA pair per two SMs, or one per tile when there are fewer tiles.  Host only.
 template <class C>
 cudaError_t launch_pair(const GemmParams& gp, int sm_count, cudaStream_t s) {
-  static int configured_device = -1;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (configured_device != dev) {
-    e = cudaFuncSetAttribute(fgg_gemm_pair_kernel<C>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    configured_device = dev;
-  }
+  if (ensure_max_dynamic_smem(reinterpret_cast<const void*>(fgg_gemm_pair_kernel<C>),
+                              int(C::SMEM_BYTES)) != FGG_OK)
+    return cudaErrorInvalidValue;
   const int pairs_avail = sm_count / 2;
   const int pairs = gp.num_tiles < pairs_avail ? (gp.num_tiles > 0 ? gp.num_tiles : 1) : pairs_avail;
   return launch_dependent(fgg_gemm_pair_kernel<C>, 2 * pairs, C::SMEM_BYTES, s, gp);
 }
 
-// Set the kernel's dynamic shared memory limit (once per device), then launch
+// Raise the kernel's dynamic shared memory limit (once per context), then launch
 // one CTA per SM, or one per tile when there are fewer tiles.  Host only.
 template <class C>
 cudaError_t launch_engine(const GemmParams& gp, int sm_count, cudaStream_t s) {
-  static int configured_device = -1;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (configured_device != dev) {
-    e = cudaFuncSetAttribute(fgg_gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(C::SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    configured_device = dev;
-  }
+  if (ensure_max_dynamic_smem(reinterpret_cast<const void*>(fgg_gemm_kernel<C>),
+                              int(C::SMEM_BYTES)) != FGG_OK)
+    return cudaErrorInvalidValue;
   const int grid = gp.num_tiles < sm_count ? (gp.num_tiles > 0 ? gp.num_tiles : 1) : sm_count;
   return launch_dependent(fgg_gemm_kernel<C>, grid, C::SMEM_BYTES, s, gp);
 }

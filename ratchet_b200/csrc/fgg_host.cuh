@@ -38,6 +38,19 @@ struct DeviceInfo {
 // Current device's properties (cached per device); FGG_EARCH unless sm_100.
 int current_device(DeviceInfo* out);
 
+// Unique id of the calling thread's current CUDA context (never reused, so a
+// context created after cudaDeviceReset gets a new one); 0 when no context is
+// current yet.  Per-context state (a __device__ symbol's address, a kernel's
+// raised shared-memory limit) is cached under this id.
+uint64_t current_context_id();
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, context).
+int ensure_max_dynamic_smem(const void* func, int bytes);
+
+// Test hooks set by fgg_debug_set_flags (0 in normal use), copied into every
+// GEMM launch's parameters.
+int32_t debug_flags();
+
 // 2-D uint8 tensor map, 128-byte swizzle, zero fill out of bounds:
 // dims {inner_bytes, rows}, row pitch = inner_bytes, box {box_inner, box_rows}.
 int encode_u8_2d(CUtensorMap* out, const void* base, uint64_t inner_bytes, uint64_t rows,

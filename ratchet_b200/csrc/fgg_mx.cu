@@ -211,6 +211,10 @@ int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
     const int64_t blocks = int64_t(pp.blocks_tiles) + pp.blocks_sfx + (sfw_lines + 255) / 256;
     FGG_CUDA_CHECK(launch_dependent(mx_prepare_kernel, int(blocks), 0, s, pp));
     FGG_CUDA_CHECK(cudaGetLastError());
+  } else {
+    // the prepare kernel, skipped here, is what clears the status words: a
+    // reused workspace must not carry an earlier call's status into this one
+    FGG_CUDA_CHECK(cudaMemsetAsync(ws + L.status, 0, 3 * sizeof(int32_t), s));
   }
 
   GemmParams gp;
@@ -239,6 +243,7 @@ int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
   gp.ksteps = L.ksteps;
   gp.nt = L.nt;
   gp.nt128 = L.nt128;
+  gp.debug_flags = debug_flags();
   cudaError_t e;
   if (L.pair) {
     if (int rc = encode_u64_rows(&gp.sfw_map, gp.sfw,

@@ -544,6 +544,7 @@ int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uin
   gp.ksteps = L.nk256;
   gp.nt = L.nt;
   gp.nt128 = L.nt128;
+  gp.debug_flags = debug_flags();
   cudaError_t e;
   if (L.pair) {
     // scale atoms as rows of uint64: a CTA's 4 weight atoms of a K step are one

@@ -77,36 +77,78 @@ __device__ __forceinline__ uint32_t e2m1_code(float y) {
   return c | (y < 0.0f ? 8u : 0u);
 }
 
-// One thread per 16-element block: 8 code bytes + 1 scale byte.
-// Thread 0 also writes the decode scale g = 1 / gs when asked (decode_scale
-// non-null), so the caller needs no host-side arithmetic on amax.
-template <typename T>
-__global__ void nvfp4_quant_kernel(const T* __restrict__ x, int64_t blocks, const float* amax_p,
-                                   uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
-                                   float* __restrict__ decode_scale) {
-  const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+// Eight consecutive elements of x (a half block) as fp32.  kVec: one or two
+// 16-byte vector loads (x 16-byte aligned); otherwise scalar loads.
+template <typename T, bool kVec>
+__device__ __forceinline__ void load8(const T* __restrict__ x, int64_t e0, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<float, true>(const float* __restrict__ x, int64_t e0,
+                                                    float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(x + e0));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(x + e0 + 4));
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16, true>(const __nv_bfloat16* __restrict__ x,
+                                                            int64_t e0, float (&v)[8]) {
+  const uint4 a = __ldg(reinterpret_cast<const uint4*>(x + e0));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float, false>(const float* __restrict__ x, int64_t e0,
+                                                     float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = load_f32(x, e0 + i);
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16, false>(const __nv_bfloat16* __restrict__ x,
+                                                             int64_t e0, float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = load_f32(x, e0 + i);
+}
+
+// Two lanes per 16-element block, eight elements each: a warp reads 256
+// consecutive elements (1 KB of fp32) per step and writes 128 consecutive
+// code bytes (each lane the 4 bytes of its half block) and 16 scale bytes.
+// The pair's block maximum comes from one shuffle; both lanes then derive the
+// same scale.  Thread 0 also writes the decode scale g = 1 / gs when asked
+// (decode_scale non-null), so the caller needs no host-side arithmetic on amax.
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(256)
+    nvfp4_quant_kernel(const T* __restrict__ x, int64_t blocks, const float* amax_p,
+                       uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
+                       float* __restrict__ decode_scale) {
+  const int64_t h = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // half-block index
   const float amax = *amax_p;
   const float gs = amax > 0.0f ? 2688.0f / amax : 1.0f;
-  if (b == 0 && decode_scale != nullptr) *decode_scale = __fdiv_rn(1.0f, gs);
-  if (b >= blocks) return;
-  float v[16];
-  float bmax = 0.0f;
+  if (h == 0 && decode_scale != nullptr) *decode_scale = __fdiv_rn(1.0f, gs);
+  const int64_t b = h >> 1;
+  const bool live = b < blocks;  // blocks * 2 may not fill the last warp
+  float v[8];
+  float m = 0.0f;
+  if (live) {
+    load8<T, kVec>(x, h * 8, v);
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    v[i] = load_f32(x, b * 16 + i);
-    bmax = fmaxf(bmax, fabsf(v[i]));
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
   }
+  const float bmax = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  if (!live) return;
   const float sval = (bmax / 6.0f) * gs;
   const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(sval, __NV_SATFINITE, __NV_E4M3);
   const float sdec = e4m3_value(uint32_t(s8));
   const float inv = sdec == 0.0f ? 0.0f : gs / sdec;
-  uint32_t lo = 0, hi = 0;
+  uint32_t word = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) lo |= e2m1_code(v[i] * inv) << (4 * i);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) hi |= e2m1_code(v[8 + i] * inv) << (4 * i);
-  reinterpret_cast<uint2*>(codes)[b] = make_uint2(lo, hi);
-  sf[b] = uint8_t(s8);
+  for (int i = 0; i < 8; ++i) word |= e2m1_code(v[i] * inv) << (4 * i);
+  reinterpret_cast<uint32_t*>(codes)[h] = word;
+  if ((h & 1) == 0) sf[b] = uint8_t(s8);
 }
 
 }  // namespace
@@ -150,16 +192,27 @@ int fgg_nvfp4_quantize(const void* x, int32_t x_dtype, int64_t rows, int32_t k, 
   const int64_t blocks = rows * (k / 16);
   if (blocks == 0 && decode_scale == nullptr) return FGG_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int64_t grid = blocks > 0 ? (blocks + 255) / 256 : 1;
+  // two threads per 16-element block
+  const int64_t grid = blocks > 0 ? (2 * blocks + 255) / 256 : 1;
   if (grid > INT32_MAX) return set_error(FGG_EBADSHAPE, "tensor too large");
-  if (x_dtype == 0)
-    nvfp4_quant_kernel<float><<<int(grid), 256, 0, s>>>(
-        static_cast<const float*>(x), blocks, amax, static_cast<uint8_t*>(codes),
-        static_cast<uint8_t*>(sf), decode_scale);
-  else
-    nvfp4_quant_kernel<__nv_bfloat16><<<int(grid), 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), blocks, amax, static_cast<uint8_t*>(codes),
-        static_cast<uint8_t*>(sf), decode_scale);
+  const bool vec = aligned16(x);
+  auto* c8 = static_cast<uint8_t*>(codes);
+  auto* s8 = static_cast<uint8_t*>(sf);
+  if (x_dtype == 0) {
+    const auto* xf = static_cast<const float*>(x);
+    if (vec)
+      nvfp4_quant_kernel<float, true><<<int(grid), 256, 0, s>>>(xf, blocks, amax, c8, s8, decode_scale);
+    else
+      nvfp4_quant_kernel<float, false><<<int(grid), 256, 0, s>>>(xf, blocks, amax, c8, s8, decode_scale);
+  } else {
+    const auto* xb = static_cast<const __nv_bfloat16*>(x);
+    if (vec)
+      nvfp4_quant_kernel<__nv_bfloat16, true><<<int(grid), 256, 0, s>>>(xb, blocks, amax, c8, s8,
+                                                                        decode_scale);
+    else
+      nvfp4_quant_kernel<__nv_bfloat16, false><<<int(grid), 256, 0, s>>>(xb, blocks, amax, c8, s8,
+                                                                         decode_scale);
+  }
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }

@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Runs only where the reference checkout is mounted (pass its path, default
-/root/reference); the GPU box and the tests use the committed .npz files.
+Runs only where the reference checkout is mounted (pass its path, or set
+RATCHET_REFERENCE); the GPU box and the tests use the committed .npz files.
 
   e2m1_cast.npz   inputs + packed codes of the reference evaluator's FP4 cast
                   (src/forgekernel/card_template/eval/leaderboard.py:608-627,
@@ -11,11 +11,12 @@ Runs only where the reference checkout is mounted (pass its path, default
                   :2679, `_pack_sf_act` :2691, `_pack_sf_wgt` :2709, the
                   block->expert table :2780): pins the SF atom layout
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 """
 from __future__ import annotations
 
 import importlib.util
+import os
 import sys
 from pathlib import Path
 
@@ -77,7 +78,12 @@ def make_mx_sf(ref_root: Path):
 
 
 def main(argv):
-    ref_root = Path(argv[1] if len(argv) > 1 else "/root/reference")
+    # the reference checkout: first argument, else $RATCHET_REFERENCE
+    arg = argv[1] if len(argv) > 1 else os.environ.get("RATCHET_REFERENCE")
+    if not arg:
+        raise SystemExit("usage: make_golden.py <reference checkout> "
+                         "(or set RATCHET_REFERENCE)")
+    ref_root = Path(arg)
     if not ref_root.exists():
         raise SystemExit(f"reference checkout not found at {ref_root}")
     make_e2m1(ref_root)

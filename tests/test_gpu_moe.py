@@ -195,3 +195,41 @@ def test_moe_two_nccl_ranks(cuda_device, tmp_path):
     for r in range(2):
         line = (tmp_path / f"rank{r}.txt").read_text()
         assert line.startswith("1 "), f"rank {r}: {line}"
+
+
+@pytest.mark.slow
+def test_moe_config3_world1_full_size(cuda_device):
+    """BASELINE config 3 at full size on one GPU: 4096 tokens, top-8 of 64
+    experts (Zipf 1.1), N = 4096, K = 7168, with the router-weighted combine.
+    A seeded sample of 256 tokens is checked, every route of each against the
+    oracle: out[t] = bf16(sum_k w[t,k] * bf16(alpha_e * deq(x_t) . deq(W_e)))."""
+    import bench
+    import ratchet_b200 as rb
+
+    wl = bench.workload("moe")
+    d = bench.moe_setup(wl, 1, 0, cuda_device)
+    layer = moe.ExpertParallelMoE(d["wc"], d["wsf"], d["wg"], d["owner"], d["slot"])
+    out = layer.forward(d["xc"], d["xs"], d["xg"], d["ids"], d["wts"])
+    rb.last_status()
+    layer.check()
+    T = wl["tokens"]
+    sample = np.sort(np.random.default_rng(11).choice(T, size=256, replace=False))
+    idx = torch.from_numpy(sample).to(cuda_device)
+    x = ref.nvfp4_dequantize_torch(d["xc"].index_select(0, idx).cpu(),
+                                   d["xs"].view(torch.uint8).index_select(0, idx).cpu())
+    ids = d["ids_all"][sample]
+    w = d["w_all"][sample]
+    xg = float(d["xg"].item())
+    acc = torch.zeros((len(sample), wl["n"]))
+    for slot_i, e in enumerate(d["mine"]):
+        hit = np.argwhere(ids == e)
+        if not len(hit):
+            continue
+        wd = ref.nvfp4_dequantize_torch(d["wc"][slot_i].cpu(), d["wsf"][slot_i].view(torch.uint8).cpu())
+        alpha = float(np.float32(np.float32(xg) * np.float32(d["wg"][slot_i].item())))
+        rows = torch.from_numpy(hit[:, 0])
+        y = ((x[rows] @ wd.T) * alpha).to(torch.bfloat16).float()
+        acc.index_add_(0, rows, y * torch.from_numpy(w[hit[:, 0], hit[:, 1]])[:, None])
+    want = acc.to(torch.bfloat16)
+    ok, st = ref.check_close(out.index_select(0, idx).cpu(), want)
+    assert ok, st

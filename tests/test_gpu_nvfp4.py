@@ -55,6 +55,26 @@ def test_quantizer_bitexact(cuda_device):
     assert np.float32(g.item()) == rg
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_quantizer_unaligned_input_bitexact(cuda_device, dtype):
+    """An input that does not start on a 16-byte boundary takes the scalar-load
+    form of the quantiser: the same bytes as the oracle."""
+    import ratchet_b200 as rb
+
+    rng = np.random.default_rng(17)
+    x = rng.standard_normal((37, 160), dtype=np.float32)
+    xt = torch.from_numpy(x).to(dtype)
+    raw = torch.empty(xt.numel() + 1, dtype=dtype, device=cuda_device)
+    view = raw[1:].view(xt.shape)
+    view.copy_(xt.to(cuda_device))
+    assert view.data_ptr() % 16 != 0
+    codes, sf, g = rb.quantize_nvfp4(view)
+    rc, rs, rg = ref.nvfp4_quantize(xt.float().numpy())
+    assert np.array_equal(codes.cpu().numpy(), rc)
+    assert np.array_equal(sf.view(torch.uint8).cpu().numpy(), rs)
+    assert np.float32(g.item()) == rg
+
+
 def test_quantizer_bf16_input(cuda_device):
     import ratchet_b200 as rb
 
