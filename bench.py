@@ -566,6 +566,136 @@ def run_reference_mx(args, wl):
     return 0
 
 
+REF_KERNEL = ROOT / "baseline" / "_ref" / "kernels" / "gemm" / "fp4_grouped_gemm" / "b200" / "kernel.py"
+MX_CAMPAIGN_SEED = 2026
+
+
+def load_reference_kernel():
+    """The reference's own B200 kernel module (kernels/gemm/fp4_grouped_gemm/
+    b200/kernel.py, unmodified), from the reference install under
+    baseline/_ref (not part of this repository).  Returns (module, None) or
+    (None, why)."""
+    import importlib.util
+
+    if not REF_KERNEL.exists():
+        return None, f"reference kernel not installed at {REF_KERNEL.relative_to(ROOT)}"
+    try:
+        spec = importlib.util.spec_from_file_location("reference_fp4_grouped_gemm", str(REF_KERNEL))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    except Exception as e:  # the DSL it needs is missing or incompatible
+        return None, f"reference kernel did not import: {type(e).__name__}: {e}"
+    return mod, None
+
+
+def mx_campaign_on_device(dev, seed: int = MX_CAMPAIGN_SEED):
+    """The MX campaign problem (oracle/mx.py campaign_problem, numpy) on the device."""
+    from oracle import mx as mref
+
+    p = mref.campaign_problem(seed)
+    t = {k: torch.from_numpy(v).to(dev) for k, v in p.items()}
+    return (t["a"].view(torch.float8_e4m3fn), t["a_sf"], t["b"], t["b_sf"], t["m_indices"]), p
+
+
+def _device_close(got, want):
+    """The operator tolerance evaluated on the device (no host copy of the outputs)."""
+    g, w = got.float(), want.float()
+    d = (g - w).abs()
+    scale = float(w.abs().max())
+    bad = int((d > 2e-2 * w.abs() + 1e-2 * scale).sum())
+    rel = float(d.max()) / scale if scale > 0 else float(d.max())
+    return {"rel": rel, "bad": bad, "max_ref": scale, "bitexact_frac": float((g == w).float().mean()),
+            "ok": rel <= 1e-2 and bad == 0}
+
+
+def run_reference_gpu_mx(args, wl):
+    """The reference's own kernel.py next to fp4_grouped_gemm on the same B200,
+    same inputs, same timing protocol: warm-up calls, then alternating windows
+    of `steps` back-to-back calls per arm (CUDA events), median per arm.  Also
+    compares the two outputs on every valid row and both with the CPU oracle on
+    sampled rows."""
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if ws > 1:
+        if rank == 0:
+            print(json.dumps({"impl": "reference-gpu", "unavailable": "the reference kernel arm "
+                              "runs on one GPU only"}))
+        return 0
+    mod, why = load_reference_kernel()
+    if mod is None:
+        print(json.dumps({"impl": "reference-gpu", "unavailable": why}))
+        return 0
+    import hashlib
+
+    import ratchet_b200 as rb
+    from oracle import mx as mref
+    from oracle import nvfp4 as ref
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    args_t, prob = mx_campaign_on_device(dev)
+    valid = args_t[4] >= 0
+    arms = {"reference": lambda: mod.fp4_grouped_gemm(*args_t),
+            "ours": lambda: rb.fp4_grouped_gemm(*args_t)}
+    t0 = time.perf_counter()
+    c_ref = arms["reference"]()
+    torch.cuda.synchronize()
+    first_ref_s = time.perf_counter() - t0
+    c_ours = arms["ours"]()
+    torch.cuda.synchronize()
+    rb.last_status()
+    parity = {"ours_vs_reference": _device_close(c_ours[valid], c_ref[valid])}
+    rows = np.flatnonzero(prob["m_indices"] >= 0)[::1024]
+    want = mref.campaign_rows_output(MX_CAMPAIGN_SEED, rows)
+    ridx = torch.from_numpy(rows).to(dev)
+    for name, c in (("oracle_vs_reference", c_ref), ("oracle_vs_ours", c_ours)):
+        ok, st = ref.check_close(c.index_select(0, ridx).cpu(), want)
+        parity[name] = dict(st, ok=ok, rows=int(rows.size))
+    del c_ref, c_ours
+    for _ in range(args.warmup):
+        for f in arms.values():
+            f()
+    torch.cuda.synchronize()
+    windows = {k: [] for k in arms}
+    sampler = ClockSampler(0)
+    sampler.start()
+    for w in range(5):
+        for name in (("reference", "ours") if w % 2 == 0 else ("ours", "reference")):
+            f = arms[name]
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(args.steps):
+                f()
+            e1.record()
+            torch.cuda.synchronize()
+            windows[name].append(e0.elapsed_time(e1) / args.steps)
+    clocks = sampler.stop()
+    rb.last_status()
+    fl = flops(wl)
+    med = {k: statistics.median(v) for k, v in windows.items()}
+    line = {
+        "impl": "reference-gpu", "metric": "grouped-GEMM TFLOPS", "unit": "TFLOP/s",
+        "value": fl / (med["reference"] * 1e-3) / 1e12, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": med["reference"], "higher_is_better": True,
+        "config": {"workload": wl["desc"], "m_total": int(prob["m_indices"].size),
+                   "seed": MX_CAMPAIGN_SEED,
+                   "l2": "one 0.36 GB input set (> L2), back-to-back calls"},
+        "reference": {"ms": med["reference"], "windows_ms": windows["reference"],
+                      "tflops": fl / (med["reference"] * 1e-3) / 1e12,
+                      "first_call_s_with_compile": first_ref_s,
+                      "kernel_sha256": hashlib.sha256(REF_KERNEL.read_bytes()).hexdigest()},
+        "ours": {"ms": med["ours"], "windows_ms": windows["ours"],
+                 "tflops": fl / (med["ours"] * 1e-3) / 1e12},
+        "ours_speedup": med["reference"] / med["ours"],
+        "parity": parity, "clocks": clocks,
+        "protocol": f"{args.warmup} warm-up calls per arm, then 5 alternating windows of "
+                    f"{args.steps} back-to-back calls per arm (CUDA events), median",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_mx(args, wl):
     """fp4_grouped_gemm, the reference's own operator, at its campaign point
     (kernel.py:213, :286-288: 0.3756 ms on the reference's B200).  One GPU, or
@@ -954,7 +1084,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--config", choices=["grouped", "dense", "decode", "moe", "mlp", "mx"],
                     default="grouped")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
@@ -966,6 +1096,12 @@ def main():
         print(json.dumps({"impl": "reference", "unavailable": "the reference operator has no "
                           "gated expert MLP; its CPU arm covers the GEMM configs"}))
         return 0
+    if args.impl == "reference-gpu":
+        if wl["name"] != "mx":
+            print(json.dumps({"impl": "reference-gpu", "unavailable": "the reference's GPU kernel "
+                              "is the MX operator: use --config mx"}))
+            return 0
+        return run_reference_gpu_mx(args, wl)
     if args.impl == "reference":
         return run_reference(args, wl)
     if wl["name"] == "moe":

@@ -59,3 +59,27 @@ def test_mx_campaign_point_scaled(cuda_device):
     rows = [int(v) for v in rng.integers(600, 1400, size=8)]
     prob = mref.random_problem(rows, 4096, 4096, seed=1)
     _check(prob, _run(prob, cuda_device))
+
+
+@pytest.mark.slow
+def test_mx_campaign_matches_reference_kernel_rows(cuda_device):
+    """fp4_grouped_gemm at the reference's campaign point (8 x 4096 rows,
+    N = K = 4096) against output rows that the reference's own kernel produced
+    on the same seeded inputs (tests/golden/make_mx_reference.py), under the
+    operator tolerance."""
+    from pathlib import Path
+
+    import bench
+    import ratchet_b200 as rb
+
+    fx = Path(__file__).resolve().parent / "golden" / "mx_reference_rows.npz"
+    if not fx.exists():
+        pytest.skip("reference kernel rows not generated")
+    d = np.load(fx)
+    args, _ = bench.mx_campaign_on_device(cuda_device, seed=int(d["seed"]))
+    c = rb.fp4_grouped_gemm(*args)
+    rb.last_status()
+    rows = torch.from_numpy(d["rows"]).to(cuda_device)
+    want = torch.from_numpy(d["out_bf16_bits"]).view(torch.bfloat16)
+    ok, st = ref.check_close(c.index_select(0, rows).cpu(), want)
+    assert ok, st

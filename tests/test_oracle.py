@@ -176,3 +176,25 @@ def test_mx_oracle_matches_direct_formula():
     assert abs(float(c[i, j]) - float(aval @ bval)) <= 1e-4 * max(1.0, abs(float(aval @ bval)))
     pad_rows = np.nonzero(p["m_indices"] < 0)[0]
     assert float(c[pad_rows].abs().max()) == 0.0
+
+
+MX_REF_ROWS = Path(__file__).resolve().parent / "golden" / "mx_reference_rows.npz"
+
+
+@pytest.mark.skipif(not MX_REF_ROWS.exists(), reason="reference kernel rows not generated")
+def test_mx_oracle_matches_reference_kernel_rows():
+    """The MX oracle against output rows of the reference's own kernel
+    (kernels/gemm/fp4_grouped_gemm/b200/kernel.py, run unmodified on a B200 by
+    tests/golden/make_mx_reference.py) at its campaign point: same seeded
+    inputs, the operator tolerance (the two differ in fp32 summation order)."""
+    import torch
+
+    from oracle import mx as mref
+    from oracle import nvfp4 as ref
+
+    d = np.load(MX_REF_ROWS)
+    rows = d["rows"]
+    got = torch.from_numpy(d["out_bf16_bits"]).view(torch.bfloat16)
+    want = mref.campaign_rows_output(int(d["seed"]), rows)
+    ok, st = ref.check_close(got, want)
+    assert ok, st
