@@ -138,6 +138,45 @@ FGG_API int fgg_nvfp4_prepare(const FggNvfp4Problem* p, void* workspace, size_t 
 FGG_API int fgg_nvfp4_gemm(const FggNvfp4Problem* p, const void* pack, void* workspace, size_t ws_bytes,
                    void* stream);
 
+/* The grouped GEMM over contiguous token rows with the group sizes in device
+ * memory: the reference operator's own M-grouped layout (one concatenated
+ * activation tensor, kernels/gemm/fp4_grouped_gemm/b200/kernel.py:10-37,
+ * :2788-2795) in the NVFP4 format, with per-group offsets instead of a per-row
+ * expert id.  Group g owns rows [offsets[g], offsets[g+1]) of a, a_sf and
+ * out; the offsets may be written by an earlier kernel on the same stream
+ * (e.g. an expert-parallel dispatch plan): the host never reads them, so a
+ * call needs no host synchronisation and its host cost does not grow with G.
+ * Rows outside every group are neither read for any output nor written.
+ * Malformed offsets (decreasing, negative, past max_rows) run no tile and
+ * leave status 0x203 in the workspace. */
+typedef struct FggNvfp4RowsProblem {
+  int32_t num_groups;
+  int32_t n;
+  int32_t k;
+  int32_t max_rows;          /* rows allocated in a, a_sf, out, row_scale        */
+  const int32_t* offsets;    /* device int32 [G + 1], nondecreasing, <= max_rows */
+  const void* a;             /* device [max_rows, K/2] codes                     */
+  const void* a_sf;          /* device [max_rows, K/16] E4M3 scales              */
+  const float* alpha;        /* device fp32 [G]                                  */
+  void* out;                 /* device bf16 [max_rows, N]                        */
+  /* Optional device fp32 [max_rows]: a per-row factor applied with alpha,
+   * out[r, n] = bf16(alpha_g * row_scale[r] * acc) (e.g. the per-source decode
+   * scale of rows gathered from several ranks); NULL = 1. */
+  const float* row_scale;
+  /* Optional device int32 [G]: the packed weight group of problem group g
+   * (NULL = g); a value outside [0, num_weight_groups) stops the kernel with
+   * status 0x202 before any load of that tile. */
+  const int32_t* b_index;
+  int32_t num_weight_groups; /* groups in `pack` when b_index is set             */
+  /* Optional host bound on every group's rows (0 = max_rows): at most 16
+   * selects the decode tiles (16 tokens, weights streamed once). */
+  int32_t max_group_rows;
+} FggNvfp4RowsProblem;
+
+FGG_API size_t fgg_nvfp4_rows_workspace_bytes(const FggNvfp4RowsProblem* p);
+FGG_API int fgg_nvfp4_grouped_gemm_rows(const FggNvfp4RowsProblem* p, const void* pack,
+                                        void* workspace, size_t ws_bytes, void* stream);
+
 /* No counterpart in the reference (its operator always allocates its scale
  * repack and outputs through torch).  fgg_nvfp4_grouped_gemm for callers that
  * cannot allocate device memory at call time: a serving loop that owns a

@@ -38,6 +38,13 @@ class FggNvfp4Problem(ctypes.Structure):
                 ("out", _VOIDP), ("b_index", _VOIDP), ("num_weight_groups", ctypes.c_int32)]
 
 
+class FggNvfp4RowsProblem(ctypes.Structure):
+    _fields_ = [("num_groups", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
+                ("max_rows", ctypes.c_int32), ("offsets", _VOIDP), ("a", _VOIDP), ("a_sf", _VOIDP),
+                ("alpha", _VOIDP), ("out", _VOIDP), ("row_scale", _VOIDP), ("b_index", _VOIDP),
+                ("num_weight_groups", ctypes.c_int32), ("max_group_rows", ctypes.c_int32)]
+
+
 class FggMxProblem(ctypes.Structure):
     _fields_ = [("m_total", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
                 ("num_groups", ctypes.c_int32), ("a", _VOIDP), ("a_sf", _VOIDP), ("b", _VOIDP),
@@ -62,6 +69,8 @@ _SIGS = {
     "fgg_nvfp4_grouped_gemm": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_nvfp4_prepare": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_nvfp4_gemm": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, ctypes.c_size_t, _VOIDP]),
+    "fgg_nvfp4_rows_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(FggNvfp4RowsProblem)]),
+    "fgg_nvfp4_grouped_gemm_rows": (ctypes.c_int, [ctypes.POINTER(FggNvfp4RowsProblem), _VOIDP, _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_nvfp4_grouped_gemm_noalloc": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, _VOIDP]),
     "fgg_moe_plan": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int32, _VOIDP, _VOIDP, ctypes.c_int32,
                                     ctypes.c_int32, ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP, _VOIDP, _VOIDP]),

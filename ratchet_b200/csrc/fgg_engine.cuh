@@ -90,7 +90,9 @@ static_assert(sizeof(SchedSlot) == 32, "slot is 8 words");
 
 struct GemmParams {
   CUtensorMap mx_tmap_w;      // MX: 3-D map of the [G, N, K] weight codes
-  CUtensorMap mx_tmap_x;      // MX: 2-D map of the [M_total, K] fp8 activations
+  // One 2-D map over contiguous token rows: MX [M_total, K] fp8 activations;
+  // NVFP4 with x_flat set: [max_rows, K/2] codes of every group
+  CUtensorMap tmap_x_flat;
   CUtensorMap sfw_map;        // pair kernel: the weight SF atoms as a 2-D uint64 tensor
   CUtensorMap sfx_map;        // pair kernel: the token SF atoms as a 2-D uint64 tensor
   const CUtensorMap* tmap_w;  // NVFP4: [G] per-group maps (global memory)
@@ -112,6 +114,16 @@ struct GemmParams {
   int32_t nt128;  // 128-row weight tiles per group (the SF pack's unit)
   int32_t epi;    // kEpiPlain or kEpiSiluMul (NVFP4 only)
   int32_t debug_flags;  // test hooks (kDebugNoLoads); 0 in normal use
+  // NVFP4: 1 = the token rows of all groups lie in one buffer read through
+  // tmap_x_flat, the tile's first row being its output row (group offsets
+  // from the device); 0 = one descriptor per group (tmap_x)
+  int32_t x_flat;
+  // optional device [rows] factor per output row (token), applied with alpha:
+  // out[t, n] = bf16(alpha_g * row_scale[t] * acc); null = 1
+  const float* row_scale;
+  // optional device word holding the tile count (written by the prepare
+  // kernel); null = num_tiles
+  const int32_t* num_tiles_dev;
 };
 
 // Test hook: the producer arms no stage and issues no load, so the MMA role's
@@ -197,20 +209,64 @@ __device__ __forceinline__ void write_slot(volatile SchedSlot* ring, int slot,
   ring[slot].wgroup = s.wgroup;
 }
 
-// Epilogue of one tile for the calling warp: its 32 TMEM lanes (output
-// columns n) x `rows` tokens, fp32 -> x alpha -> bf16.
-__device__ __forceinline__ void epilogue_tile(__nv_bfloat16* out, int ldn, int n, size_t row0,
-                                              int rows, int ncols, float alpha, uint32_t taddr) {
-  __nv_bfloat16* orow = out + row0 * size_t(ldn) + size_t(n);
+// Shared-memory staging of the plain epilogue: 16 tokens x 16 words (32 bf16
+// output columns) per epilogue warp.
+constexpr uint32_t kEpiStageBytes = 4 * 16 * 16 * 4;
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Epilogue of one tile for the calling warp: its 32 TMEM lanes are the
+// output columns n0 + lane, its TMEM columns the tile's tokens.  Per 16
+// tokens: one tcgen05.ld (lane = column, register j = token), x alpha (x the
+// token's row scale), then a transpose through the warp's 1 KB staging area so
+// that every lane stores 16 contiguous bytes -- 8 columns of one token row --
+// instead of 16 scattered 2-byte values:
+//   * token pairs (j, j+1): one shuffle across neighbouring lanes gives the
+//     even lane columns (l, l+1) of token j and the odd lane the same columns
+//     of token j+1; each stores that word at [token][column pair] (the two
+//     rows of a pair land in opposite bank halves: conflict-free);
+//   * each lane reads back 16 bytes (token lane/4, then lane/4 + 8; columns
+//     8 (lane % 4) .. +7) and stores them to global memory.
+// A row scale, when given, comes one value per lane (lanes 0-15) and is
+// broadcast by shuffles.  Rows past `rows` are neither scaled nor stored.
+__device__ __forceinline__ void epilogue_tile(__nv_bfloat16* out, int ldn, int n0, size_t row0,
+                                              int rows, int ncols, float alpha,
+                                              const float* __restrict__ row_scale, uint32_t taddr,
+                                              uint32_t* stage) {
+  const int lane = threadIdx.x & 31;
+  const bool odd = lane & 1;
   for (int c0 = 0; c0 < ncols; c0 += 16) {
     uint32_t r[16];
     tmem_ld16(taddr + c0, r);
+    float rs = 1.0f;
+    if (row_scale != nullptr && lane < 16 && c0 + lane < rows)
+      rs = __ldg(row_scale + row0 + size_t(c0 + lane));
     tmem_wait_ld();
+    float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      if (c0 + j < rows)
-        orow[size_t(c0 + j) * ldn] = __float2bfloat16_rn(alpha * __uint_as_float(r[j]));
+      v[j] = alpha * __uint_as_float(r[j]);
+      if (row_scale != nullptr) v[j] *= __shfl_sync(kFullMask, rs, j);
     }
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      const float got = __shfl_xor_sync(kFullMask, odd ? v[j] : v[j + 1], 1);
+      const uint32_t w = odd ? pack_bf16x2(got, v[j + 1]) : pack_bf16x2(v[j], got);
+      stage[(j + (odd ? 1 : 0)) * 16 + (lane >> 1)] = w;
+    }
+    __syncwarp();
+    const int seg = lane & 3;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int t = (lane >> 2) + 8 * h;
+      const uint4 q = *reinterpret_cast<const uint4*>(stage + t * 16 + 4 * seg);
+      if (c0 + t < rows)
+        *reinterpret_cast<uint4*>(out + (row0 + size_t(c0 + t)) * size_t(ldn) + size_t(n0 + 8 * seg)) = q;
+    }
+    __syncwarp();
   }
 }
 
@@ -269,12 +325,16 @@ struct EngineCfg {
   // token scales: CH atoms per MMA (NVFP4) or per K step (MX)
   static constexpr uint32_t SFX_BYTES = MX ? CH * 512 : 4 * CH * 512;
   static constexpr uint32_t TX_BYTES = W_TX + X_BYTES + SFW_BYTES + SFX_BYTES;
-  // bytes of one K step's tiles; a stage holds KSUB of them
-  static constexpr uint32_t SUB_BYTES =
-      (W_BYTES + X_BYTES + SFW_BYTES + SFX_BYTES + 1023) / 1024 * 1024;
-  static constexpr uint32_t STAGE_BYTES = KSUB * SUB_BYTES;
+  // Shared memory of one K step: its two operand tiles (1024 B aligned for
+  // the 128-byte swizzle) in one region, its scale atoms in another, so that
+  // no stage pads its atoms up to a 1024-byte boundary.  A stage holds KSUB
+  // K steps.
+  static constexpr uint32_t OP_BYTES = W_BYTES + X_BYTES;
+  static constexpr uint32_t SF_BYTES = SFW_BYTES + SFX_BYTES;
+  static constexpr uint32_t SUB_SLOTS = STAGES_ * KSUB;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "BN must be a multiple of 16");
-  static_assert((W_BYTES + X_BYTES) % 1024 == 0, "operand tiles must stay 1024 B aligned");
+  static_assert(OP_BYTES % 1024 == 0, "operand tiles must stay 1024 B aligned");
+  static_assert(SF_BYTES % 128 == 0, "scale atoms must stay 128 B aligned");
   // TMEM columns: two accumulators of BN fp32 columns, then a ring of scale
   // slots (4 columns of weight scales + 4 per token atom).  NVFP4 takes one
   // slot per MMA, MX one per K step.
@@ -294,7 +354,11 @@ struct EngineCfg {
   // drain taken
   static constexpr uint32_t NBARS = 2 * STAGES + 4 + 2 * SCHED + 3;
   static constexpr uint32_t MISC_BYTES = 8 * NBARS + 32 * SCHED + 16;
-  static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + MISC_BYTES;
+  // carve-out: [operand tiles][scale atoms][barriers, ring, words][epilogue staging]
+  static constexpr uint32_t SF_REGION = SUB_SLOTS * OP_BYTES;
+  static constexpr uint32_t BAR_REGION = SF_REGION + SUB_SLOTS * SF_BYTES;
+  static constexpr uint32_t EPI_REGION = (BAR_REGION + MISC_BYTES + 15) / 16 * 16;
+  static constexpr uint32_t SMEM_BYTES = 1024 + EPI_REGION + kEpiStageBytes;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
 
@@ -305,7 +369,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
 
-  const uint32_t bars = base + C::STAGES * C::STAGE_BYTES;
+  const uint32_t bars = base + C::BAR_REGION;
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (C::STAGES + s); };
   auto accf_bar = [&](int b) { return bars + 8u * (2 * C::STAGES + b); };
@@ -315,7 +379,10 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
   const uint32_t tmem_ready_bar = bars + 8u * (2 * C::STAGES + 4 + 2 * C::SCHED);
   const uint32_t drain_bar = tmem_ready_bar + 8u;
   const uint32_t taken_bar = tmem_ready_bar + 16u;  // producer took a slot
-  uint8_t* const misc = gbase + C::STAGES * C::STAGE_BYTES + 8 * C::NBARS;
+  uint8_t* const misc = gbase + C::BAR_REGION + 8 * C::NBARS;
+  // this warp's epilogue staging (warps 4-7)
+  uint32_t* const epi_stage = reinterpret_cast<uint32_t*>(
+      gbase + C::EPI_REGION + ((threadIdx.x >> 5) & 3) * (kEpiStageBytes / 4));
   volatile SchedSlot* const ring = reinterpret_cast<volatile SchedSlot*>(misc);
   volatile uint32_t* const tmem_holder =
       reinterpret_cast<volatile uint32_t*>(misc + 32 * C::SCHED);
@@ -325,12 +392,10 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
   const int lane = threadIdx.x & 31;
 
   // tiles of K-step slot q = stage * KSUB + (K step within the stage)
-  auto sW = [&](int q) { return base + q * C::SUB_BYTES; };
-  auto sX = [&](int q) { return base + q * C::SUB_BYTES + C::W_BYTES; };
-  auto sSFW = [&](int q) { return base + q * C::SUB_BYTES + C::W_BYTES + C::X_BYTES; };
-  auto sSFX = [&](int q) {
-    return base + q * C::SUB_BYTES + C::W_BYTES + C::X_BYTES + C::SFW_BYTES;
-  };
+  auto sW = [&](int q) { return base + q * C::OP_BYTES; };
+  auto sX = [&](int q) { return base + q * C::OP_BYTES + C::W_BYTES; };
+  auto sSFW = [&](int q) { return base + C::SF_REGION + q * C::SF_BYTES; };
+  auto sSFX = [&](int q) { return base + C::SF_REGION + q * C::SF_BYTES + C::SFW_BYTES; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -380,6 +445,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
     if (lane == 0 && !aborted_early) {
       int slot = 0;
       uint32_t sphase = 0;
+      const int num_tiles = p.num_tiles_dev != nullptr ? *p.num_tiles_dev : p.num_tiles;
       for (uint32_t n = 0;; ++n) {
         // Claim tile n only once the producer has taken tile n-1: a CTA holds
         // at most one tile it has not started, so the tail of the tile list
@@ -389,7 +455,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
                                  kStatusTimeoutProducer))
           break;
         const int t = atomicAdd(p.status + 1, 1);
-        const uint32_t tile = (t < p.num_tiles) ? __ldg(p.tiles + t) : kEndTile;
+        const uint32_t tile = (t < num_tiles) ? __ldg(p.tiles + t) : kEndTile;
         const SchedSlot s = make_slot<C::MX, C::BN>(p, tile);
         if (!mbar_wait1(schede_bar(slot), sphase ^ 1, abort_flag, p.status,
                         kStatusTimeoutProducer))
@@ -414,11 +480,9 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
       int slot = 0;
       uint32_t sphase = 0;
       uint32_t arms = 0;
-      if constexpr (C::MX) {
-        if (lane == 0) {
-          prefetch_tensormap(&p.mx_tmap_w);
-          prefetch_tensormap(&p.mx_tmap_x);
-        }
+      if (lane == 0) {
+        if constexpr (C::MX) prefetch_tensormap(&p.mx_tmap_w);
+        if (C::MX || p.x_flat) prefetch_tensormap(&p.tmap_x_flat);
       }
       while (true) {
         if (!mbar_wait(schedf_bar(slot), sphase, abort_flag, p.status, kStatusTimeoutProducer))
@@ -426,6 +490,7 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
         const uint32_t tile = __shfl_sync(kFullMask, ring[slot].tile, 0);
         const int xtile_index = __shfl_sync(kFullMask, ring[slot].xtile_index, 0);
         const int wgroup = __shfl_sync(kFullMask, ring[slot].wgroup, 0);
+        const int row0 = __shfl_sync(kFullMask, ring[slot].row0, 0);
         if (lane == 0) {
           mbar_arrive(schede_bar(slot));
           mbar_arrive(taken_bar);
@@ -454,14 +519,20 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
         }
         const CUtensorMap* tw;
         const CUtensorMap* tx;
+        // first token row of the tile in the map's coordinates
+        const int xrow = (C::MX || p.x_flat) ? row0 : xti * C::BN;
         if constexpr (C::MX) {
           tw = &p.mx_tmap_w;
-          tx = &p.mx_tmap_x;
+          tx = &p.tmap_x_flat;
         } else {
           tw = p.tmap_w + wgroup;
-          tx = p.tmap_x + g;
           tensormap_acquire(tw);  // every lane: the issuing one among them
-          tensormap_acquire(tx);
+          if (p.x_flat) {
+            tx = &p.tmap_x_flat;
+          } else {
+            tx = p.tmap_x + g;
+            tensormap_acquire(tx);
+          }
         }
         const uint8_t* sfx = p.sfx + size_t(xtile_index) * size_t(p.ksteps) * C::SFX_BYTES;
         const uint8_t* sfw =
@@ -487,13 +558,11 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
                 if (ks >= p.ksteps) break;
               }
               const int q = stage * C::KSUB + sub;
-              if constexpr (C::MX) {
+              if constexpr (C::MX)
                 tma_load_3d(sW(q), tw, fb, ks * C::K_STEP, nti * 128, g);
-                tma_load_2d(sX(q), tx, fb, ks * C::K_STEP, xti * C::BN);
-              } else {
+              else
                 tma_load_2d(sW(q), tw, fb, ks * 128, nti * 128);
-                tma_load_2d(sX(q), tx, fb, ks * 128, xti * C::BN);
-              }
+              tma_load_2d(sX(q), tx, fb, ks * 128, xrow);
               bulk_g2s(sSFW(q), sfw + size_t(ks) * C::SFW_BYTES, C::SFW_BYTES, fb);
               bulk_g2s(sSFX(q), sfx + size_t(ks) * C::SFX_BYTES, C::SFX_BYTES, fb);
             }
@@ -658,8 +727,8 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
         epilogue_tile_silu_mul(p.out, p.n / 2, nti * 128 + q * 32, size_t(s.row0), s.rows, ncols,
                                s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
       else
-        epilogue_tile(p.out, p.n, nti * 128 + q * 32 + lane, size_t(s.row0), s.rows, ncols,
-                      s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
+        epilogue_tile(p.out, p.n, nti * 128 + q * 32, size_t(s.row0), s.rows, ncols, s.alpha,
+                      p.row_scale, tmem + (uint32_t(q * 32) << 16) + b * C::BN, epi_stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(b));
@@ -728,11 +797,12 @@ struct PairCfg {
   static constexpr uint32_t SFX_ROW_U64 = SFX_BYTES / 8 > 256 ? 256 : SFX_BYTES / 8;
   static constexpr uint32_t SFX_BOX_ROWS = SFX_BYTES / (8 * SFX_ROW_U64);
   static constexpr uint32_t TX_CTA = W_TX + X_BYTES + SFW_BYTES + SFX_BYTES;
-  // bytes of one K step's tiles; a stage holds KSUB of them
-  static constexpr uint32_t SUB_BYTES =
-      (W_BYTES + X_BYTES + SFW_BYTES + SFX_BYTES + 1023) / 1024 * 1024;
-  static constexpr uint32_t STAGE_BYTES = KSUB * SUB_BYTES;
-  static_assert((W_BYTES + X_BYTES) % 1024 == 0, "operand tiles must stay 1024 B aligned");
+  // operand tiles and scale atoms of a K step in separate regions (see EngineCfg)
+  static constexpr uint32_t OP_BYTES = W_BYTES + X_BYTES;
+  static constexpr uint32_t SF_BYTES = SFW_BYTES + SFX_BYTES;
+  static constexpr uint32_t SUB_SLOTS = STAGES_ * KSUB;
+  static_assert(OP_BYTES % 1024 == 0, "operand tiles must stay 1024 B aligned");
+  static_assert(SF_BYTES % 128 == 0, "scale atoms must stay 128 B aligned");
   static constexpr int SF_BASE = 2 * BN;          // 448
   // [weights 4 | tokens 8]: per MMA (NVFP4) or per K step (MX)
   static constexpr int SF_SLOT = 12;
@@ -746,7 +816,10 @@ struct PairCfg {
   static constexpr uint32_t SCHED_READERS = 11;
   static constexpr uint32_t NBARS = 2 * STAGES + 4 + 2 * SCHED + 3;
   static constexpr uint32_t MISC_BYTES = 8 * NBARS + 32 * SCHED + 16;
-  static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + MISC_BYTES;
+  static constexpr uint32_t SF_REGION = SUB_SLOTS * OP_BYTES;
+  static constexpr uint32_t BAR_REGION = SF_REGION + SUB_SLOTS * SF_BYTES;
+  static constexpr uint32_t EPI_REGION = (BAR_REGION + MISC_BYTES + 15) / 16 * 16;
+  static constexpr uint32_t SMEM_BYTES = 1024 + EPI_REGION + kEpiStageBytes;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
 
@@ -758,7 +831,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
 
-  const uint32_t bars = base + C::STAGES * C::STAGE_BYTES;
+  const uint32_t bars = base + C::BAR_REGION;
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (C::STAGES + s); };
   auto accf_bar = [&](int b) { return bars + 8u * (2 * C::STAGES + b); };
@@ -768,7 +841,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   const uint32_t tmem_ready_bar = bars + 8u * (2 * C::STAGES + 4 + 2 * C::SCHED);
   const uint32_t drain_bar = tmem_ready_bar + 8u;
   const uint32_t taken_bar = tmem_ready_bar + 16u;  // producer took a slot
-  uint8_t* const misc = gbase + C::STAGES * C::STAGE_BYTES + 8 * C::NBARS;
+  uint8_t* const misc = gbase + C::BAR_REGION + 8 * C::NBARS;
+  // this warp's epilogue staging (warps 4-7)
+  uint32_t* const epi_stage = reinterpret_cast<uint32_t*>(
+      gbase + C::EPI_REGION + ((threadIdx.x >> 5) & 3) * (kEpiStageBytes / 4));
   volatile SchedSlot* const ring = reinterpret_cast<volatile SchedSlot*>(misc);
   volatile uint32_t* const tmem_holder =
       reinterpret_cast<volatile uint32_t*>(misc + 32 * C::SCHED);
@@ -781,12 +857,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   const uint32_t peer = rank ^ 1u;
 
   // tiles of K-step slot q = stage * KSUB + (K step within the stage)
-  auto sW = [&](int q) { return base + q * C::SUB_BYTES; };
-  auto sX = [&](int q) { return base + q * C::SUB_BYTES + C::W_BYTES; };
-  auto sSFW = [&](int q) { return base + q * C::SUB_BYTES + C::W_BYTES + C::X_BYTES; };
-  auto sSFX = [&](int q) {
-    return base + q * C::SUB_BYTES + C::W_BYTES + C::X_BYTES + C::SFW_BYTES;
-  };
+  auto sW = [&](int q) { return base + q * C::OP_BYTES; };
+  auto sX = [&](int q) { return base + q * C::OP_BYTES + C::W_BYTES; };
+  auto sSFW = [&](int q) { return base + C::SF_REGION + q * C::SF_BYTES; };
+  auto sSFX = [&](int q) { return base + C::SF_REGION + q * C::SF_BYTES + C::SFW_BYTES; };
   // MMA N of a tile: a multiple of 32 so that each CTA holds a multiple of 16 rows
   auto tile_ncols = [&](int rows) -> int { return min(C::BN, (rows + 31) & ~31); };
 
@@ -850,6 +924,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     if (lane == 0 && leader && !aborted_early) {
       int slot = 0;
       uint32_t sphase = 0;
+      const int num_tiles = p.num_tiles_dev != nullptr ? *p.num_tiles_dev : p.num_tiles;
       const uint32_t remote_ring0 = mapa_shared(smem_u32(const_cast<SchedSlot*>(ring)), peer);
       const uint32_t remote_schedf0 = mapa_shared(schedf_bar(0), peer);
       for (uint32_t n = 0;; ++n) {
@@ -858,7 +933,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                                  kStatusTimeoutProducer))
           break;
         const int t = atomicAdd(p.status + 1, 1);
-        const uint32_t tile = (t < p.num_tiles) ? __ldg(p.tiles + t) : kEndTile;
+        const uint32_t tile = (t < num_tiles) ? __ldg(p.tiles + t) : kEndTile;
         const SchedSlot s = make_slot<C::MX, C::BN>(p, tile);
         if (!mbar_wait1<true>(schede_bar(slot), sphase ^ 1, abort_flag, p.status,
                               kStatusTimeoutProducer))
@@ -886,10 +961,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       uint32_t sphase = 0;
       uint32_t arms = 0;
       if (lane == 0) {
-        if constexpr (C::MX) {
-          prefetch_tensormap(&p.mx_tmap_w);
-          prefetch_tensormap(&p.mx_tmap_x);
-        }
+        if constexpr (C::MX) prefetch_tensormap(&p.mx_tmap_w);
+        if (C::MX || p.x_flat) prefetch_tensormap(&p.tmap_x_flat);
         prefetch_tensormap(&p.sfw_map);
         prefetch_tensormap(&p.sfx_map);
       }
@@ -901,6 +974,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const int rows = __shfl_sync(kFullMask, ring[slot].rows, 0);
         const int xtile_index = __shfl_sync(kFullMask, ring[slot].xtile_index, 0);
         const int wgroup = __shfl_sync(kFullMask, ring[slot].wgroup, 0);
+        const int row0 = __shfl_sync(kFullMask, ring[slot].row0, 0);
         if (lane == 0) {
           release_slot(slot);
           if (leader) mbar_arrive(taken_bar);
@@ -929,15 +1003,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const CUtensorMap* tx;
         if constexpr (C::MX) {
           tw = &p.mx_tmap_w;
-          tx = &p.mx_tmap_x;
+          tx = &p.tmap_x_flat;
         } else {
           tw = p.tmap_w + wgroup;
-          tx = p.tmap_x + g;
           tensormap_acquire(tw);  // every lane: the issuing one among them
-          tensormap_acquire(tx);
+          if (p.x_flat) {
+            tx = &p.tmap_x_flat;
+          } else {
+            tx = p.tmap_x + g;
+            tensormap_acquire(tx);
+          }
         }
         const int wrow = nti * 256 + int(rank) * 128;
-        const int xrow = xti * C::BN + int(rank) * half;
+        // this CTA's first token row in the map's coordinates
+        const int xrow = ((C::MX || p.x_flat) ? row0 : xti * C::BN) + int(rank) * half;
         // this CTA's weight scale atoms of the tile: one row of SFW_BYTES per K step
         const int sfw_y =
             ((wgroup * p.nt128 + 2 * nti + int(rank)) * p.ksteps) * int(C::SFW_BOX_ROWS);
@@ -1131,8 +1210,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                                size_t(s.row0), s.rows, ncols, s.alpha,
                                tmem + (uint32_t(q * 32) << 16) + b * C::BN);
       else
-        epilogue_tile(p.out, p.n, nti * 256 + int(rank) * 128 + q * 32 + lane, size_t(s.row0),
-                      s.rows, ncols, s.alpha, tmem + (uint32_t(q * 32) << 16) + b * C::BN);
+        epilogue_tile(p.out, p.n, nti * 256 + int(rank) * 128 + q * 32, size_t(s.row0), s.rows,
+                      ncols, s.alpha, p.row_scale, tmem + (uint32_t(q * 32) << 16) + b * C::BN,
+                      epi_stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {

@@ -225,7 +225,7 @@ int fgg_mx_grouped_gemm(const FggMxProblem* p, void* workspace, size_t ws_bytes,
                          uint64_t(p->k), uint64_t(p->n), uint64_t(p->num_groups),
                          uint64_t(p->k) / 2, uint64_t(p->n) * uint64_t(p->k) / 2, 128, 128, 1))
     return rc;
-  if (int rc = encode_2d(&gp.mx_tmap_x, CU_TENSOR_MAP_DATA_TYPE_UINT8, p->a, uint64_t(p->k),
+  if (int rc = encode_2d(&gp.tmap_x_flat, CU_TENSOR_MAP_DATA_TYPE_UINT8, p->a, uint64_t(p->k),
                          uint64_t(p->m_total), uint64_t(p->k), 128,
                          L.pair ? CfgMxPair::BNH : kMxBlockM))
     return rc;

@@ -18,6 +18,10 @@
 
 namespace fgg {
 
+// activation bytes up to which the tile list runs weight-tile-major over all
+// groups (a quarter of the 126 MB L2: the weights in flight need the rest)
+constexpr int64_t kAcrossGroupsMaxBytes = 32ll << 20;
+
 // ------------------------------------------------------- prepare kernels
 // The per-group arrays travel as kernel parameters; CAP groups of room (a
 // small instance for the common few-group call keeps the launch light).
@@ -41,6 +45,19 @@ struct PrepParams {
   int32_t across_groups;
   int32_t sf_vec;  // 1: K % 256 == 0 and every a_sf[g] 16-byte aligned (vector repack)  // tile order: 1 weight-tile-major over all groups, 0 group-major
 };
+
+// Group whose tiles (its token tiles x nt weight tiles, group-major) hold tile t.
+__device__ __forceinline__ int find_group_tiles(const int32_t* begin, int g_count, int t, int nt) {
+  int lo = 0, hi = g_count;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (begin[mid] * nt <= t)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  return lo;
+}
 
 __device__ __forceinline__ int find_group(const int32_t* begin, int g_count, int x) {
   int lo = 0, hi = g_count;
@@ -186,6 +203,177 @@ __global__ void __launch_bounds__(256)
                             size_t(r0) * 16u) = make_uint4(v[0], v[1], v[2], v[3]);
 }
 
+// ------------------------------------------- prepare, device group offsets
+// The contiguous-rows form: every group's token rows lie in one buffer, group
+// g owning rows [offsets[g], offsets[g+1]) with the offsets in device memory
+// (written by an earlier kernel, e.g. an expert-parallel dispatch plan), so
+// the host never learns the group sizes.  Every block of this kernel rebuilds
+// the per-group token-tile prefix from the offsets in shared memory; block 0
+// also writes the status words, the tile count and the GroupInfo table.
+constexpr int kStatusBadOffsets = 0x203;  // offsets decreasing or past max_rows
+
+struct RowsPrepParams {
+  const int32_t* offsets;  // [G + 1] device
+  const int32_t* b_index;  // [G] device or null
+  const uint8_t* a_sf;     // [max_rows, K/16]
+  GroupInfo* ginfo_out;
+  uint32_t* tiles_out;
+  uint8_t* sfx_out;
+  int* status;             // [0] status [1] tile counter [2] finished CTAs [3] tile count
+  int32_t g, wg, k, bn, ch, nk64p, nt, max_rows;
+  int32_t tile_cap, xt_cap;  // room in tiles_out / token tiles in sfx_out
+  int32_t blocks_tiles;
+  int32_t sf_vec;     // K % 256 == 0 and a_sf 16-byte aligned
+  int32_t decode;     // decode tiles: never the across-groups order
+};
+
+// Shared-memory prefix of the token tiles per group: begin[g] for g <= G.
+// Returns the total, or -1 when the offsets are malformed.
+__device__ int rows_tile_prefix(const RowsPrepParams& p, int32_t* begin, int32_t* off) {
+  __shared__ int s_bad;
+  __shared__ int32_t s_warp[8];
+  if (threadIdx.x == 0) s_bad = 0;
+  for (int i = threadIdx.x; i <= p.g; i += blockDim.x) off[i] = __ldg(p.offsets + i);
+  __syncthreads();
+  // each thread sums the tiles of a contiguous run of groups
+  const int per = (p.g + blockDim.x - 1) / blockDim.x;
+  const int g0 = threadIdx.x * per, g1 = min(p.g, g0 + per);
+  int run = 0;
+  for (int g = g0; g < g1; ++g) {
+    const int m = off[g + 1] - off[g];
+    if (m < 0 || off[g] < 0 || off[g + 1] > p.max_rows) s_bad = 1;
+    run += m > 0 ? (m + p.bn - 1) / p.bn : 0;
+  }
+  // block-wide exclusive scan of the runs
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  int wbase = 0;
+  for (int w = 0; w < warp; ++w) wbase += s_warp[w];
+  int acc = wbase + incl - run;
+  for (int g = g0; g < g1; ++g) {
+    begin[g] = acc;
+    const int m = off[g + 1] - off[g];
+    acc += m > 0 ? (m + p.bn - 1) / p.bn : 0;
+  }
+  if (threadIdx.x == blockDim.x - 1) begin[p.g] = wbase + incl;
+  __syncthreads();
+  if (s_bad) return -1;
+  return begin[p.g];
+}
+
+__global__ void __launch_bounds__(256)
+    nvfp4_prepare_rows_kernel(const __grid_constant__ RowsPrepParams p) {
+  griddep_launch_dependents();
+  griddep_wait();
+  __shared__ int32_t sbegin[FGG_MAX_GROUPS + 1];
+  __shared__ int32_t soff[FGG_MAX_GROUPS + 1];
+  const int xt_total = rows_tile_prefix(p, sbegin, soff);
+  const bool bad = xt_total < 0 || xt_total > p.xt_cap;
+  const int num_tiles = bad ? 0 : xt_total * p.nt;
+  int blk = blockIdx.x;
+  if (blk == 0) {
+    if (threadIdx.x == 0) {
+      p.status[0] = bad ? kStatusBadOffsets : 0;
+      p.status[1] = 0;
+      p.status[2] = 0;
+      p.status[3] = num_tiles;
+    }
+    for (int g = threadIdx.x; g < p.g; g += blockDim.x) {
+      GroupInfo gi;
+      gi.m = bad ? 0 : soff[g + 1] - soff[g];
+      gi.out_row = soff[g];
+      gi.xtile_begin = bad ? 0 : sbegin[g];
+      int wg = p.b_index != nullptr ? __ldg(p.b_index + g) : g;
+      gi.wgroup = wg;
+      p.ginfo_out[g] = gi;
+    }
+    return;
+  }
+  if (bad) return;
+  blk -= 1;
+  if (blk < p.blocks_tiles) {
+    const int t = blk * blockDim.x + threadIdx.x;
+    if (t >= num_tiles) return;
+    const bool across = !p.decode && p.g > 1 &&
+                        int64_t(soff[p.g]) * (p.k / 2 + p.k / 16) <= kAcrossGroupsMaxBytes;
+    if (across) {
+      const int nti = t / xt_total;
+      const int X = t - nti * xt_total;
+      const int g = find_group(sbegin, p.g, X);
+      p.tiles_out[t] = pack_tile(g, nti, X - sbegin[g]);
+    } else {
+      // group-major: a group's tiles are its token tiles x NT weight tiles
+      const int X0 = find_group_tiles(sbegin, p.g, t, p.nt);
+      const int g = X0;
+      const int local = t - sbegin[g] * p.nt;
+      const int xts = sbegin[g + 1] - sbegin[g];
+      p.tiles_out[t] = pack_tile(g, local / xts, local % xts);
+    }
+    return;
+  }
+  blk -= p.blocks_tiles;
+  const int kq = p.k / 16;
+  if (p.sf_vec) {
+    const int64_t quad = int64_t(blk) * blockDim.x + threadIdx.x;
+    const int nk256 = p.nk64p / 4;
+    const int64_t quads_per_xt = int64_t(nk256) * p.ch * 32;
+    if (quad >= int64_t(xt_total) * quads_per_xt) return;
+    const int X = int(quad / quads_per_xt);
+    const int rem = int(quad - int64_t(X) * quads_per_xt);
+    const int s4 = rem / (p.ch * 32);
+    const int c = (rem / 32) % p.ch;
+    const int r0 = rem & 31;
+    const int g = find_group(sbegin, p.g, X);
+    const int xt = X - sbegin[g];
+    const int m = soff[g + 1] - soff[g];
+    uint4 v[4];
+#pragma unroll
+    for (int r1 = 0; r1 < 4; ++r1) {
+      const int rr = c * 128 + r1 * 32 + r0;
+      const int row = xt * p.bn + rr;
+      v[r1] = make_uint4(0u, 0u, 0u, 0u);
+      if (rr < p.bn && row < m)
+        v[r1] = __ldg(reinterpret_cast<const uint4*>(p.a_sf + size_t(soff[g] + row) * kq + 16 * s4));
+    }
+    uint8_t* dst = p.sfx_out + ((size_t(X) * p.nk64p + 4 * s4) * p.ch + c) * 512u + size_t(r0) * 16u;
+    const size_t jstride = size_t(p.ch) * 512u;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(v[0].x, v[1].x, v[2].x, v[3].x);
+    *reinterpret_cast<uint4*>(dst + jstride) = make_uint4(v[0].y, v[1].y, v[2].y, v[3].y);
+    *reinterpret_cast<uint4*>(dst + 2 * jstride) = make_uint4(v[0].z, v[1].z, v[2].z, v[3].z);
+    *reinterpret_cast<uint4*>(dst + 3 * jstride) = make_uint4(v[0].w, v[1].w, v[2].w, v[3].w);
+    return;
+  }
+  const int64_t line = int64_t(blk) * blockDim.x + threadIdx.x;
+  const int64_t lines_per_xt = int64_t(p.nk64p) * p.ch * 32;
+  if (line >= int64_t(xt_total) * lines_per_xt) return;
+  const int X = int(line / lines_per_xt);
+  const int rem = int(line - int64_t(X) * lines_per_xt);
+  const int j = rem / (p.ch * 32);
+  const int c = (rem / 32) % p.ch;
+  const int r0 = rem & 31;
+  const int g = find_group(sbegin, p.g, X);
+  const int xt = X - sbegin[g];
+  const int m = soff[g + 1] - soff[g];
+  uint32_t v[4];
+#pragma unroll
+  for (int r1 = 0; r1 < 4; ++r1) {
+    const int rr = c * 128 + r1 * 32 + r0;
+    const int row = xt * p.bn + rr;
+    v[r1] = 0u;
+    if (rr < p.bn && row < m && 4 * j < kq)
+      v[r1] = __ldg(reinterpret_cast<const uint32_t*>(p.a_sf + size_t(soff[g] + row) * kq + 4 * j));
+  }
+  *reinterpret_cast<uint4*>(p.sfx_out + ((size_t(X) * p.nk64p + j) * p.ch + c) * 512u +
+                            size_t(r0) * 16u) = make_uint4(v[0], v[1], v[2], v[3]);
+}
+
 struct PackParams {
   CUtensorMap tmpl;
   const uint8_t* b[FGG_MAX_GROUPS];
@@ -264,9 +452,6 @@ static PackLayout pack_layout(int g, int n, int k) {
   return L;
 }
 
-// activation bytes up to which the tile list runs weight-tile-major over all
-// groups (a quarter of the 126 MB L2: the weights in flight need the rest)
-constexpr int64_t kAcrossGroupsMaxBytes = 32ll << 20;
 
 struct WsLayout {
   int bn = 0, ch = 0, stages = 0;
@@ -625,6 +810,177 @@ int fgg_nvfp4_grouped_gemm_silu_mul(const FggNvfp4Problem* p, const void* pack, 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (int rc = prepare_impl(p, L, first, ws, s)) return rc;
   return gemm_impl(p, L, pack, ws, dev, s, kEpiSiluMul);
+}
+
+}  // extern "C"
+
+namespace fgg {
+namespace {
+
+struct RowsLayout {
+  int bn = 0, ch = 0, nk64p = 0, nk256 = 0, nt = 0, nt128 = 0, xt_cap = 0, tile_cap = 0;
+  bool pair = false, decode = false;
+  int box_rows = 0;
+  size_t status = 0, ginfo = 0, tiles = 0, sfx = 0, total = 0;
+};
+
+int plan_rows(const FggNvfp4RowsProblem* p, RowsLayout* L) {
+  if (p == nullptr) return set_error(FGG_EINVAL, "problem is null");
+  const int G = p->num_groups;
+  if (G < 1 || G > FGG_MAX_GROUPS)
+    return set_error(FGG_EINVAL, "num_groups=%d outside [1, %d]", G, FGG_MAX_GROUPS);
+  if (p->n <= 0 || p->n % 128 != 0)
+    return set_error(FGG_EBADSHAPE, "N=%d must be a positive multiple of 128", p->n);
+  if (p->k < 64 || p->k % 64 != 0)
+    return set_error(FGG_EBADSHAPE, "K=%d must be a positive multiple of 64", p->k);
+  if (p->n / 128 > 2047) return set_error(FGG_EBADSHAPE, "N=%d too large", p->n);
+  if (p->max_rows < 0) return set_error(FGG_EINVAL, "max_rows=%d is negative", p->max_rows);
+  if (p->b_index != nullptr &&
+      (p->num_weight_groups < 1 || p->num_weight_groups > FGG_MAX_GROUPS))
+    return set_error(FGG_EINVAL, "num_weight_groups=%d outside [1, %d]", p->num_weight_groups,
+                     FGG_MAX_GROUPS);
+  const int maxg = p->max_group_rows > 0 ? std::min(p->max_group_rows, p->max_rows) : p->max_rows;
+  L->decode = maxg <= 16;
+  L->pair = !L->decode && (p->n % 256 == 0);
+  L->bn = L->decode ? CfgDecode::BN : CfgPrefill::BN;
+  L->ch = L->decode ? CfgDecode::CH : CfgPrefill::CH;
+  L->box_rows = L->pair ? CfgPair::BNH : L->bn;
+  L->nk256 = (p->k + 255) / 256;
+  L->nk64p = 4 * L->nk256;
+  L->nt128 = p->n / 128;
+  L->nt = L->pair ? p->n / 256 : L->nt128;
+  // token tiles: sum_g ceil(M_g / BN) <= max_rows / BN + G
+  const int64_t xt_cap = (int64_t(p->max_rows) + L->bn - 1) / L->bn + G;
+  const int64_t tile_cap = xt_cap * L->nt;
+  if (xt_cap > INT32_MAX / 2 || tile_cap > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
+  if (int64_t(maxg + L->bn - 1) / L->bn > 2047)
+    return set_error(FGG_EBADSHAPE, "groups of up to %d rows are too large", maxg);
+  L->xt_cap = int(xt_cap);
+  L->tile_cap = int(tile_cap);
+  Carver cv;
+  L->status = cv.take(kStatusBytes, 256);
+  L->ginfo = cv.take(size_t(G) * sizeof(GroupInfo), 256);
+  L->tiles = cv.take(size_t(std::max<int64_t>(tile_cap, 1)) * 4, 256);
+  L->sfx = cv.take(size_t(std::max<int64_t>(xt_cap, 1)) * L->nk64p * L->ch * 512, 256);
+  L->total = cv.off;
+  return FGG_OK;
+}
+
+}  // namespace
+}  // namespace fgg
+
+extern "C" {
+
+size_t fgg_nvfp4_rows_workspace_bytes(const FggNvfp4RowsProblem* p) {
+  RowsLayout L;
+  if (plan_rows(p, &L) != FGG_OK) return 0;
+  return L.total;
+}
+
+int fgg_nvfp4_grouped_gemm_rows(const FggNvfp4RowsProblem* p, const void* pack, void* workspace,
+                                size_t ws_bytes, void* stream) {
+  RowsLayout L;
+  if (int rc = plan_rows(p, &L)) return rc;
+  if (workspace == nullptr) return set_error(FGG_EINVAL, "workspace is null");
+  if (!aligned16(workspace)) return set_error(FGG_EALIGN, "workspace must be 16-byte aligned");
+  if (ws_bytes < L.total)
+    return set_error(FGG_EWORKSPACE, "workspace has %zu bytes, needs %zu", ws_bytes, L.total);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (p->max_rows == 0) {
+    FGG_CUDA_CHECK(cudaMemsetAsync(ws + L.status, 0, kStatusBytes, s));
+    return FGG_OK;
+  }
+  if (p->offsets == nullptr || p->a == nullptr || p->a_sf == nullptr || p->alpha == nullptr ||
+      p->out == nullptr)
+    return set_error(FGG_EINVAL, "offsets / a / a_sf / alpha / out is null");
+  if (pack == nullptr) return set_error(FGG_EINVAL, "pack is null");
+  if (!aligned16(p->a) || !aligned16(p->out) || !aligned16(pack))
+    return set_error(FGG_EALIGN, "a, out and pack must be 16-byte aligned");
+  if (!aligned4(p->a_sf) || !aligned4(p->offsets) || !aligned4(p->alpha) ||
+      (p->row_scale != nullptr && !aligned4(p->row_scale)) ||
+      (p->b_index != nullptr && !aligned4(p->b_index)))
+    return set_error(FGG_EALIGN, "a_sf, offsets, alpha, row_scale and b_index must be 4-byte aligned");
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  const int G = p->num_groups;
+  const int wg = p->b_index != nullptr ? p->num_weight_groups : G;
+
+  RowsPrepParams pp;
+  memset(&pp, 0, sizeof(pp));
+  pp.offsets = p->offsets;
+  pp.b_index = p->b_index;
+  pp.a_sf = static_cast<const uint8_t*>(p->a_sf);
+  pp.ginfo_out = reinterpret_cast<GroupInfo*>(ws + L.ginfo);
+  pp.tiles_out = reinterpret_cast<uint32_t*>(ws + L.tiles);
+  pp.sfx_out = ws + L.sfx;
+  pp.status = reinterpret_cast<int*>(ws + L.status);
+  pp.g = G;
+  pp.wg = wg;
+  pp.k = p->k;
+  pp.bn = L.bn;
+  pp.ch = L.ch;
+  pp.nk64p = L.nk64p;
+  pp.nt = L.nt;
+  pp.max_rows = p->max_rows;
+  pp.tile_cap = L.tile_cap;
+  pp.xt_cap = L.xt_cap;
+  pp.blocks_tiles = (L.tile_cap + 255) / 256;
+  pp.sf_vec = (p->k % 256 == 0 && aligned16(p->a_sf)) ? 1 : 0;
+  pp.decode = L.decode ? 1 : 0;
+  const int64_t sf_lines = int64_t(L.xt_cap) * L.nk64p * L.ch * 32 / (pp.sf_vec ? 4 : 1);
+  const int64_t blocks = 1 + int64_t(pp.blocks_tiles) + (sf_lines + 255) / 256;
+  if (blocks > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
+  FGG_CUDA_CHECK(launch_dependent(nvfp4_prepare_rows_kernel, int(blocks), 0, s, pp));
+  FGG_CUDA_CHECK(cudaGetLastError());
+
+  const uint8_t* pk = static_cast<const uint8_t*>(pack);
+  const PackLayout PL = pack_layout(wg, p->n, p->k);
+  GemmParams gp;
+  memset(&gp, 0, sizeof(gp));
+  if (int rc = encode_u8_2d(&gp.tmap_x_flat, p->a, uint64_t(p->k) / 2, uint64_t(p->max_rows), 128,
+                            uint32_t(L.box_rows)))
+    return rc;
+  gp.x_flat = 1;
+  gp.tmap_w = reinterpret_cast<const CUtensorMap*>(pk + PL.tmaps);
+  gp.sfw = pk + PL.sfw;
+  gp.sfx = ws + L.sfx;
+  gp.ginfo = reinterpret_cast<const GroupInfo*>(ws + L.ginfo);
+  gp.tiles = reinterpret_cast<const uint32_t*>(ws + L.tiles);
+  gp.alpha = p->alpha;
+  gp.row_scale = p->row_scale;
+  gp.pack = reinterpret_cast<const PackHeader*>(pk + PL.header);
+  gp.out = static_cast<__nv_bfloat16*>(p->out);
+  gp.status = reinterpret_cast<int*>(ws + L.status);
+  gp.num_tiles_dev = reinterpret_cast<const int32_t*>(ws + L.status) + 3;
+  gp.g = G;
+  gp.wg = wg;
+  gp.n = p->n;
+  gp.k = p->k;
+  gp.epi = kEpiPlain;
+  gp.num_tiles = L.tile_cap;  // the launch's grid bound; the kernels read the real count
+  gp.ksteps = L.nk256;
+  gp.nt = L.nt;
+  gp.nt128 = L.nt128;
+  gp.debug_flags = debug_flags();
+  cudaError_t e;
+  if (L.pair) {
+    if (int rc = encode_u64_rows(&gp.sfw_map, gp.sfw,
+                                 uint64_t(wg) * L.nt128 * L.nk256 * CfgPair::SFW_BOX_ROWS,
+                                 CfgPair::SFW_ROW_U64, CfgPair::SFW_BOX_ROWS))
+      return rc;
+    if (int rc = encode_u64_rows(&gp.sfx_map, gp.sfx,
+                                 uint64_t(L.xt_cap) * L.nk256 * CfgPair::SFX_BOX_ROWS,
+                                 CfgPair::SFX_ROW_U64, CfgPair::SFX_BOX_ROWS))
+      return rc;
+    e = launch_pair<CfgPair>(gp, dev.sm_count, s);
+  } else if (L.decode) {
+    e = launch_engine<CfgDecode>(gp, dev.sm_count, s);
+  } else {
+    e = launch_engine<CfgPrefill>(gp, dev.sm_count, s);
+  }
+  if (e != cudaSuccess) return set_error(FGG_ECUDA, "GEMM launch failed: %s", cudaGetErrorString(e));
+  return FGG_OK;
 }
 
 }  // extern "C"
