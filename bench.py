@@ -872,9 +872,12 @@ def run_moe(args, wl):
     """one expert-parallel MoE projection over N ranks.
     The 4096 tokens are split evenly over the ranks (each rank routes its own
     share); the 64 experts are placed by expected load (LPT, equal counts).
-    A step = plan + all-to-all dispatch + grouped GEMM + all-to-all combine
-    with the router-weighted sum per token.  Total work is fixed, so the
-    scaling is strong; value = all FLOPs / the slowest rank's step time."""
+    A step = pack + all-gather dispatch + expand + grouped GEMM + weighted
+    reduce + all-to-all combine + partial sum, with no host synchronisation.
+    Total work is fixed, so the scaling is strong; value = all FLOPs / the
+    slowest rank's step time.  The line carries a per-phase breakdown (CUDA
+    events between the phases on the compute stream, mean over the timed
+    steps, max over ranks)."""
     from ratchet_b200 import moe
 
     ws, rank, local = dist_init()
@@ -888,12 +891,12 @@ def run_moe(args, wl):
     d = moe_setup(wl, ws, rank, dev)
     tl, ids_all, mine = d["tl"], d["ids_all"], d["mine"]
     xc, xs, xg, ids, wts = d["xc"], d["xs"], d["xg"], d["ids"], d["wts"]
-    layer = moe.ExpertParallelMoE(d["wc"], d["wsf"], d["wg"], d["owner"], d["slot"])
+    layer = moe.ExpertParallelMoE(d["wc"], d["wsf"], d["wg"], d["owner"], d["slot"], max_tokens=tl)
     torch.cuda.synchronize()
     fl = 2.0 * T * topk * n * k
 
     def step(ev=None):
-        return layer.forward(xc, xs, xg, ids, wts, gemm_events=ev)
+        return layer.forward(xc, xs, xg, ids, wts, events=ev)
 
     for _ in range(args.warmup):
         step()
@@ -903,19 +906,24 @@ def run_moe(args, wl):
     sampler = ClockSampler(local)
     sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    gev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
+    evs = [dict() for _ in range(args.steps)]
     e0.record()
     for i in range(args.steps):
-        step(gev[i])
+        step(evs[i])
     e1.record()
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
     clocks = sampler.stop()
+    layer.check()
     rb.last_status()
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws, dev)
-    g_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in gev) / args.steps, ws, dev)
+    names = list(moe.PHASES) + ["end"]
+    phases = {}
+    for a, b in zip(names[:-1], names[1:]):
+        mean = sum(ev[a].elapsed_time(ev[b]) for ev in evs) / args.steps
+        phases[a] = max_over_ranks(mean, ws, dev)
+    g_ms = phases["gemm"]
     # GEMM rows on this rank (the kernel's FLOPs): the routes of its experts from every rank
     counts = np.bincount(ids_all.ravel(), minlength=E)
     my_rows = int(counts[np.asarray(mine)].sum())
@@ -926,15 +934,15 @@ def run_moe(args, wl):
     roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
             "frac": achieved / peak, "traffic": traffic_from_profiles("moe"),
             "peak_basis": f"4 x {pk['src']} dense bf16 ({pk['bf16']:.0f} TF/s)",
-            "kernel_ms": g_ms, "kernel": "grouped GEMM inside the layer (prepare + GEMM), "
-                                        "slowest rank"}
+            "kernel_ms": g_ms, "kernel": "grouped GEMM inside the layer (device-offset prepare + "
+                                        "fgg_gemm_pair_kernel), slowest rank"}
 
     # end to end: this rank's activations from pinned host memory, the output back
     h_xc = xc.cpu().pin_memory()
     h_xs = xs.view(torch.uint8).cpu().pin_memory()
     d_xc, d_xs = torch.empty_like(xc), torch.empty_like(xs.view(torch.uint8))
     h_out = torch.empty((tl, n), dtype=torch.bfloat16).pin_memory()
-    e2e_steps = max(3, args.steps // 2)
+    e2e_steps = args.steps
 
     def e2e_step():
         d_xc.copy_(h_xc, non_blocking=True)
@@ -967,13 +975,18 @@ def run_moe(args, wl):
             "config": {"workload": wl["desc"], "tokens": T, "experts": E, "topk": topk,
                        "n": n, "k": k, "parallelism": f"ep{ws}",
                        "placement": "LPT on expected expert load, equal expert counts",
+                       "dispatch": "NCCL all-gather of token records (capacity = tokens per rank)"
+                                   if ws > 1 else "none (one rank)",
+                       "combine": "NCCL all-to-all of router-weighted partial rows, fp32 sum"
+                                  if ws > 1 else "router-weighted sum on the rank",
                        "l2": f"expert weights {E * n * k * 0.5625 / ws / 1e6:.0f} MB per rank "
                              "read every step"},
+            "phases_ms": phases,
             "clocks": clocks,
             "e2e": {"value": fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": int(h_xc.numel() + h_xs.numel()) * ws,
                     "d2h_bytes_per_step": int(h_out.numel() * 2) * ws, "ms_per_step": e2e_ms},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": (7 if ws > 1 else 5) * args.steps,
             "roofline": roof,
             "cpu_baseline": cpu_sample(wl) if (ws == 1 and not args.no_cpu) else None,
         }
@@ -983,7 +996,6 @@ def run_moe(args, wl):
 
         dist.destroy_process_group()
     return 0
-
 
 
 def run_mlp(args, wl):

@@ -286,6 +286,71 @@ FGG_API int fgg_moe_combine(const void* rows, int64_t num_rows, const int32_t* r
                             const float* weights, int32_t num_tokens, int32_t topk, int32_t n,
                             void* out, int* bad, void* stream);
 
+/* The expert-parallel layer without a host synchronisation.  No counterpart
+ * in the reference's code (it has no distributed path); the single-GPU
+ * analogue is `_moe_forward` (tasks/muse_prefill_boundary/reference/
+ * submission.py:843-895: gather plan, grouped expert GEMM, weighted combine).
+ * A dispatch buffer that can never overflow gives every (source, destination)
+ * pair room for all of the source's tokens, which is the byte count of an
+ * all-gather of the tokens: so each rank packs its tokens into records
+ * (fgg_moe_pack_tokens), the ranks all-gather them, each rank expands the
+ * routes of its own experts into expert-ordered rows (fgg_moe_expand_plan,
+ * fgg_moe_expand_rows), runs fgg_nvfp4_grouped_gemm_rows on them with the
+ * plan's offsets, sums every token's local routes with its router weights
+ * (fgg_moe_reduce) and the ranks exchange those partial rows with an
+ * equal-split all-to-all that each rank sums (fgg_moe_sum_partials).  All
+ * sizes stay on the device.
+ *
+ * Tokens are described by strided views so that one set of kernels reads a
+ * caller's own tensors or the gathered records alike; strides are in bytes. */
+typedef struct FggMoeTokens {
+  int32_t num_tokens;
+  int32_t topk;
+  int32_t k;                 /* hidden size: codes K/2 bytes, scales K/16 bytes */
+  const void* codes;         int64_t codes_stride;
+  const void* sf;            int64_t sf_stride;
+  const int32_t* ids;        int64_t ids_stride;      /* topk expert ids per token  */
+  const float* weights;      int64_t weights_stride;  /* topk router weights; NULL = 1 */
+  const float* scale;        int64_t scale_stride;    /* decode scale; stride 0 = one */
+} FggMoeTokens;
+
+/* Bytes of one token record: codes, scales, ids, weights, decode scale,
+ * padded to 16 bytes (0 for a bad geometry). */
+FGG_API size_t fgg_moe_record_bytes(int32_t k, int32_t topk);
+/* Write one record per token into `records` (device, 16-byte aligned). */
+FGG_API int fgg_moe_pack_tokens(const FggMoeTokens* tokens, void* records, void* stream);
+/* Host-only: a view of `num_tokens` consecutive records as FggMoeTokens. */
+FGG_API int fgg_moe_records_view(const void* records, int32_t num_tokens, int32_t k, int32_t topk,
+                                 FggMoeTokens* out);
+/* Plan of this rank's routes: offsets[0..local] (device) place the routes of
+ * local expert s (slot) at rows [offsets[s], offsets[s+1]); route_row[t*topk+k]
+ * is route (t, k)'s row or -1 (another rank's expert, or an absent route:
+ * expert id < 0, as on the padding tokens of a fixed-capacity dispatch);
+ * src_token[row] and row_scale[row] (the token's decode scale) describe each
+ * row.  An expert id >= num_experts sets *bad = 1; more routes than max_rows
+ * sets *bad = 2 (the excess is dropped).  local <= 1024. */
+FGG_API int fgg_moe_expand_plan(const FggMoeTokens* tokens, const int32_t* owner,
+                                const int32_t* slot, int32_t num_experts, int32_t rank,
+                                int32_t local, int32_t max_rows, int32_t* offsets,
+                                int32_t* route_row, int32_t* src_token, float* row_scale, int* bad,
+                                void* stream);
+/* Expanded rows: row r = token src_token[r]'s codes and scales, for
+ * r < *count (device, e.g. offsets + local), at most max_rows. */
+FGG_API int fgg_moe_expand_rows(const FggMoeTokens* tokens, const int32_t* src_token,
+                                const int32_t* count, int32_t max_rows, void* out_codes,
+                                void* out_sf, int* bad, void* stream);
+/* out[t, :] = bf16(sum_k weights[t, k] * rows[route_row[t*topk + k], :]) over
+ * the routes with a row (>= 0), fp32 accumulation; zeros for a token with
+ * none.  rows bf16 [num_rows, n]; n % 8 == 0. */
+FGG_API int fgg_moe_reduce(const void* rows, int32_t num_rows, const int32_t* route_row,
+                           const FggMoeTokens* tokens, int32_t n, void* out, int* bad,
+                           void* stream);
+/* out[t, :] = bf16(sum_s parts[s * per_source + t, :]) in fp32 for t < tokens:
+ * the partial rows every rank returned for this rank's tokens (per_source =
+ * the dispatch capacity per rank). */
+FGG_API int fgg_moe_sum_partials(const void* parts, int32_t world, int32_t per_source,
+                                 int32_t tokens, int32_t n, void* out, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* NVFP4 quantisation (activations and weights)                              */
 /* ------------------------------------------------------------------------ */

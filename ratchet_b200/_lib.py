@@ -52,6 +52,15 @@ class FggMxProblem(ctypes.Structure):
                 ("reuse_prepared", ctypes.c_int32)]
 
 
+class FggMoeTokens(ctypes.Structure):
+    _fields_ = [("num_tokens", ctypes.c_int32), ("topk", ctypes.c_int32), ("k", ctypes.c_int32),
+                ("codes", _VOIDP), ("codes_stride", ctypes.c_int64),
+                ("sf", _VOIDP), ("sf_stride", ctypes.c_int64),
+                ("ids", _VOIDP), ("ids_stride", ctypes.c_int64),
+                ("weights", _VOIDP), ("weights_stride", ctypes.c_int64),
+                ("scale", _VOIDP), ("scale_stride", ctypes.c_int64)]
+
+
 class FggError(RuntimeError):
     def __init__(self, code: int, where: str, detail: str):
         self.code = code
@@ -78,6 +87,19 @@ _SIGS = {
                                            _VOIDP, ctypes.c_int64, _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
     "fgg_moe_combine": (ctypes.c_int, [_VOIDP, ctypes.c_int64, _VOIDP, _VOIDP, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP]),
+    "fgg_moe_record_bytes": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32]),
+    "fgg_moe_pack_tokens": (ctypes.c_int, [ctypes.POINTER(FggMoeTokens), _VOIDP, _VOIDP]),
+    "fgg_moe_records_view": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.POINTER(FggMoeTokens)]),
+    "fgg_moe_expand_plan": (ctypes.c_int, [ctypes.POINTER(FggMoeTokens), _VOIDP, _VOIDP, ctypes.c_int32,
+                                           ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _VOIDP, _VOIDP,
+                                           _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
+    "fgg_moe_expand_rows": (ctypes.c_int, [ctypes.POINTER(FggMoeTokens), _VOIDP, _VOIDP, ctypes.c_int32,
+                                           _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
+    "fgg_moe_reduce": (ctypes.c_int, [_VOIDP, ctypes.c_int32, _VOIDP, ctypes.POINTER(FggMoeTokens),
+                                      ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP]),
+    "fgg_moe_sum_partials": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int32, _VOIDP, _VOIDP]),
     "fgg_nvfp4_grouped_gemm_silu_mul": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_mx_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(FggMxProblem)]),
     "fgg_mx_grouped_gemm": (ctypes.c_int, [ctypes.POINTER(FggMxProblem), _VOIDP, ctypes.c_size_t, _VOIDP]),

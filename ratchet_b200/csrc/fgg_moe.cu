@@ -10,7 +10,10 @@
 // (tasks/muse_prefill_boundary/reference/submission.py:843-895).
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "fgg_host.cuh"
+#include "fgg_ptx.cuh"
 
 namespace fgg {
 namespace {
@@ -191,12 +194,435 @@ __global__ void __launch_bounds__(kPlanWarps * 32) plan_kernel(
   }
 }
 
+// ---- the expert-parallel layer without a host synchronisation -------------
+//
+// The dispatch may send any token of a rank to any rank, so an exchange
+// buffer that can never overflow gives each (source, destination) pair room
+// for all of the source's tokens.  At that capacity the dispatch moves the
+// bytes of an all-gather of the tokens: every token leaves its rank once as
+// one record (codes, scales, expert ids, router weights, decode scale) and
+// each rank expands the routes of its own experts.  The combine sends one
+// router-weighted partial row per (token, rank) back along an equal-split
+// all-to-all and the token's rank sums those rows in fp32.  No size ever has
+// to reach the host, so nothing in the layer synchronises it.
+
+struct MoeTok {
+  const uint8_t* codes;
+  const uint8_t* sf;
+  const uint8_t* ids;
+  const uint8_t* weights;
+  const uint8_t* scale;
+  int64_t codes_stride, sf_stride, ids_stride, weights_stride, scale_stride;
+  int32_t num_tokens, topk, k;
+};
+
+__device__ __forceinline__ int32_t tok_id(const MoeTok& t, int64_t i, int k) {
+  return __ldg(reinterpret_cast<const int32_t*>(t.ids + i * t.ids_stride) + k);
+}
+__device__ __forceinline__ float tok_weight(const MoeTok& t, int64_t i, int k) {
+  return t.weights == nullptr
+             ? 1.0f
+             : __ldg(reinterpret_cast<const float*>(t.weights + i * t.weights_stride) + k);
+}
+__device__ __forceinline__ float tok_scale(const MoeTok& t, int64_t i) {
+  return t.scale == nullptr ? 1.0f
+                            : __ldg(reinterpret_cast<const float*>(t.scale + i * t.scale_stride));
+}
+
+// Copy `bytes` (a multiple of 16, both ends 16-byte aligned) with the calling
+// warp: each lane moves every 32nd 16-byte vector.
+__device__ __forceinline__ void warp_copy16(uint8_t* __restrict__ dst,
+                                            const uint8_t* __restrict__ src, int bytes) {
+  const int n = bytes / 16;
+  for (int i = threadIdx.x & 31; i < n; i += 32)
+    reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+}
+// Same with 4-byte words (multiples of 4, 4-byte aligned).
+__device__ __forceinline__ void warp_copy4(uint8_t* __restrict__ dst,
+                                           const uint8_t* __restrict__ src, int bytes) {
+  const int n = bytes / 4;
+  for (int i = threadIdx.x & 31; i < n; i += 32)
+    reinterpret_cast<uint32_t*>(dst)[i] = __ldg(reinterpret_cast<const uint32_t*>(src) + i);
+}
+
+// One token record per warp: [codes K/2][scales K/16][ids topk][weights topk][scale].
+template <bool kVec>
+__global__ void __launch_bounds__(256) moe_pack_kernel(MoeTok t, uint8_t* __restrict__ rec,
+                                                       int64_t rec_bytes) {
+  const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (i >= t.num_tokens) return;
+  const int lane = threadIdx.x & 31;
+  uint8_t* r = rec + i * rec_bytes;
+  const int kh = t.k / 2, ks = t.k / 16;
+  if (kVec) {
+    warp_copy16(r, t.codes + i * t.codes_stride, kh);
+    warp_copy16(r + kh, t.sf + i * t.sf_stride, ks);
+  } else {
+    warp_copy4(r, t.codes + i * t.codes_stride, kh);
+    warp_copy4(r + kh, t.sf + i * t.sf_stride, ks);
+  }
+  int32_t* ids = reinterpret_cast<int32_t*>(r + kh + ks);
+  float* w = reinterpret_cast<float*>(ids + t.topk);
+  for (int k = lane; k < t.topk; k += 32) {
+    ids[k] = tok_id(t, i, k);
+    w[k] = tok_weight(t, i, k);
+  }
+  if (lane == 0) w[t.topk] = tok_scale(t, i);
+}
+
+// Expand plan, one block: the routes of this rank's experts, counted per
+// local expert (slot), their rows placed expert by expert.  Route (i, k) to a
+// local expert gets row route_row[i * topk + k] in the expanded buffer, which
+// holds token src_token[row] scaled by row_scale[row] (its source's decode
+// scale).  Routes to other ranks and absent routes (expert id < 0, e.g. the
+// padding tokens of a fixed-capacity dispatch) get -1; an expert id >= E or
+// a placement outside the local slots sets *bad and gets -1.  The order inside
+// an expert follows the atomics: every expanded row is computed on its own
+// and summed back in route order, so the results do not depend on it.
+constexpr int kExpandThreads = 1024;
+constexpr int kExpandMaxLocal = 1024;
+
+__global__ void __launch_bounds__(kExpandThreads)
+    moe_expand_plan_kernel(MoeTok t, const int32_t* __restrict__ owner,
+                           const int32_t* __restrict__ slot, int32_t num_experts, int32_t rank,
+                           int32_t local, int32_t max_rows, int32_t* __restrict__ offsets,
+                           int32_t* __restrict__ route_row, int32_t* __restrict__ src_token,
+                           float* __restrict__ row_scale, int* __restrict__ bad) {
+  griddep_wait();
+  __shared__ int32_t cnt[kExpandMaxLocal];
+  __shared__ int32_t base[kExpandMaxLocal + 1];
+  for (int i = threadIdx.x; i < local; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int64_t routes = int64_t(t.num_tokens) * t.topk;
+  auto local_slot = [&](int64_t r) -> int {
+    const int e = tok_id(t, r / t.topk, int(r % t.topk));
+    if (e < 0) return -1;  // an absent route (a padding token's)
+    if (e >= num_experts) {
+      atomicExch(bad, 1);
+      return -1;
+    }
+    if (__ldg(owner + e) != rank) return -1;
+    const int s = __ldg(slot + e);
+    if (s < 0 || s >= local) {
+      atomicExch(bad, 1);
+      return -1;
+    }
+    return s;
+  };
+  for (int64_t r = threadIdx.x; r < routes; r += blockDim.x) {
+    const int s = local_slot(r);
+    if (s >= 0) atomicAdd(&cnt[s], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int s = 0; s < local; ++s) {
+      base[s] = run;
+      run += cnt[s];
+    }
+    base[local] = run;
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s <= local; s += blockDim.x) offsets[s] = min(base[s], max_rows);
+  for (int i = threadIdx.x; i < local; i += blockDim.x) cnt[i] = 0;  // cursors
+  __syncthreads();
+  for (int64_t r = threadIdx.x; r < routes; r += blockDim.x) {
+    const int s = local_slot(r);
+    int row = -1;
+    if (s >= 0) {
+      row = base[s] + atomicAdd(&cnt[s], 1);
+      if (row >= max_rows) {  // the caller's buffer is too small: flag, drop
+        atomicExch(bad, 2);
+        row = -1;
+      } else {
+        const int64_t tok = r / t.topk;
+        src_token[row] = int32_t(tok);
+        row_scale[row] = tok_scale(t, tok);
+      }
+    }
+    route_row[r] = row;
+  }
+  // the grouped GEMM behind this kernel may launch now
+  griddep_launch_dependents();
+}
+
+// Expanded rows: row r of the expert-ordered buffer is token src_token[r]'s
+// codes and scales, one warp per row.  The row count is the plan's last
+// offset (device), so the grid's warps stride over at most max_rows rows.
+template <bool kVec>
+__global__ void __launch_bounds__(256) moe_expand_rows_kernel(MoeTok t,
+                                                              const int32_t* __restrict__ src_token,
+                                                              const int32_t* __restrict__ count,
+                                                              int32_t max_rows,
+                                                              uint8_t* __restrict__ out_codes,
+                                                              uint8_t* __restrict__ out_sf,
+                                                              int* __restrict__ bad) {
+  griddep_wait();
+  const int rows = min(*count, max_rows);
+  const int kh = t.k / 2, ks = t.k / 16;
+  const int warps = int(gridDim.x * blockDim.x) >> 5;
+  // one row per warp at a time
+  for (int r = int((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r < rows; r += warps) {
+    const int64_t tok = src_token[r];
+    if (tok < 0 || tok >= t.num_tokens) {
+      if ((threadIdx.x & 31) == 0) atomicExch(bad, 1);
+      continue;
+    }
+    if (kVec) {
+      warp_copy16(out_codes + int64_t(r) * kh, t.codes + tok * t.codes_stride, kh);
+      warp_copy16(out_sf + int64_t(r) * ks, t.sf + tok * t.sf_stride, ks);
+    } else {
+      warp_copy4(out_codes + int64_t(r) * kh, t.codes + tok * t.codes_stride, kh);
+      warp_copy4(out_sf + int64_t(r) * ks, t.sf + tok * t.sf_stride, ks);
+    }
+  }
+  griddep_launch_dependents();
+}
+
+// Router-weighted sum of a token's local routes: out[i, :] =
+// bf16(sum_k w[i, k] * rows[route_row[i * topk + k], :]) over the routes with
+// a row (>= 0); a token with none gets a zero row.  fp32 accumulation, each
+// thread 8 consecutive columns.
+__global__ void __launch_bounds__(256) moe_reduce_kernel(MoeTok t,
+                                                         const __nv_bfloat16* __restrict__ rows,
+                                                         int32_t num_rows,
+                                                         const int32_t* __restrict__ route_row,
+                                                         int32_t n, __nv_bfloat16* __restrict__ out,
+                                                         int* __restrict__ bad) {
+  griddep_wait();
+  const int64_t i = blockIdx.x;
+  const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (i >= t.num_tokens || col >= n) return;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  for (int k = 0; k < t.topk; ++k) {
+    const int r = route_row[i * t.topk + k];
+    if (r < 0) continue;
+    if (r >= num_rows) {
+      atomicExch(bad, 1);
+      continue;
+    }
+    const float wk = tok_weight(t, i, k);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(rows + int64_t(r) * n + col));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      acc[2 * j] = fmaf(wk, f.x, acc[2 * j]);
+      acc[2 * j + 1] = fmaf(wk, f.y, acc[2 * j + 1]);
+    }
+  }
+  uint4 o;
+  __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+  *reinterpret_cast<uint4*>(out + i * n + col) = o;
+}
+
+// out[i, :] = bf16(sum_s parts[s * per_source + i, :]) in fp32 (the partial
+// rows every rank sent back for this rank's tokens).
+__global__ void __launch_bounds__(256) moe_sum_parts_kernel(const __nv_bfloat16* __restrict__ parts,
+                                                            int32_t world, int32_t per_source,
+                                                            int32_t tokens, int32_t n,
+                                                            __nv_bfloat16* __restrict__ out) {
+  griddep_wait();
+  const int64_t i = blockIdx.x;
+  const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (i >= tokens || col >= n) return;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  for (int s = 0; s < world; ++s) {
+    const uint4 v =
+        __ldg(reinterpret_cast<const uint4*>(parts + (int64_t(s) * per_source + i) * n + col));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      acc[2 * j] += f.x;
+      acc[2 * j + 1] += f.y;
+    }
+  }
+  uint4 o;
+  __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+  *reinterpret_cast<uint4*>(out + i * n + col) = o;
+}
+
+int to_dev(const FggMoeTokens* t, MoeTok* d) {
+  if (t == nullptr) return set_error(FGG_EINVAL, "tokens is null");
+  if (t->num_tokens < 0 || t->topk < 1 || t->k < 64 || t->k % 64 != 0)
+    return set_error(FGG_EBADSHAPE, "need num_tokens >= 0, topk >= 1, K a multiple of 64");
+  if (t->num_tokens > 0 && (t->ids == nullptr))
+    return set_error(FGG_EINVAL, "ids is null");
+  d->codes = static_cast<const uint8_t*>(t->codes);
+  d->sf = static_cast<const uint8_t*>(t->sf);
+  d->ids = reinterpret_cast<const uint8_t*>(t->ids);
+  d->weights = reinterpret_cast<const uint8_t*>(t->weights);
+  d->scale = reinterpret_cast<const uint8_t*>(t->scale);
+  d->codes_stride = t->codes_stride;
+  d->sf_stride = t->sf_stride;
+  d->ids_stride = t->ids_stride;
+  d->weights_stride = t->weights_stride;
+  d->scale_stride = t->scale_stride;
+  d->num_tokens = t->num_tokens;
+  d->topk = t->topk;
+  d->k = t->k;
+  if ((t->ids_stride & 3) || (t->weights_stride & 3) || (t->scale_stride & 3) ||
+      !aligned4(t->ids) || !aligned4(t->weights) || !aligned4(t->scale))
+    return set_error(FGG_EALIGN, "ids, weights and scale (and their strides) must be 4-byte aligned");
+  return FGG_OK;
+}
+
+// 16-byte rows when every row start is 16-byte aligned, 4-byte otherwise.
+bool rows_vec16(const MoeTok& t) {
+  return aligned16(t.codes) && aligned16(t.sf) && t.codes_stride % 16 == 0 &&
+         t.sf_stride % 16 == 0 && (t.k / 16) % 16 == 0;
+}
+bool rows_vec4(const MoeTok& t) {
+  return aligned4(t.codes) && aligned4(t.sf) && t.codes_stride % 4 == 0 && t.sf_stride % 4 == 0 &&
+         (t.k / 16) % 4 == 0;
+}
+
 }  // namespace
 }  // namespace fgg
 
 using namespace fgg;
 
 extern "C" {
+
+size_t fgg_moe_record_bytes(int32_t k, int32_t topk) {
+  if (k < 64 || k % 64 != 0 || topk < 1) return 0;
+  return align_up(size_t(k) / 2 + size_t(k) / 16 + 8u * size_t(topk) + 4u, 16);
+}
+
+int fgg_moe_pack_tokens(const FggMoeTokens* tokens, void* records, void* stream) {
+  MoeTok t;
+  if (int rc = to_dev(tokens, &t)) return rc;
+  if (t.num_tokens == 0) return FGG_OK;
+  if (records == nullptr || t.codes == nullptr || t.sf == nullptr)
+    return set_error(FGG_EINVAL, "records / codes / sf is null");
+  const size_t rb = fgg_moe_record_bytes(t.k, t.topk);
+  if (!aligned16(records)) return set_error(FGG_EALIGN, "records must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = unsigned((int64_t(t.num_tokens) + 7) / 8);  // 8 warps = 8 records a block
+  if (rows_vec16(t))
+    moe_pack_kernel<true><<<grid, 256, 0, s>>>(t, static_cast<uint8_t*>(records), int64_t(rb));
+  else if (rows_vec4(t))
+    moe_pack_kernel<false><<<grid, 256, 0, s>>>(t, static_cast<uint8_t*>(records), int64_t(rb));
+  else
+    return set_error(FGG_EALIGN, "token rows must start on 4-byte boundaries");
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+int fgg_moe_records_view(const void* records, int32_t num_tokens, int32_t k, int32_t topk,
+                         FggMoeTokens* out) {
+  if (out == nullptr) return set_error(FGG_EINVAL, "out is null");
+  const size_t rb = fgg_moe_record_bytes(k, topk);
+  if (rb == 0 || num_tokens < 0) return set_error(FGG_EBADSHAPE, "bad record geometry");
+  const uint8_t* r = static_cast<const uint8_t*>(records);
+  const size_t kh = size_t(k) / 2, ks = size_t(k) / 16;
+  out->num_tokens = num_tokens;
+  out->topk = topk;
+  out->k = k;
+  out->codes = r;
+  out->sf = r + kh;
+  out->ids = reinterpret_cast<const int32_t*>(r + kh + ks);
+  out->weights = reinterpret_cast<const float*>(r + kh + ks + 4 * size_t(topk));
+  out->scale = reinterpret_cast<const float*>(r + kh + ks + 8 * size_t(topk));
+  out->codes_stride = out->sf_stride = out->ids_stride = out->weights_stride =
+      out->scale_stride = int64_t(rb);
+  return FGG_OK;
+}
+
+int fgg_moe_expand_plan(const FggMoeTokens* tokens, const int32_t* owner, const int32_t* slot,
+                        int32_t num_experts, int32_t rank, int32_t local, int32_t max_rows,
+                        int32_t* offsets, int32_t* route_row, int32_t* src_token,
+                        float* row_scale, int* bad, void* stream) {
+  MoeTok t;
+  if (int rc = to_dev(tokens, &t)) return rc;
+  if (num_experts < 1 || local < 1 || local > kExpandMaxLocal || rank < 0 || max_rows < 0)
+    return set_error(FGG_EBADSHAPE, "need num_experts >= 1, 1 <= local <= %d, rank >= 0",
+                     kExpandMaxLocal);
+  if (int64_t(t.num_tokens) * t.topk > INT32_MAX) return set_error(FGG_EBADSHAPE, "too many routes");
+  if (owner == nullptr || slot == nullptr || offsets == nullptr || bad == nullptr ||
+      (t.num_tokens > 0 && route_row == nullptr) ||
+      (max_rows > 0 && (src_token == nullptr || row_scale == nullptr)))
+    return set_error(FGG_EINVAL, "null pointer");
+  FGG_CUDA_CHECK(launch_pdl(moe_expand_plan_kernel, dim3(1), dim3(kExpandThreads), 0,
+                            reinterpret_cast<cudaStream_t>(stream), t, owner, slot, num_experts,
+                            rank, local, max_rows, offsets, route_row, src_token, row_scale, bad));
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+int fgg_moe_expand_rows(const FggMoeTokens* tokens, const int32_t* src_token, const int32_t* count,
+                        int32_t max_rows, void* out_codes, void* out_sf, int* bad, void* stream) {
+  MoeTok t;
+  if (int rc = to_dev(tokens, &t)) return rc;
+  if (max_rows < 0) return set_error(FGG_EINVAL, "max_rows is negative");
+  if (max_rows == 0) return FGG_OK;
+  if (src_token == nullptr || count == nullptr || out_codes == nullptr || out_sf == nullptr ||
+      bad == nullptr || t.codes == nullptr || t.sf == nullptr)
+    return set_error(FGG_EINVAL, "null pointer");
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  const int grid = std::min((max_rows + 7) / 8, dev.sm_count * 8);  // 8 rows in flight a block
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto* oc = static_cast<uint8_t*>(out_codes);
+  auto* of = static_cast<uint8_t*>(out_sf);
+  if (rows_vec16(t) && aligned16(out_codes) && aligned16(out_sf))
+    FGG_CUDA_CHECK(launch_pdl(moe_expand_rows_kernel<true>, dim3(grid), dim3(256), 0, s, t,
+                              src_token, count, max_rows, oc, of, bad));
+  else if (rows_vec4(t) && aligned4(out_codes) && aligned4(out_sf))
+    FGG_CUDA_CHECK(launch_pdl(moe_expand_rows_kernel<false>, dim3(grid), dim3(256), 0, s, t,
+                              src_token, count, max_rows, oc, of, bad));
+  else
+    return set_error(FGG_EALIGN, "token rows must start on 4-byte boundaries");
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+int fgg_moe_reduce(const void* rows, int32_t num_rows, const int32_t* route_row,
+                   const FggMoeTokens* tokens, int32_t n, void* out, int* bad, void* stream) {
+  MoeTok t;
+  if (int rc = to_dev(tokens, &t)) return rc;
+  if (n <= 0 || n % 8 != 0 || num_rows < 0)
+    return set_error(FGG_EBADSHAPE, "n must be a positive multiple of 8");
+  if (t.num_tokens == 0) return FGG_OK;
+  if (route_row == nullptr || out == nullptr || bad == nullptr || (num_rows > 0 && rows == nullptr))
+    return set_error(FGG_EINVAL, "null pointer");
+  if (!aligned16(rows) || !aligned16(out))
+    return set_error(FGG_EALIGN, "rows and out must be 16-byte aligned");
+  const dim3 grid(unsigned(t.num_tokens), unsigned((n / 8 + 255) / 256));
+  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel, grid, dim3(256), 0,
+                            reinterpret_cast<cudaStream_t>(stream), t,
+                            static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, n,
+                            static_cast<__nv_bfloat16*>(out), bad));
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+int fgg_moe_sum_partials(const void* parts, int32_t world, int32_t per_source, int32_t tokens,
+                         int32_t n, void* out, void* stream) {
+  if (world < 1 || tokens < 0 || per_source < tokens || n <= 0 || n % 8 != 0)
+    return set_error(FGG_EBADSHAPE, "need world >= 1, 0 <= tokens <= per_source, n a positive "
+                                    "multiple of 8");
+  if (tokens == 0) return FGG_OK;
+  if (parts == nullptr || out == nullptr) return set_error(FGG_EINVAL, "null pointer");
+  if (!aligned16(parts) || !aligned16(out))
+    return set_error(FGG_EALIGN, "parts and out must be 16-byte aligned");
+  const dim3 grid(unsigned(tokens), unsigned((n / 8 + 255) / 256));
+  FGG_CUDA_CHECK(launch_pdl(moe_sum_parts_kernel, grid, dim3(256), 0,
+                            reinterpret_cast<cudaStream_t>(stream),
+                            static_cast<const __nv_bfloat16*>(parts), world, per_source, tokens, n,
+                            static_cast<__nv_bfloat16*>(out)));
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
 
 int fgg_moe_gather_rows(const void* codes, const void* sf, int64_t rows_in, int32_t code_bytes,
                         int32_t sf_bytes, const int32_t* src_row, int64_t num_rows,

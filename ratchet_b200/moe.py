@@ -5,27 +5,37 @@ The single-GPU analogue in the reference is `_moe_forward`
 puts the routed token rows of each expert together, one grouped GEMM runs
 every expert, and a combine weights the rows and sums them back per token.
 Here the experts are sharded over the ranks of a process group (one process
-per GPU) and the rows travel between ranks:
+per GPU) and the tokens travel between ranks.
 
-  1. plan      every (token, k) route gets its owner rank and the expert's
-               slot on that rank; routes are ordered by (rank, slot) with one
-               stable sort, and counted per (rank, slot)
-  2. dispatch  all-to-all of the counts (with each rank's activation decode
-               scale), then of the NVFP4 rows (codes and E4M3 scales) in that
-               order
-  3. GEMM      the received rows are source-major: the rows of one local
-               expert arrive as one contiguous chunk per source rank.  Each
-               (source, expert) chunk is one problem group of the grouped
-               GEMM, pointing at the expert's packed weights through b_index,
-               so nothing is permuted on the receiving side
-  4. combine   all-to-all of the bf16 output rows back along the same splits,
-               an index_copy_ that undoes the plan's order, and (with router
-               weights) the weighted sum over each token's k routes
+No size ever reaches the host, so a forward never synchronises it (and can be
+captured in a CUDA graph).  That fixes the exchange buffers' shapes: a
+dispatch that can never overflow gives every (source, destination) pair room
+for all of the source's tokens (`max_tokens`, the per-rank capacity), and at
+that capacity the dispatch moves exactly the bytes of an all-gather of the
+tokens.  So a forward is:
+
+  1. pack       each token becomes one record (NVFP4 codes and scales, its
+                top-k expert ids and router weights, its rank's decode
+                scale); slots past the rank's tokens carry no route
+  2. dispatch   NCCL all-gather of the records (one NVLink crossing per token
+                and rank)
+  3. expand     every rank plans the routes of its own experts (expert by
+                expert) and gathers their token rows into one buffer
+  4. GEMM       one grouped GEMM over the expanded rows with the plan's device
+                offsets (fgg_nvfp4_grouped_gemm_rows); each row carries its
+                source's decode scale as a row factor
+  5. combine    each rank sums every token's local routes with their router
+                weights into one partial row per token, an equal-split NCCL
+                all-to-all returns each source its tokens' partial rows, and
+                the source sums them in fp32
+
+At world size 1 steps 1, 2 and the exchange of step 5 drop out: the expand
+reads the caller's tensors and the weighted sum is the output.
 
 Collectives go through torch.distributed (NCCL on GPUs, gloo for the CPU
-tests of this host logic).  The expert compute is the library's tcgen05
-grouped GEMM; `gemm_fn` may replace it only to test the host logic without
-a GPU.
+tests of the host logic).  `gemm_fn` replaces the device path with a host
+emulation of the same steps (torch CPU ops around a stand-in GEMM), only to
+test the host logic without a GPU.
 """
 from __future__ import annotations
 
@@ -105,6 +115,8 @@ def place_experts(load: Sequence[float], world: int):
 # ------------------------------------------------------------------ layer
 GemmFn = Callable[[list, list, list, torch.Tensor, torch.Tensor], None]
 
+PHASES = ("pack", "dispatch", "expand", "gemm", "reduce", "combine", "sum")
+
 
 class ExpertParallelMoE:
     """One expert-parallel MoE projection (e.g. the fused gate+up of every
@@ -113,11 +125,15 @@ class ExpertParallelMoE:
     w_codes / w_sf / w_scale: this rank's experts, in slot order: codes
     [N, K/2] uint8, E4M3 scales [N, K/16], fp32 decode scale (0-dim tensor
     or float).  owner / slot: the placement of every expert (place_experts).
+    max_tokens: the dispatch capacity, the most tokens any rank passes to one
+    forward (every rank must use the same value); default: the first
+    forward's token count.  topk: routes per token (default: the first
+    forward's).
     """
 
     def __init__(self, w_codes: Sequence[torch.Tensor], w_sf: Sequence[torch.Tensor],
                  w_scale: Sequence, owner: np.ndarray, slot: np.ndarray, group=None,
-                 gemm_fn: GemmFn | None = None):
+                 gemm_fn: GemmFn | None = None, max_tokens: int | None = None):
         import torch.distributed as dist
 
         self.group = group
@@ -141,51 +157,97 @@ class ExpertParallelMoE:
         dev = self.w_codes[0].device
         self.device = dev
         self.w_scale = torch.stack([torch.as_tensor(s, dtype=torch.float32, device=dev).reshape(())
-                                    for s in w_scale])
-        self.owner_t = torch.from_numpy(owner).to(dev, torch.int64)
-        self.slot_t = torch.from_numpy(slot).to(dev, torch.int64)
+                                    for s in w_scale]).contiguous()
+        self.owner_np, self.slot_np = owner, slot
         self.gemm_fn = gemm_fn
+        self.max_tokens = max_tokens
+        self.topk = None
+        self.bufs = None
         self.pack = None
         self.bad = None
-        self.ws = None
-        self._host_counts = None  # pinned landing buffer of the per-forward count exchange
         if gemm_fn is None:
             # the product path: weights packed once and reused by every
-            # forward; the gather / combine kernels raise this flag on an
-            # out-of-range row index (see check())
+            # forward; the kernels raise this flag on a bad id or index
             self.pack = ops.pack_weights(self.w_codes, self.w_sf)
             self.bad = torch.zeros(1, dtype=torch.int32, device=dev)
-            self.owner_i32 = torch.from_numpy(owner).to(dev)
-            self.slot_i32 = torch.from_numpy(slot).to(dev)
-            self.ws = torch.empty(0, dtype=torch.uint8, device=dev)  # GEMM workspace, grown on demand
-        # problem group g = (source rank, local slot), source-major
-        self.b_index = [e for _ in range(self.world) for e in range(self.local)]
-        self.b_index_np = np.asarray(self.b_index, dtype=np.int32)
+            self.owner_d = torch.from_numpy(owner).to(dev)
+            self.slot_d = torch.from_numpy(slot).to(dev)
 
-    # -------------------------------------------------------------- pieces
-    def plan(self, topk_ids: torch.Tensor):
-        """Order of the routes by (owner rank, slot) and their counts."""
-        flat = topk_ids.reshape(-1).to(self.owner_t.device, torch.int64)
-        key = self.owner_t[flat] * self.local + self.slot_t[flat]
-        order = torch.argsort(key, stable=True)
-        counts = torch.bincount(key, minlength=self.world * self.local).to(torch.int32)
-        return order, counts
+    # ---------------------------------------------------------- buffers
+    def _buffers(self, T: int, topk: int):
+        """Device buffers of one forward geometry, made on first use."""
+        if self.max_tokens is None:
+            self.max_tokens = T
+        if self.topk is None:
+            self.topk = topk
+        C, W, E = self.max_tokens, self.world, self.local
+        if T > C:
+            raise ValueError(f"{T} tokens exceed the layer's dispatch capacity max_tokens={C}")
+        if topk != self.topk:
+            raise ValueError(f"topk={topk}, the layer was set up for {self.topk}")
+        if self.bufs is not None:
+            return self.bufs
+        L = _lib.lib()
+        dev, kh, ks, n = self.device, self.k // 2, self.k // 16, self.n
+        NT = W * C if W > 1 else C           # tokens the expand plan walks
+        R = NT * min(topk, E)                # local routes at most
+        b = {"NT": NT, "R": R}
+        if W > 1:
+            rb = int(L.fgg_moe_record_bytes(self.k, topk))
+            b["rb"] = rb
+            b["records"] = torch.empty((C, rb), dtype=torch.uint8, device=dev)
+            b["gathered"] = torch.empty((W * C, rb), dtype=torch.uint8, device=dev)
+            b["partial"] = torch.empty((W * C, n), dtype=torch.bfloat16, device=dev)
+            b["recv"] = torch.empty((W * C, n), dtype=torch.bfloat16, device=dev)
+            toks = _lib.FggMoeTokens()
+            _lib.check(L.fgg_moe_records_view(b["gathered"].data_ptr(), W * C, self.k, topk, toks),
+                       "fgg_moe_records_view")
+            b["gathered_view"] = toks
+        b["offsets"] = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        b["route_row"] = torch.empty(NT * topk, dtype=torch.int32, device=dev)
+        b["src_token"] = torch.empty(R, dtype=torch.int32, device=dev)
+        b["row_scale"] = torch.empty(R, dtype=torch.float32, device=dev)
+        b["a"] = torch.empty((R, kh), dtype=torch.uint8, device=dev)
+        b["a_sf"] = torch.empty((R, ks), dtype=torch.uint8, device=dev)
+        b["y"] = torch.empty((R, n), dtype=torch.bfloat16, device=dev)
+        prob = _lib.FggNvfp4RowsProblem(E, n, self.k, R, b["offsets"].data_ptr(), b["a"].data_ptr(),
+                                        b["a_sf"].data_ptr(), self.w_scale.data_ptr(),
+                                        b["y"].data_ptr(), b["row_scale"].data_ptr(), None, E, 0)
+        nbytes = int(L.fgg_nvfp4_rows_workspace_bytes(prob))
+        if nbytes == 0:
+            _lib.check(L.fgg_nvfp4_grouped_gemm_rows(prob, None, None, 0, None), "grouped GEMM")
+        b["prob"] = prob
+        b["ws"] = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.bufs = b
+        return b
 
-    def _a2a(self, out, inp, out_splits=None, in_splits=None):
+    def _tokens_view(self, x_u8, s_u8, ids32, w32, xs):
+        T, topk = int(ids32.shape[0]), int(ids32.shape[1])
+        t = _lib.FggMoeTokens()
+        t.num_tokens, t.topk, t.k = T, topk, self.k
+        t.codes, t.codes_stride = x_u8.data_ptr(), x_u8.stride(0)
+        t.sf, t.sf_stride = s_u8.data_ptr(), s_u8.stride(0)
+        t.ids, t.ids_stride = ids32.data_ptr(), 4 * ids32.stride(0)
+        t.weights, t.weights_stride = (w32.data_ptr(), 4 * w32.stride(0)) if w32 is not None else (None, 0)
+        t.scale, t.scale_stride = xs.data_ptr(), 0
+        return t
+
+    def _a2a(self, out, inp):
         import torch.distributed as dist
 
         if inp.dtype == torch.bfloat16:  # rows as bytes: bit-exact on every backend
             out, inp = out.view(torch.uint8), inp.view(torch.uint8)
-        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+        dist.all_to_all_single(out, inp, group=self.group)
 
+    # ---------------------------------------------------------- forward
     def forward(self, x_codes: torch.Tensor, x_sf: torch.Tensor, x_scale, topk_ids: torch.Tensor,
-                topk_weights: torch.Tensor | None = None, gemm_events=None) -> torch.Tensor:
+                topk_weights: torch.Tensor | None = None, events: dict | None = None) -> torch.Tensor:
         """x_codes [T, K/2] uint8 and x_sf [T, K/16] E4M3: this rank's tokens,
-        quantised with decode scale x_scale.  topk_ids [T, k] expert ids.
-        Returns [T, k, N] bf16 per-route outputs, or [T, N] bf16 (the
-        weighted sum over k) when topk_weights [T, k] is given.
-        gemm_events: optional (start, end) CUDA events recorded around the
-        grouped GEMM on the current stream (for timing the kernel alone)."""
+        quantised with decode scale x_scale.  topk_ids [T, k] expert ids (an
+        id < 0 is an absent route).  Returns [T, N] bf16, the router-weighted
+        sum over each token's routes (topk_weights [T, k]; None = weights of 1).
+        events: optional dict; CUDA events (start of each of PHASES, and "end")
+        are recorded into it on the current stream, for a per-phase breakdown."""
         T, topk = int(topk_ids.shape[0]), int(topk_ids.shape[1])
         kh, ks = self.k // 2, self.k // 16
         x_u8 = x_codes.view(torch.uint8)
@@ -193,147 +255,144 @@ class ExpertParallelMoE:
         if x_u8.shape != (T, kh) or s_u8.shape != (T, ks):
             raise ValueError(f"x_codes {tuple(x_u8.shape)} / x_sf {tuple(s_u8.shape)} do not match "
                              f"T={T}, K={self.k}")
-        dev = x_u8.device
-        W, E = self.world, self.local
-        S = T * topk
-        L = _lib.lib() if self.gemm_fn is None else None
-        stream = ops._stream_ptr(dev) if L is not None else None
-        # 1. plan
-        if L is not None:
-            ids32 = topk_ids.to(dev, torch.int32).contiguous()
-            counts = torch.empty(W * E, dtype=torch.int32, device=dev)
-            src_row = torch.empty(S, dtype=torch.int32, device=dev)
-            route_pos = torch.empty(S, dtype=torch.int32, device=dev)
-            _lib.check(L.fgg_moe_plan(ids32.data_ptr(), T, topk, self.owner_i32.data_ptr(),
-                                      self.slot_i32.data_ptr(), self.num_experts, W, E,
-                                      counts.data_ptr(), src_row.data_ptr(), route_pos.data_ptr(),
-                                      self.bad.data_ptr(), stream), "fgg_moe_plan")
-        else:  # host-logic tests without a GPU
-            order, counts = self.plan(topk_ids)
-        # 2. to every rank: the counts of the routes it gets from here and
-        #    this rank's activation decode scale (its bits after the counts)
-        xs = torch.as_tensor(x_scale, dtype=torch.float32, device=dev).reshape(1)
-        info = torch.empty((W, E + 1), dtype=torch.int32, device=dev)
-        info[:, :E] = counts.view(W, E)
-        info[:, E] = xs.view(torch.int32)
-        if W == 1:
-            recv_info = info
-        else:
-            recv_info = torch.empty_like(info)
-            self._a2a(recv_info, info)
-        # the counts travel to the host ahead of the row gather: the host waits
-        # for this copy alone (one host sync per forward) and plans the GEMM
-        # while the device still gathers
-        both_d = torch.stack([info, recv_info])
-        counts_ready = None
-        if both_d.is_cuda:
-            if self._host_counts is None or self._host_counts.shape != both_d.shape:
-                self._host_counts = torch.empty(both_d.shape, dtype=torch.int32, pin_memory=True)
-            both = self._host_counts
-            both.copy_(both_d, non_blocking=True)
-            counts_ready = torch.cuda.Event()
-            counts_ready.record()
-        else:
-            both = both_d
-        # 3. the rows in (owner, slot) order
-        if L is not None:
-            send_codes = torch.empty((S, kh), dtype=torch.uint8, device=dev)
-            send_sf = torch.empty((S, ks), dtype=torch.uint8, device=dev)
-            _lib.check(L.fgg_moe_gather_rows(
-                x_u8.data_ptr(), s_u8.data_ptr(), T, kh, ks, src_row.data_ptr(), S,
-                send_codes.data_ptr(), send_sf.data_ptr(), self.bad.data_ptr(), stream),
-                "fgg_moe_gather_rows")
-        else:
-            rows = order // topk
-            send_codes = x_u8.index_select(0, rows)
-            send_sf = s_u8.index_select(0, rows)
-        # alpha of problem group (source, slot) = source's activation scale x
-        # the slot's weight scale: device work, queued before the host waits
-        src_scale = recv_info[:, E].contiguous().view(torch.float32)
-        alpha = (src_scale[:, None] * self.w_scale[None, :]).reshape(-1).contiguous()
-        # on one rank every route stays: the GEMM output size is known up front
-        out = torch.empty((S, self.n), dtype=torch.bfloat16, device=dev) if W == 1 else None
-        if counts_ready is not None:
-            counts_ready.synchronize()
-        send_ce, recv_ce = both[0, :, :E], both[1, :, :E]
-        send_splits = send_ce.sum(1).tolist()
-        recv_splits = recv_ce.sum(1).tolist()
-        R = int(sum(recv_splits))
-        if W == 1:  # nothing leaves the rank
-            recv_codes, recv_sf = send_codes, send_sf
-        else:
-            recv_codes = torch.empty((R, kh), dtype=torch.uint8, device=dev)
-            recv_sf = torch.empty((R, ks), dtype=torch.uint8, device=dev)
-            self._a2a(recv_codes, send_codes, recv_splits, send_splits)
-            self._a2a(recv_sf, send_sf, recv_splits, send_splits)
-        # 4. grouped GEMM over the (source, slot) chunks
-        if out is None:
-            out = torch.empty((R, self.n), dtype=torch.bfloat16, device=dev)
-        if gemm_events is not None:
-            gemm_events[0].record()
-        if L is not None:
-            if R > 0:
-                self._gemm(L, recv_ce, recv_codes, recv_sf, alpha, out, stream)
-        else:
-            ms = recv_ce.reshape(-1).tolist()
-            a_list = list(recv_codes.split(ms))
-            sf_list = [t.view(torch.float8_e4m3fn) for t in recv_sf.split(ms)]
-            self.gemm_fn(a_list, sf_list, self.b_index, alpha, out)
-        if gemm_events is not None:
-            gemm_events[1].record()
-        # 5. combine: rows go back along the dispatch splits, then to route order
-        if W == 1:
-            back = out
-        else:
-            back = torch.empty((T * topk, self.n), dtype=torch.bfloat16, device=dev)
-            self._a2a(back, out, send_splits, recv_splits)
-        if L is not None:
-            if topk_weights is None:
-                return back.index_select(0, route_pos.long()).view(T, topk, self.n)
-            # one pass: each token reads its k rows where the dispatch order
-            # left them and writes the weighted sum
-            w = topk_weights.to(dev, torch.float32).contiguous()
-            res = torch.empty((T, self.n), dtype=torch.bfloat16, device=dev)
-            _lib.check(L.fgg_moe_combine(back.data_ptr(), S, route_pos.data_ptr(), w.data_ptr(), T,
-                                         topk, self.n, res.data_ptr(), self.bad.data_ptr(),
-                                         stream), "fgg_moe_combine")
-            return res
-        res = torch.empty_like(back)
-        res.index_copy_(0, order, back)
-        res = res.view(T, topk, self.n)
-        if topk_weights is None:
-            return res
-        w = topk_weights.to(dev, torch.float32).view(T, topk, 1)
-        return (res.float() * w).sum(1).to(torch.bfloat16)
+        if self.gemm_fn is not None:
+            return self._forward_host(x_u8, s_u8, x_scale, topk_ids, topk_weights)
+        b = self._buffers(T, topk)
+        dev = self.device
+        L = _lib.lib()
+        stream = ops._stream_ptr(dev)
+        W, E, n, C = self.world, self.local, self.n, self.max_tokens
 
-    def _gemm(self, L, recv_ce, recv_codes, recv_sf, alpha, out, stream):
-        """The grouped GEMM through the C ABI directly: the group pointers are
-        offsets into the two receive buffers, so no per-group tensor views."""
-        kh, ks = self.k // 2, self.k // 16
-        ms = recv_ce.reshape(-1).numpy().astype(np.int32)
-        offs = np.zeros_like(ms, dtype=np.uint64)
-        offs[1:] = np.cumsum(ms[:-1], dtype=np.uint64)
-        a_ptrs = np.uint64(recv_codes.data_ptr()) + offs * np.uint64(kh)
-        sf_ptrs = np.uint64(recv_sf.data_ptr()) + offs * np.uint64(ks)
-        prob = _lib.FggNvfp4Problem(len(ms), self.n, self.k, ms.ctypes.data, a_ptrs.ctypes.data,
-                                    sf_ptrs.ctypes.data, alpha.data_ptr(), out.data_ptr(),
-                                    self.b_index_np.ctypes.data, self.local)
-        nbytes = int(L.fgg_nvfp4_workspace_bytes(prob))
-        if nbytes == 0:
-            _lib.check(L.fgg_nvfp4_grouped_gemm(prob, None, None, 0, None), "grouped GEMM")
-        if self.ws.numel() < nbytes:
-            self.ws = torch.empty(nbytes, dtype=torch.uint8, device=out.device)
-        _lib.check(L.fgg_nvfp4_grouped_gemm(prob, self.pack.buf.data_ptr(), self.ws.data_ptr(),
-                                            self.ws.numel(), stream), "grouped GEMM")
+        def mark(name):
+            if events is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                events[name] = ev
+
+        ids32 = topk_ids.to(device=dev, dtype=torch.int32).contiguous()
+        w32 = None if topk_weights is None else topk_weights.to(device=dev, dtype=torch.float32).contiguous()
+        xs = torch.as_tensor(x_scale, dtype=torch.float32, device=dev).reshape(1)
+        mine = self._tokens_view(x_u8, s_u8, ids32, w32, xs)
+        mark("pack")
+        if W > 1:
+            if T < C:  # slots past this rank's tokens carry no route (expert id -1)
+                b["records"][T:, kh + ks:kh + ks + 4 * topk].view(torch.int32).fill_(-1)
+            _lib.check(L.fgg_moe_pack_tokens(mine, b["records"].data_ptr(), stream), "fgg_moe_pack_tokens")
+            mark("dispatch")
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(b["gathered"], b["records"], group=self.group)
+            toks = b["gathered_view"]
+        else:
+            mark("dispatch")
+            toks = mine
+        mark("expand")
+        _lib.check(L.fgg_moe_expand_plan(toks, self.owner_d.data_ptr(), self.slot_d.data_ptr(),
+                                         self.num_experts, self.rank, E, b["R"],
+                                         b["offsets"].data_ptr(), b["route_row"].data_ptr(),
+                                         b["src_token"].data_ptr(), b["row_scale"].data_ptr(),
+                                         self.bad.data_ptr(), stream), "fgg_moe_expand_plan")
+        _lib.check(L.fgg_moe_expand_rows(toks, b["src_token"].data_ptr(), b["offsets"][E:].data_ptr(),
+                                         b["R"], b["a"].data_ptr(), b["a_sf"].data_ptr(),
+                                         self.bad.data_ptr(), stream), "fgg_moe_expand_rows")
+        mark("gemm")
+        _lib.check(L.fgg_nvfp4_grouped_gemm_rows(b["prob"], self.pack.buf.data_ptr(),
+                                                 b["ws"].data_ptr(), b["ws"].numel(), stream),
+                   "fgg_nvfp4_grouped_gemm_rows")
+        ops._set_last_ws(b["ws"])
+        mark("reduce")
+        out = torch.empty((T, n), dtype=torch.bfloat16, device=dev)
+        target = b["partial"] if W > 1 else out
+        _lib.check(L.fgg_moe_reduce(b["y"].data_ptr(), b["R"], b["route_row"].data_ptr(), toks, n,
+                                    target.data_ptr(), self.bad.data_ptr(), stream), "fgg_moe_reduce")
+        mark("combine")
+        if W > 1:
+            self._a2a(b["recv"], b["partial"])
+        mark("sum")
+        if W > 1:
+            _lib.check(L.fgg_moe_sum_partials(b["recv"].data_ptr(), W, C, T, n, out.data_ptr(), stream),
+                       "fgg_moe_sum_partials")
+        mark("end")
+        return out
+
+    # ------------------------------------------------ host emulation (tests)
+    def _forward_host(self, x_u8, s_u8, x_scale, topk_ids, topk_weights):
+        """The same steps with torch CPU ops and the stand-in GEMM: records
+        padded to the capacity, all-gathered, expanded per local expert (and
+        per source, whose decode scale goes into that chunk's alpha), the
+        router-weighted partial rows, the equal-split all-to-all, the fp32 sum."""
+        import torch.distributed as dist
+
+        T, topk = int(topk_ids.shape[0]), int(topk_ids.shape[1])
+        if self.max_tokens is None:
+            self.max_tokens = T
+        C, W, E, n = self.max_tokens, self.world, self.local, self.n
+        if T > C:
+            raise ValueError(f"{T} tokens exceed the layer's dispatch capacity max_tokens={C}")
+        ids = torch.full((C, topk), -1, dtype=torch.int32)
+        ids[:T] = topk_ids.to(torch.int32)
+        w = torch.zeros((C, topk), dtype=torch.float32)
+        w[:T] = 1.0 if topk_weights is None else topk_weights.to(torch.float32)
+        codes = torch.zeros((C, x_u8.shape[1]), dtype=torch.uint8)
+        codes[:T] = x_u8
+        sf = torch.zeros((C, s_u8.shape[1]), dtype=torch.uint8)
+        sf[:T] = s_u8
+        xs = torch.as_tensor(x_scale, dtype=torch.float32).reshape(1)
+        if W > 1:
+            def gather(t):
+                out = torch.empty((W * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype)
+                dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+                return out
+            ids, w, codes, sf, scales = gather(ids), gather(w), gather(codes), gather(sf), gather(xs)
+        else:
+            scales = xs
+        NT = ids.shape[0]
+        owner = torch.from_numpy(self.owner_np.astype(np.int64))
+        slot = torch.from_numpy(self.slot_np.astype(np.int64))
+        flat = ids.reshape(-1).long()
+        present = flat >= 0
+        if bool((flat >= self.num_experts).any()):
+            raise ValueError("an expert id is out of range")
+        safe = flat.clamp_min(0)
+        local = present & (owner[safe] == self.rank)
+        route_idx = torch.nonzero(local).flatten()               # routes of local experts
+        tok = route_idx // topk
+        src = tok // C
+        key = slot[safe[route_idx]] * W + src                    # chunk (expert, source)
+        order = torch.argsort(key, stable=True)
+        route_idx, tok, src, key = route_idx[order], tok[order], src[order], key[order]
+        ms = torch.bincount(key, minlength=E * W).tolist()
+        a_list = list(codes[tok].split(ms))
+        sf_list = [s.view(torch.float8_e4m3fn) for s in sf[tok].split(ms)]
+        b_index = [g // W for g in range(E * W)]
+        alpha = (self.w_scale.cpu()[:, None] * scales[None, :]).reshape(-1)
+        y = torch.empty((route_idx.numel(), n), dtype=torch.bfloat16)
+        self.gemm_fn(a_list, sf_list, b_index, alpha, y)
+        route_row = torch.full((NT * topk,), -1, dtype=torch.long)
+        route_row[route_idx] = torch.arange(route_idx.numel())
+        partial = torch.zeros((NT, n), dtype=torch.float32)
+        rr = route_row.view(NT, topk)
+        for k in range(topk):
+            sel = torch.nonzero(rr[:, k] >= 0).flatten()
+            partial[sel] += w[sel, k][:, None] * y[rr[sel, k]].float()
+        partial = partial.to(torch.bfloat16)
+        if W == 1:
+            return partial[:T]
+        recv = torch.empty_like(partial)
+        self._a2a(recv, partial)
+        return recv.view(W, C, n).float().sum(0)[:T].to(torch.bfloat16)
 
     def check(self) -> None:
-        """Raise if a plan, gather or combine kernel met an out-of-range index,
-        or a bounded wait in the GEMM gave up (synchronises the device)."""
-        if self.bad is not None and int(self.bad.item()) != 0:
-            raise _lib.FggError(_lib.FGG_EINVAL, "ExpertParallelMoE",
-                                "an expert id or a dispatch / combine row index was out of range")
-        if self.ws is not None and self.ws.numel():
+        """Raise if a plan, expand or combine kernel met a bad expert id or
+        index, or a bounded wait in the GEMM gave up (synchronises the device)."""
+        if self.bad is not None:
+            v = int(self.bad.item())
+            if v != 0:
+                raise _lib.FggError(_lib.FGG_EINVAL, "ExpertParallelMoE",
+                                    "an expert id was out of range" if v == 1 else
+                                    "more local routes than the expanded buffer holds")
+        if self.bufs is not None:
             L = _lib.lib()
-            _lib.check(L.fgg_read_device_status(self.ws.data_ptr(),
+            _lib.check(L.fgg_read_device_status(self.bufs["ws"].data_ptr(),
                                                 torch.cuda.current_stream(self.device).cuda_stream),
                        "grouped GEMM status")

@@ -452,6 +452,12 @@ def _quantize_on(x, amax, dev, rows, k):
     return codes, sf.view(torch.float8_e4m3fn), g
 
 
+def _set_last_ws(ws: torch.Tensor) -> None:
+    """Record the workspace of a GEMM launched outside this module (last_status reads it)."""
+    global _last_ws
+    _last_ws = ws
+
+
 def last_status() -> int:
     """Synchronise the current stream and return the device status word of the
     most recent GEMM call (0 = ok); raises FggError on a device timeout."""

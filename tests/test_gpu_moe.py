@@ -1,7 +1,9 @@
 """Expert-parallel MoE layer on B200 with the tcgen05 grouped GEMM, against
 the CPU oracle: world size 1 on one GPU, and two NCCL ranks when two GPUs are
-visible.  Tolerance: the operator's (max|err|/max|ref| <= 1e-2; per element
-|err| <= 2e-2 |ref| + 1e-2 max|ref|)."""
+visible; and the layer's byte-moving kernels (pack, expand plan, expand rows,
+router-weighted reduce, partial-row sum) against plain PyTorch, bit-exact for
+the integer and byte work.  GEMM tolerance: the operator's (max|err|/max|ref|
+<= 1e-2; per element |err| <= 2e-2 |ref| + 1e-2 max|ref|)."""
 import os
 import socket
 
@@ -22,41 +24,43 @@ def _weights(seed=1):
     return [ref.nvfp4_quantize(rng.standard_normal((N, K), dtype=np.float32)) for _ in range(E)]
 
 
-def _expected(xc, xs, xg, ids, w_all):
+def _expected(xc, xs, xg, ids, w_all, w=None):
+    """bf16(sum_k w[t,k] * bf16(xg * g_e * deq(x_t) . deq(W_e))) per token."""
     X = torch.from_numpy(ref.nvfp4_dequantize(xc, xs))
     Wd = [torch.from_numpy(ref.nvfp4_dequantize(c, s)) for c, s, _ in w_all]
     T = ids.shape[0]
-    out = torch.empty((T, TOPK, N))
+    acc = torch.zeros((T, N))
     for e in range(E):
         sel = np.argwhere(ids == e)
         if len(sel):
             t = torch.from_numpy(sel[:, 0])
-            out[t, torch.from_numpy(sel[:, 1])] = (X[t] @ Wd[e].T) * float(np.float32(xg * w_all[e][2]))
-    return out.to(torch.bfloat16)
+            y = ((X[t] @ Wd[e].T) * float(np.float32(xg * w_all[e][2]))).to(torch.bfloat16).float()
+            wk = 1.0 if w is None else torch.from_numpy(w[sel[:, 0], sel[:, 1]])[:, None]
+            acc.index_add_(0, t, y * wk)
+    return acc.to(torch.bfloat16)
 
 
-def _layer(w_all, owner, slot, rank, dev):
+def _layer(w_all, owner, slot, rank, dev, max_tokens=None):
     mine = sorted(np.flatnonzero(owner == rank).tolist(), key=lambda e: slot[e])
     return moe.ExpertParallelMoE([torch.from_numpy(w_all[e][0]).to(dev) for e in mine],
                                  [torch.from_numpy(w_all[e][1]).to(dev).view(torch.float8_e4m3fn)
                                   for e in mine],
-                                 [float(w_all[e][2]) for e in mine], owner, slot)
+                                 [float(w_all[e][2]) for e in mine], owner, slot,
+                                 max_tokens=max_tokens)
 
 
 def _check(layer, rank, T, dev, w_all):
     rng = np.random.default_rng(100 + rank)
     xc, xs, xg = ref.nvfp4_quantize(rng.standard_normal((T, K), dtype=np.float32))
     ids, w = moe.zipf_routing(T, E, TOPK, seed=30 + rank)
-    got = layer.forward(torch.from_numpy(xc).to(dev),
-                        torch.from_numpy(xs).to(dev).view(torch.float8_e4m3fn), float(xg),
-                        torch.from_numpy(ids).to(dev))
-    want = _expected(xc, xs, xg, ids, w_all)
-    ok, st = ref.check_close(got.cpu().float(), want.float())
-    summed = layer.forward(torch.from_numpy(xc).to(dev),
-                           torch.from_numpy(xs).to(dev).view(torch.float8_e4m3fn), float(xg),
-                           torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev))
-    ok2, st2 = ref.check_close(summed.cpu().float(),
-                               (want.float() * torch.from_numpy(w)[..., None]).sum(1))
+    ids[3, 2] = -1  # an absent route
+    args = (torch.from_numpy(xc).to(dev), torch.from_numpy(xs).to(dev).view(torch.float8_e4m3fn),
+            float(xg), torch.from_numpy(ids).to(dev))
+    got = layer.forward(*args)
+    ok, st = ref.check_close(got.cpu().float(), _expected(xc, xs, xg, ids, w_all).float())
+    summed = layer.forward(*args, torch.from_numpy(w).to(dev))
+    ok2, st2 = ref.check_close(summed.cpu().float(), _expected(xc, xs, xg, ids, w_all, w).float())
+    layer.check()
     return ok and ok2, (st, st2)
 
 
@@ -179,7 +183,7 @@ def _nccl_worker(rank, world, port, result_dir):
     try:
         w_all = _weights()
         owner, slot = moe.place_experts(moe.expert_popularity(E, seed=2), world)
-        layer = _layer(w_all, owner, slot, rank, dev)
+        layer = _layer(w_all, owner, slot, rank, dev, max_tokens=300)
         ok, st = _check(layer, rank, 200 + 57 * rank, dev, w_all)
         with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
             f.write(f"{int(ok)} {st}\n")
@@ -233,3 +237,123 @@ def test_moe_config3_world1_full_size(cuda_device):
     want = acc.to(torch.bfloat16)
     ok, st = ref.check_close(out.index_select(0, idx).cpu(), want)
     assert ok, st
+
+
+def _tok_view(codes, sf, ids, w, scale):
+    from ratchet_b200 import _lib
+
+    t = _lib.FggMoeTokens()
+    t.num_tokens, t.topk, t.k = int(ids.shape[0]), int(ids.shape[1]), int(codes.shape[1]) * 2
+    t.codes, t.codes_stride = codes.data_ptr(), codes.stride(0)
+    t.sf, t.sf_stride = sf.data_ptr(), sf.stride(0)
+    t.ids, t.ids_stride = ids.data_ptr(), 4 * ids.stride(0)
+    t.weights, t.weights_stride = w.data_ptr(), 4 * w.stride(0)
+    t.scale, t.scale_stride = scale.data_ptr(), 4 * scale.stride(0) if scale.numel() > 1 else 0
+    return t
+
+
+def test_expand_kernels_bitexact(cuda_device):
+    """pack -> records view -> expand plan -> expand rows, against the same
+    steps in PyTorch: every record byte, the per-expert counts, each route's
+    row holding exactly that token's bytes, and -1 for absent and remote routes."""
+    from ratchet_b200 import _lib
+
+    L = _lib.lib()
+    dev = cuda_device
+    st = torch.cuda.current_stream().cuda_stream
+    T, k, topk, Ex, world, rank = 300, 512, 8, 64, 4, 1
+    g = torch.Generator(device=dev).manual_seed(3)
+    codes = torch.randint(0, 256, (T, k // 2), dtype=torch.uint8, device=dev, generator=g)
+    sf = torch.randint(0, 256, (T, k // 16), dtype=torch.uint8, device=dev, generator=g)
+    ids_np, w_np = moe.zipf_routing(T, Ex, topk, seed=4)
+    ids_np[7, :] = -1
+    ids = torch.from_numpy(ids_np).to(dev)
+    w = torch.from_numpy(w_np).to(dev)
+    scale = torch.rand(T, device=dev, generator=g)
+    src = _tok_view(codes, sf, ids, w, scale)
+    rb = L.fgg_moe_record_bytes(k, topk)
+    rec = torch.empty((T, rb), dtype=torch.uint8, device=dev)
+    _lib.check(L.fgg_moe_pack_tokens(src, rec.data_ptr(), st), "pack")
+    kh, ks = k // 2, k // 16
+    assert torch.equal(rec[:, :kh], codes) and torch.equal(rec[:, kh:kh + ks], sf)
+    assert torch.equal(rec[:, kh + ks:kh + ks + 4 * topk].contiguous().view(torch.int32), ids)
+    assert torch.equal(rec[:, kh + ks + 4 * topk:kh + ks + 8 * topk].contiguous().view(torch.float32), w)
+    assert torch.equal(rec[:, kh + ks + 8 * topk:kh + ks + 8 * topk + 4].contiguous().view(torch.float32)[:, 0], scale)
+    view = _lib.FggMoeTokens()
+    _lib.check(L.fgg_moe_records_view(rec.data_ptr(), T, k, topk, view), "view")
+    owner, slot = moe.place_experts(moe.expert_popularity(Ex, seed=5), world)
+    loc = Ex // world
+    R = T * topk
+    offsets = torch.empty(loc + 1, dtype=torch.int32, device=dev)
+    route_row = torch.empty(T * topk, dtype=torch.int32, device=dev)
+    src_tok = torch.full((R,), -7, dtype=torch.int32, device=dev)
+    rscale = torch.empty(R, dtype=torch.float32, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    o_d, s_d = torch.from_numpy(owner).to(dev), torch.from_numpy(slot).to(dev)
+    _lib.check(L.fgg_moe_expand_plan(view, o_d.data_ptr(), s_d.data_ptr(), Ex, rank, loc, R,
+                                     offsets.data_ptr(), route_row.data_ptr(), src_tok.data_ptr(),
+                                     rscale.data_ptr(), bad.data_ptr(), st), "plan")
+    a = torch.empty((R, kh), dtype=torch.uint8, device=dev)
+    a_sf = torch.empty((R, ks), dtype=torch.uint8, device=dev)
+    _lib.check(L.fgg_moe_expand_rows(view, src_tok.data_ptr(), offsets[loc:].data_ptr(), R,
+                                     a.data_ptr(), a_sf.data_ptr(), bad.data_ptr(), st), "rows")
+    torch.cuda.synchronize()
+    assert int(bad.item()) == 0
+    flat = ids_np.reshape(-1)
+    is_local = (flat >= 0) & (owner[np.maximum(flat, 0)] == rank)
+    cnt = np.bincount(slot[flat[is_local]], minlength=loc)
+    off = offsets.cpu().numpy()
+    assert off[0] == 0 and np.array_equal(np.diff(off), cnt)
+    rr = route_row.cpu().numpy()
+    assert (rr[~is_local] == -1).all()
+    rows = rr[is_local]
+    assert np.array_equal(np.sort(rows), np.arange(cnt.sum()))        # a permutation
+    tok = np.flatnonzero(is_local) // topk
+    for e_slot in range(loc):                                          # each row in its expert's range
+        sel = slot[flat[is_local]] == e_slot
+        assert ((rows[sel] >= off[e_slot]) & (rows[sel] < off[e_slot + 1])).all()
+    assert np.array_equal(src_tok.cpu().numpy()[rows], tok)
+    rows_t = torch.from_numpy(rows).to(dev).long()
+    tok_t = torch.from_numpy(tok).to(dev).long()
+    assert torch.equal(a[rows_t], codes[tok_t]) and torch.equal(a_sf[rows_t], sf[tok_t])
+    assert torch.equal(rscale[rows_t], scale[tok_t])
+
+
+def test_reduce_and_sum_partials_match_fp32(cuda_device):
+    """fgg_moe_reduce: sum_k w[t,k] * rows[route_row[t,k]] over the routes with
+    a row (fp32, one bf16 rounding; zeros for a token without one);
+    fgg_moe_sum_partials: the fp32 sum of the partial rows of every source."""
+    from ratchet_b200 import _lib
+
+    L = _lib.lib()
+    dev = cuda_device
+    st = torch.cuda.current_stream().cuda_stream
+    T, topk, n, R = 129, 8, 512, 700
+    g = torch.Generator(device=dev).manual_seed(8)
+    rows = torch.randn((R, n), generator=g, device=dev).to(torch.bfloat16)
+    rr = torch.randint(0, R, (T, topk), generator=g, device=dev, dtype=torch.int32)
+    rr[torch.rand((T, topk), generator=g, device=dev) < 0.4] = -1
+    rr[5] = -1                                           # a token with no local route
+    w = torch.rand((T, topk), generator=g, device=dev)
+    ids = torch.zeros((T, topk), dtype=torch.int32, device=dev)
+    codes = torch.zeros((T, 32), dtype=torch.uint8, device=dev)
+    sf = torch.zeros((T, 4), dtype=torch.uint8, device=dev)
+    scale = torch.ones(1, device=dev)
+    view = _tok_view(codes, sf, ids, w, scale)
+    out = torch.full((T, n), float("nan"), dtype=torch.bfloat16, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.check(L.fgg_moe_reduce(rows.data_ptr(), R, rr.data_ptr(), view, n, out.data_ptr(),
+                                bad.data_ptr(), st), "reduce")
+    valid = (rr >= 0).float()[..., None]
+    want = (rows.float()[rr.clamp_min(0).long()] * w[..., None] * valid).sum(1)
+    err = (out.float() - want).abs()
+    assert (err <= want.abs() * 2.0 ** -7 + 1e-6).all()
+    assert (out[5].float() == 0).all() and int(bad.item()) == 0
+    world, per = 3, 150
+    parts = torch.randn((world * per, n), generator=g, device=dev).to(torch.bfloat16)
+    summed = torch.empty((T, n), dtype=torch.bfloat16, device=dev)
+    _lib.check(L.fgg_moe_sum_partials(parts.data_ptr(), world, per, T, n, summed.data_ptr(), st),
+               "sum")
+    p3 = parts.float().view(world, per, n)[:, :T]
+    want = (p3[0] + p3[1]) + p3[2]                       # the kernel's order, fp32
+    assert torch.equal(summed, want.to(torch.bfloat16))

@@ -4,10 +4,11 @@ and over two gloo ranks.  The expert GEMM is the CPU oracle here (the layer
 accepts a stand-in GEMM for exactly this purpose); the GPU tests run the
 same forward with the tcgen05 kernel.
 
-Expected output of route (t, k) to expert e:
-    bf16( x_scale * w_scale[e] * deq(x_t) . deq(W_e)^T )
-compared within the operator tolerance (the oracle GEMM sums a chunk of rows
-at once, the expected value one row at a time).
+Expected output of token t: the router-weighted sum of its routes,
+    bf16( sum_k w[t,k] * bf16( x_scale * w_scale[e] * deq(x_t) . deq(W_e)^T ) )
+(weights of 1 when none are given), compared within the operator tolerance
+(the oracle GEMM sums a chunk of rows at once, the expected value one row at
+a time).
 """
 import os
 import socket
@@ -75,25 +76,31 @@ def _oracle_gemm(local_w):
     return fn
 
 
-def _expected(xc, xs, xg, ids, weights_all):
+def _expected(xc, xs, xg, ids, weights_all, w=None):
+    """Router-weighted sum per token: bf16(sum_k w[t,k] * bf16(route output))
+    (weights of 1 when w is None); ids < 0 are absent routes."""
     X = ref.nvfp4_dequantize(xc, xs)
     T, K = ids.shape
     n = weights_all[0][0].shape[0]
-    out = np.zeros((T, K, n), dtype=np.float32)
+    out = np.zeros((T, n), dtype=np.float32)
     for t in range(T):
         for k in range(K):
+            if ids[t, k] < 0:
+                continue
             c, s, g = weights_all[ids[t, k]]
-            out[t, k] = (X[t:t + 1] @ ref.nvfp4_dequantize(c, s).T)[0] * np.float32(xg * g)
+            y = (X[t:t + 1] @ ref.nvfp4_dequantize(c, s).T)[0] * np.float32(xg * g)
+            y = torch.from_numpy(y).to(torch.bfloat16).float().numpy()
+            out[t] += (1.0 if w is None else w[t, k]) * y
     return torch.from_numpy(out).to(torch.bfloat16)
 
 
-def _build_layer(weights_all, owner, slot, rank, gemm=True):
+def _build_layer(weights_all, owner, slot, rank, max_tokens=None):
     mine = [weights_all[e] for e in np.flatnonzero(owner == rank)]
     mine = [mine[i] for i in np.argsort([slot[e] for e in np.flatnonzero(owner == rank)])]
     return moe.ExpertParallelMoE([torch.from_numpy(c) for c, _, _ in mine],
                                  [torch.from_numpy(s) for _, s, _ in mine],
                                  [float(g) for _, _, g in mine], owner, slot,
-                                 gemm_fn=_oracle_gemm(mine))
+                                 gemm_fn=_oracle_gemm(mine), max_tokens=max_tokens)
 
 
 def test_forward_world1_matches_oracle():
@@ -102,27 +109,26 @@ def test_forward_world1_matches_oracle():
     owner, slot = moe.place_experts(moe.expert_popularity(E, seed=2), 1)
     layer = _build_layer(weights_all, owner, slot, 0)
     ids, w = moe.zipf_routing(T, E, topk, seed=2)
+    ids[5, 1] = -1                        # an absent route
     xc, xs, xg = _tokens(T, k, seed=4)
     got = layer.forward(torch.from_numpy(xc), torch.from_numpy(xs), float(xg), torch.from_numpy(ids))
-    want = _expected(xc, xs, xg, ids, weights_all)
-    ok, st = ref.check_close(got.float(), want.float())
+    ok, st = ref.check_close(got.float(), _expected(xc, xs, xg, ids, weights_all).float())
     assert ok, st
     summed = layer.forward(torch.from_numpy(xc), torch.from_numpy(xs), float(xg),
                            torch.from_numpy(ids), torch.from_numpy(w))
-    want_sum = (want.float() * torch.from_numpy(w)[..., None]).sum(1)
-    ok, st = ref.check_close(summed.float(), want_sum)
+    ok, st = ref.check_close(summed.float(), _expected(xc, xs, xg, ids, weights_all, w).float())
     assert ok, st
 
 
-def test_plan_orders_routes_by_owner_then_slot():
-    E = 8
-    owner, slot = moe.place_experts(np.arange(E, 0, -1, dtype=np.float64), 1)
-    layer = _build_layer(_weights(E, 16, 32, seed=5), owner, slot, 0)
-    ids = torch.tensor([[3, 0], [7, 3], [0, 5]], dtype=torch.int32)
-    order, counts = layer.plan(ids)
-    keys = torch.from_numpy(slot.astype(np.int64))[ids.reshape(-1).long()]
-    assert torch.equal(keys[order], torch.sort(keys, stable=True).values)
-    assert counts.tolist() == np.bincount(keys.numpy(), minlength=E).tolist()
+def test_capacity_is_enforced():
+    E, n, k = 4, 16, 64
+    weights_all = _weights(E, n, k, seed=5)
+    owner, slot = moe.place_experts(np.ones(E), 1)
+    layer = _build_layer(weights_all, owner, slot, 0, max_tokens=8)
+    xc, xs, xg = _tokens(9, k, seed=6)
+    ids, _ = moe.zipf_routing(9, E, 2, seed=7)
+    with pytest.raises(ValueError):
+        layer.forward(torch.from_numpy(xc), torch.from_numpy(xs), float(xg), torch.from_numpy(ids))
 
 
 def _free_port():
@@ -141,17 +147,17 @@ def _worker(rank, world, port, result_dir):
         E, n, k, T, topk = 8, 32, 64, 37 + 11 * rank, 3
         weights_all = _weights(E, n, k, seed=1)           # the same experts on every rank
         owner, slot = moe.place_experts(moe.expert_popularity(E, seed=2), world)
-        layer = _build_layer(weights_all, owner, slot, rank)
+        # ranks pass different token counts under one dispatch capacity
+        layer = _build_layer(weights_all, owner, slot, rank, max_tokens=64)
         ids, w = moe.zipf_routing(T, E, topk, seed=10 + rank)
         xc, xs, xg = _tokens(T, k, seed=20 + rank)         # each rank its own tokens and scale
         got = layer.forward(torch.from_numpy(xc), torch.from_numpy(xs), float(xg),
                             torch.from_numpy(ids))
-        want = _expected(xc, xs, xg, ids, weights_all)
-        ok, st = ref.check_close(got.float(), want.float())
+        ok, st = ref.check_close(got.float(), _expected(xc, xs, xg, ids, weights_all).float())
         summed = layer.forward(torch.from_numpy(xc), torch.from_numpy(xs), float(xg),
                                torch.from_numpy(ids), torch.from_numpy(w))
-        want_sum = (want.float() * torch.from_numpy(w)[..., None]).sum(1)
-        ok2, st2 = ref.check_close(summed.float(), want_sum)
+        ok2, st2 = ref.check_close(summed.float(),
+                                   _expected(xc, xs, xg, ids, weights_all, w).float())
         with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
             f.write(f"{int(ok and ok2)} {st} {st2}\n")
     finally:
