@@ -294,8 +294,8 @@ FGG_API int fgg_moe_combine(const void* rows, int64_t num_rows, const int32_t* r
  * pair room for all of the source's tokens, which is the byte count of an
  * all-gather of the tokens: so each rank packs its tokens into records
  * (fgg_moe_pack_tokens), the ranks all-gather them, each rank expands the
- * routes of its own experts into expert-ordered rows (fgg_moe_expand_plan,
- * fgg_moe_expand_rows), runs fgg_nvfp4_grouped_gemm_rows on them with the
+ * routes of its own experts into expert-ordered rows (fgg_moe_expand), runs
+ * fgg_nvfp4_grouped_gemm_rows on them with the
  * plan's offsets, sums every token's local routes with its router weights
  * (fgg_moe_reduce) and the ranks exchange those partial rows with an
  * equal-split all-to-all that each rank sums (fgg_moe_sum_partials).  All
@@ -322,23 +322,23 @@ FGG_API int fgg_moe_pack_tokens(const FggMoeTokens* tokens, void* records, void*
 /* Host-only: a view of `num_tokens` consecutive records as FggMoeTokens. */
 FGG_API int fgg_moe_records_view(const void* records, int32_t num_tokens, int32_t k, int32_t topk,
                                  FggMoeTokens* out);
-/* Plan of this rank's routes: offsets[0..local] (device) place the routes of
- * local expert s (slot) at rows [offsets[s], offsets[s+1]); route_row[t*topk+k]
- * is route (t, k)'s row or -1 (another rank's expert, or an absent route:
- * expert id < 0, as on the padding tokens of a fixed-capacity dispatch);
- * src_token[row] and row_scale[row] (the token's decode scale) describe each
- * row.  An expert id >= num_experts sets *bad = 1; more routes than max_rows
- * sets *bad = 2 (the excess is dropped).  local <= 1024. */
-FGG_API int fgg_moe_expand_plan(const FggMoeTokens* tokens, const int32_t* owner,
-                                const int32_t* slot, int32_t num_experts, int32_t rank,
-                                int32_t local, int32_t max_rows, int32_t* offsets,
-                                int32_t* route_row, int32_t* src_token, float* row_scale, int* bad,
-                                void* stream);
-/* Expanded rows: row r = token src_token[r]'s codes and scales, for
- * r < *count (device, e.g. offsets + local), at most max_rows. */
-FGG_API int fgg_moe_expand_rows(const FggMoeTokens* tokens, const int32_t* src_token,
-                                const int32_t* count, int32_t max_rows, void* out_codes,
-                                void* out_sf, int* bad, void* stream);
+/* The routes of this rank's experts as expert-ordered token rows:
+ * offsets[0..local] (device) place the routes of local expert s (its slot) at
+ * rows [offsets[s], offsets[s+1]) of out_codes [max_rows, K/2] / out_sf
+ * [max_rows, K/16]; route_row[t*topk + k] is route (t, k)'s row or -1
+ * (another rank's expert, or an absent route: expert id < 0, as on the
+ * padding tokens of a fixed-capacity dispatch); src_token[row] and
+ * row_scale[row] (the token's decode scale) describe each row.  counts:
+ * device scratch of 2 * local int32.  An expert id >= num_experts sets
+ * *bad = 1; more routes than max_rows sets *bad = 2 (the excess is dropped).
+ * local <= 1024.  Rows are placed by atomics, so their order inside an
+ * expert may change from call to call; fgg_moe_reduce sums them back in
+ * route order, so its output does not. */
+FGG_API int fgg_moe_expand(const FggMoeTokens* tokens, const int32_t* owner, const int32_t* slot,
+                           int32_t num_experts, int32_t rank, int32_t local, int32_t max_rows,
+                           int32_t* counts, int32_t* offsets, int32_t* route_row,
+                           int32_t* src_token, float* row_scale, void* out_codes, void* out_sf,
+                           int* bad, void* stream);
 /* out[t, :] = bf16(sum_k weights[t, k] * rows[route_row[t*topk + k], :]) over
  * the routes with a row (>= 0), fp32 accumulation; zeros for a token with
  * none.  rows bf16 [num_rows, n]; n % 8 == 0. */

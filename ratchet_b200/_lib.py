@@ -91,11 +91,9 @@ _SIGS = {
     "fgg_moe_pack_tokens": (ctypes.c_int, [ctypes.POINTER(FggMoeTokens), _VOIDP, _VOIDP]),
     "fgg_moe_records_view": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                             ctypes.POINTER(FggMoeTokens)]),
-    "fgg_moe_expand_plan": (ctypes.c_int, [ctypes.POINTER(FggMoeTokens), _VOIDP, _VOIDP, ctypes.c_int32,
-                                           ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _VOIDP, _VOIDP,
-                                           _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
-    "fgg_moe_expand_rows": (ctypes.c_int, [ctypes.POINTER(FggMoeTokens), _VOIDP, _VOIDP, ctypes.c_int32,
-                                           _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
+    "fgg_moe_expand": (ctypes.c_int, [ctypes.POINTER(FggMoeTokens), _VOIDP, _VOIDP, ctypes.c_int32,
+                                      ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _VOIDP, _VOIDP,
+                                      _VOIDP, _VOIDP, _VOIDP, _VOIDP, _VOIDP, _VOIDP, _VOIDP]),
     "fgg_moe_reduce": (ctypes.c_int, [_VOIDP, ctypes.c_int32, _VOIDP, ctypes.POINTER(FggMoeTokens),
                                       ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP]),
     "fgg_moe_sum_partials": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,

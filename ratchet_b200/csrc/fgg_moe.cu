@@ -270,110 +270,112 @@ __global__ void __launch_bounds__(256) moe_pack_kernel(MoeTok t, uint8_t* __rest
   if (lane == 0) w[t.topk] = tok_scale(t, i);
 }
 
-// Expand plan, one block: the routes of this rank's experts, counted per
-// local expert (slot), their rows placed expert by expert.  Route (i, k) to a
-// local expert gets row route_row[i * topk + k] in the expanded buffer, which
-// holds token src_token[row] scaled by row_scale[row] (its source's decode
-// scale).  Routes to other ranks and absent routes (expert id < 0, e.g. the
-// padding tokens of a fixed-capacity dispatch) get -1; an expert id >= E or
-// a placement outside the local slots sets *bad and gets -1.  The order inside
-// an expert follows the atomics: every expanded row is computed on its own
-// and summed back in route order, so the results do not depend on it.
-constexpr int kExpandThreads = 1024;
+// Expand: the routes of this rank's experts, placed expert by expert into
+// one buffer of token rows.  Two kernels over the routes, many blocks each:
+//   count  per-block histograms of the local routes by slot, added into
+//          counts[slot] (zeroed before the launch)
+//   place  every block scans counts into offsets (block 0 publishes them for
+//          the GEMM); then one warp per route: a local route takes the next
+//          row of its expert (atomic cursor), records it in route_row, and the
+//          warp copies the token's codes and scales into that row.
+// Route (i, k) to another rank's expert, or absent (expert id < 0, e.g. a
+// padding token's), gets route_row -1; an expert id >= E or a placement
+// outside the local slots sets *bad = 1 and gets -1.  The row order inside an
+// expert follows the atomics: each expanded row is computed on its own and
+// summed back in route order, so the results do not depend on it.
 constexpr int kExpandMaxLocal = 1024;
 
-__global__ void __launch_bounds__(kExpandThreads)
-    moe_expand_plan_kernel(MoeTok t, const int32_t* __restrict__ owner,
-                           const int32_t* __restrict__ slot, int32_t num_experts, int32_t rank,
-                           int32_t local, int32_t max_rows, int32_t* __restrict__ offsets,
-                           int32_t* __restrict__ route_row, int32_t* __restrict__ src_token,
-                           float* __restrict__ row_scale, int* __restrict__ bad) {
+__device__ __forceinline__ int local_slot_of(const MoeTok& t, int64_t r,
+                                             const int32_t* __restrict__ owner,
+                                             const int32_t* __restrict__ slot, int num_experts,
+                                             int rank, int local, int* bad) {
+  const int e = tok_id(t, r / t.topk, int(r % t.topk));
+  if (e < 0) return -1;  // an absent route
+  if (e >= num_experts) {
+    atomicExch(bad, 1);
+    return -1;
+  }
+  if (__ldg(owner + e) != rank) return -1;
+  const int s = __ldg(slot + e);
+  if (s < 0 || s >= local) {
+    atomicExch(bad, 1);
+    return -1;
+  }
+  return s;
+}
+
+__global__ void __launch_bounds__(256)
+    moe_expand_count_kernel(MoeTok t, const int32_t* __restrict__ owner,
+                            const int32_t* __restrict__ slot, int32_t num_experts, int32_t rank,
+                            int32_t local, int32_t* __restrict__ counts, int* __restrict__ bad) {
   griddep_wait();
-  __shared__ int32_t cnt[kExpandMaxLocal];
-  __shared__ int32_t base[kExpandMaxLocal + 1];
-  for (int i = threadIdx.x; i < local; i += blockDim.x) cnt[i] = 0;
+  __shared__ int32_t hist[kExpandMaxLocal];
+  for (int i = threadIdx.x; i < local; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   const int64_t routes = int64_t(t.num_tokens) * t.topk;
-  auto local_slot = [&](int64_t r) -> int {
-    const int e = tok_id(t, r / t.topk, int(r % t.topk));
-    if (e < 0) return -1;  // an absent route (a padding token's)
-    if (e >= num_experts) {
-      atomicExch(bad, 1);
-      return -1;
-    }
-    if (__ldg(owner + e) != rank) return -1;
-    const int s = __ldg(slot + e);
-    if (s < 0 || s >= local) {
-      atomicExch(bad, 1);
-      return -1;
-    }
-    return s;
-  };
-  for (int64_t r = threadIdx.x; r < routes; r += blockDim.x) {
-    const int s = local_slot(r);
-    if (s >= 0) atomicAdd(&cnt[s], 1);
+  for (int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; r < routes;
+       r += int64_t(gridDim.x) * blockDim.x) {
+    const int s = local_slot_of(t, r, owner, slot, num_experts, rank, local, bad);
+    if (s >= 0) atomicAdd(&hist[s], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  for (int i = threadIdx.x; i < local; i += blockDim.x)
+    if (hist[i]) atomicAdd(counts + i, hist[i]);
+  griddep_launch_dependents();
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(256)
+    moe_expand_place_kernel(MoeTok t, const int32_t* __restrict__ owner,
+                            const int32_t* __restrict__ slot, int32_t num_experts, int32_t rank,
+                            int32_t local, int32_t max_rows, const int32_t* __restrict__ counts,
+                            int32_t* __restrict__ cursor, int32_t* __restrict__ offsets,
+                            int32_t* __restrict__ route_row, int32_t* __restrict__ src_token,
+                            float* __restrict__ row_scale, uint8_t* __restrict__ out_codes,
+                            uint8_t* __restrict__ out_sf, int* __restrict__ bad) {
+  griddep_wait();
+  __shared__ int32_t base[kExpandMaxLocal + 1];
+  if (threadIdx.x == 0) {  // local <= 1024: a serial scan of the counts
     int run = 0;
     for (int s = 0; s < local; ++s) {
       base[s] = run;
-      run += cnt[s];
+      run += counts[s];
     }
     base[local] = run;
   }
   __syncthreads();
-  for (int s = threadIdx.x; s <= local; s += blockDim.x) offsets[s] = min(base[s], max_rows);
-  for (int i = threadIdx.x; i < local; i += blockDim.x) cnt[i] = 0;  // cursors
-  __syncthreads();
-  for (int64_t r = threadIdx.x; r < routes; r += blockDim.x) {
-    const int s = local_slot(r);
-    int row = -1;
-    if (s >= 0) {
-      row = base[s] + atomicAdd(&cnt[s], 1);
-      if (row >= max_rows) {  // the caller's buffer is too small: flag, drop
-        atomicExch(bad, 2);
-        row = -1;
-      } else {
-        const int64_t tok = r / t.topk;
-        src_token[row] = int32_t(tok);
-        row_scale[row] = tok_scale(t, tok);
-      }
-    }
-    route_row[r] = row;
-  }
-  // the grouped GEMM behind this kernel may launch now
-  griddep_launch_dependents();
-}
-
-// Expanded rows: row r of the expert-ordered buffer is token src_token[r]'s
-// codes and scales, one warp per row.  The row count is the plan's last
-// offset (device), so the grid's warps stride over at most max_rows rows.
-template <bool kVec>
-__global__ void __launch_bounds__(256) moe_expand_rows_kernel(MoeTok t,
-                                                              const int32_t* __restrict__ src_token,
-                                                              const int32_t* __restrict__ count,
-                                                              int32_t max_rows,
-                                                              uint8_t* __restrict__ out_codes,
-                                                              uint8_t* __restrict__ out_sf,
-                                                              int* __restrict__ bad) {
-  griddep_wait();
-  const int rows = min(*count, max_rows);
+  if (blockIdx.x == 0)
+    for (int s = threadIdx.x; s <= local; s += blockDim.x) offsets[s] = min(base[s], max_rows);
+  const int lane = threadIdx.x & 31;
   const int kh = t.k / 2, ks = t.k / 16;
-  const int warps = int(gridDim.x * blockDim.x) >> 5;
-  // one row per warp at a time
-  for (int r = int((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r < rows; r += warps) {
-    const int64_t tok = src_token[r];
-    if (tok < 0 || tok >= t.num_tokens) {
-      if ((threadIdx.x & 31) == 0) atomicExch(bad, 1);
-      continue;
+  const int64_t routes = int64_t(t.num_tokens) * t.topk;
+  const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < routes; r += warps) {
+    int row = -1;
+    if (lane == 0) {
+      const int s = local_slot_of(t, r, owner, slot, num_experts, rank, local, bad);
+      if (s >= 0) {
+        row = base[s] + atomicAdd(cursor + s, 1);
+        if (row >= max_rows) {  // the caller's buffer is too small: flag, drop
+          atomicExch(bad, 2);
+          row = -1;
+        }
+      }
+      route_row[r] = row;
+    }
+    row = __shfl_sync(0xffffffffu, row, 0);
+    if (row < 0) continue;
+    const int64_t tok = r / t.topk;
+    if (lane == 0) {
+      src_token[row] = int32_t(tok);
+      row_scale[row] = tok_scale(t, tok);
     }
     if (kVec) {
-      warp_copy16(out_codes + int64_t(r) * kh, t.codes + tok * t.codes_stride, kh);
-      warp_copy16(out_sf + int64_t(r) * ks, t.sf + tok * t.sf_stride, ks);
+      warp_copy16(out_codes + int64_t(row) * kh, t.codes + tok * t.codes_stride, kh);
+      warp_copy16(out_sf + int64_t(row) * ks, t.sf + tok * t.sf_stride, ks);
     } else {
-      warp_copy4(out_codes + int64_t(r) * kh, t.codes + tok * t.codes_stride, kh);
-      warp_copy4(out_sf + int64_t(r) * ks, t.sf + tok * t.sf_stride, ks);
+      warp_copy4(out_codes + int64_t(row) * kh, t.codes + tok * t.codes_stride, kh);
+      warp_copy4(out_sf + int64_t(row) * ks, t.sf + tok * t.sf_stride, ks);
     }
   }
   griddep_launch_dependents();
@@ -538,50 +540,49 @@ int fgg_moe_records_view(const void* records, int32_t num_tokens, int32_t k, int
   return FGG_OK;
 }
 
-int fgg_moe_expand_plan(const FggMoeTokens* tokens, const int32_t* owner, const int32_t* slot,
-                        int32_t num_experts, int32_t rank, int32_t local, int32_t max_rows,
-                        int32_t* offsets, int32_t* route_row, int32_t* src_token,
-                        float* row_scale, int* bad, void* stream) {
+int fgg_moe_expand(const FggMoeTokens* tokens, const int32_t* owner, const int32_t* slot,
+                   int32_t num_experts, int32_t rank, int32_t local, int32_t max_rows,
+                   int32_t* counts, int32_t* offsets, int32_t* route_row, int32_t* src_token,
+                   float* row_scale, void* out_codes, void* out_sf, int* bad, void* stream) {
   MoeTok t;
   if (int rc = to_dev(tokens, &t)) return rc;
   if (num_experts < 1 || local < 1 || local > kExpandMaxLocal || rank < 0 || max_rows < 0)
     return set_error(FGG_EBADSHAPE, "need num_experts >= 1, 1 <= local <= %d, rank >= 0",
                      kExpandMaxLocal);
-  if (int64_t(t.num_tokens) * t.topk > INT32_MAX) return set_error(FGG_EBADSHAPE, "too many routes");
-  if (owner == nullptr || slot == nullptr || offsets == nullptr || bad == nullptr ||
-      (t.num_tokens > 0 && route_row == nullptr) ||
-      (max_rows > 0 && (src_token == nullptr || row_scale == nullptr)))
+  const int64_t routes = int64_t(t.num_tokens) * t.topk;
+  if (routes > INT32_MAX) return set_error(FGG_EBADSHAPE, "too many routes");
+  if (owner == nullptr || slot == nullptr || counts == nullptr || offsets == nullptr ||
+      bad == nullptr || (routes > 0 && route_row == nullptr) ||
+      (max_rows > 0 && (src_token == nullptr || row_scale == nullptr || out_codes == nullptr ||
+                        out_sf == nullptr)))
     return set_error(FGG_EINVAL, "null pointer");
-  FGG_CUDA_CHECK(launch_pdl(moe_expand_plan_kernel, dim3(1), dim3(kExpandThreads), 0,
-                            reinterpret_cast<cudaStream_t>(stream), t, owner, slot, num_experts,
-                            rank, local, max_rows, offsets, route_row, src_token, row_scale, bad));
-  FGG_CUDA_CHECK(cudaGetLastError());
-  return FGG_OK;
-}
-
-int fgg_moe_expand_rows(const FggMoeTokens* tokens, const int32_t* src_token, const int32_t* count,
-                        int32_t max_rows, void* out_codes, void* out_sf, int* bad, void* stream) {
-  MoeTok t;
-  if (int rc = to_dev(tokens, &t)) return rc;
-  if (max_rows < 0) return set_error(FGG_EINVAL, "max_rows is negative");
-  if (max_rows == 0) return FGG_OK;
-  if (src_token == nullptr || count == nullptr || out_codes == nullptr || out_sf == nullptr ||
-      bad == nullptr || t.codes == nullptr || t.sf == nullptr)
-    return set_error(FGG_EINVAL, "null pointer");
+  if (routes > 0 && (t.codes == nullptr || t.sf == nullptr))
+    return set_error(FGG_EINVAL, "codes / sf is null");
+  const bool v16 = rows_vec16(t) && aligned16(out_codes) && aligned16(out_sf);
+  const bool v4 = rows_vec4(t) && aligned4(out_codes) && aligned4(out_sf);
+  if (routes > 0 && !v16 && !v4)
+    return set_error(FGG_EALIGN, "token rows must start on 4-byte boundaries");
   DeviceInfo dev;
   if (int rc = current_device(&dev)) return rc;
-  const int grid = std::min((max_rows + 7) / 8, dev.sm_count * 8);  // 8 rows in flight a block
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // counts[0, local) and the cursors counts[local, 2 local)
+  FGG_CUDA_CHECK(cudaMemsetAsync(counts, 0, 2 * size_t(local) * sizeof(int32_t), s));
+  const int count_grid = int(std::min<int64_t>((routes + 255) / 256, int64_t(dev.sm_count) * 2));
+  FGG_CUDA_CHECK(launch_pdl(moe_expand_count_kernel, dim3(std::max(count_grid, 1)), dim3(256), 0,
+                            s, t, owner, slot, num_experts, rank, local, counts, bad));
+  const int place_grid = int(std::min<int64_t>((routes + 7) / 8, int64_t(dev.sm_count) * 8));
   auto* oc = static_cast<uint8_t*>(out_codes);
   auto* of = static_cast<uint8_t*>(out_sf);
-  if (rows_vec16(t) && aligned16(out_codes) && aligned16(out_sf))
-    FGG_CUDA_CHECK(launch_pdl(moe_expand_rows_kernel<true>, dim3(grid), dim3(256), 0, s, t,
-                              src_token, count, max_rows, oc, of, bad));
-  else if (rows_vec4(t) && aligned4(out_codes) && aligned4(out_sf))
-    FGG_CUDA_CHECK(launch_pdl(moe_expand_rows_kernel<false>, dim3(grid), dim3(256), 0, s, t,
-                              src_token, count, max_rows, oc, of, bad));
+  if (v16)
+    FGG_CUDA_CHECK(launch_pdl(moe_expand_place_kernel<true>, dim3(std::max(place_grid, 1)),
+                              dim3(256), 0, s, t, owner, slot, num_experts, rank, local, max_rows,
+                              counts, counts + local, offsets, route_row, src_token, row_scale, oc,
+                              of, bad));
   else
-    return set_error(FGG_EALIGN, "token rows must start on 4-byte boundaries");
+    FGG_CUDA_CHECK(launch_pdl(moe_expand_place_kernel<false>, dim3(std::max(place_grid, 1)),
+                              dim3(256), 0, s, t, owner, slot, num_experts, rank, local, max_rows,
+                              counts, counts + local, offsets, route_row, src_token, row_scale, oc,
+                              of, bad));
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }

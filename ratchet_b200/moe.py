@@ -203,6 +203,7 @@ class ExpertParallelMoE:
             _lib.check(L.fgg_moe_records_view(b["gathered"].data_ptr(), W * C, self.k, topk, toks),
                        "fgg_moe_records_view")
             b["gathered_view"] = toks
+        b["counts"] = torch.empty(2 * E, dtype=torch.int32, device=dev)
         b["offsets"] = torch.empty(E + 1, dtype=torch.int32, device=dev)
         b["route_row"] = torch.empty(NT * topk, dtype=torch.int32, device=dev)
         b["src_token"] = torch.empty(R, dtype=torch.int32, device=dev)
@@ -287,14 +288,12 @@ class ExpertParallelMoE:
             mark("dispatch")
             toks = mine
         mark("expand")
-        _lib.check(L.fgg_moe_expand_plan(toks, self.owner_d.data_ptr(), self.slot_d.data_ptr(),
-                                         self.num_experts, self.rank, E, b["R"],
-                                         b["offsets"].data_ptr(), b["route_row"].data_ptr(),
-                                         b["src_token"].data_ptr(), b["row_scale"].data_ptr(),
-                                         self.bad.data_ptr(), stream), "fgg_moe_expand_plan")
-        _lib.check(L.fgg_moe_expand_rows(toks, b["src_token"].data_ptr(), b["offsets"][E:].data_ptr(),
-                                         b["R"], b["a"].data_ptr(), b["a_sf"].data_ptr(),
-                                         self.bad.data_ptr(), stream), "fgg_moe_expand_rows")
+        _lib.check(L.fgg_moe_expand(toks, self.owner_d.data_ptr(), self.slot_d.data_ptr(),
+                                    self.num_experts, self.rank, E, b["R"], b["counts"].data_ptr(),
+                                    b["offsets"].data_ptr(), b["route_row"].data_ptr(),
+                                    b["src_token"].data_ptr(), b["row_scale"].data_ptr(),
+                                    b["a"].data_ptr(), b["a_sf"].data_ptr(), self.bad.data_ptr(),
+                                    stream), "fgg_moe_expand")
         mark("gemm")
         _lib.check(L.fgg_nvfp4_grouped_gemm_rows(b["prob"], self.pack.buf.data_ptr(),
                                                  b["ws"].data_ptr(), b["ws"].numel(), stream),

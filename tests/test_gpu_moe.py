@@ -253,9 +253,9 @@ def _tok_view(codes, sf, ids, w, scale):
 
 
 def test_expand_kernels_bitexact(cuda_device):
-    """pack -> records view -> expand plan -> expand rows, against the same
-    steps in PyTorch: every record byte, the per-expert counts, each route's
-    row holding exactly that token's bytes, and -1 for absent and remote routes."""
+    """pack -> records view -> expand, against the same steps in PyTorch:
+    every record byte, the per-expert counts, each route's row holding exactly
+    that token's bytes and decode scale, and -1 for absent and remote routes."""
     from ratchet_b200 import _lib
 
     L = _lib.lib()
@@ -284,19 +284,19 @@ def test_expand_kernels_bitexact(cuda_device):
     owner, slot = moe.place_experts(moe.expert_popularity(Ex, seed=5), world)
     loc = Ex // world
     R = T * topk
+    counts = torch.full((2 * loc,), 99, dtype=torch.int32, device=dev)   # zeroed by the call
     offsets = torch.empty(loc + 1, dtype=torch.int32, device=dev)
     route_row = torch.empty(T * topk, dtype=torch.int32, device=dev)
     src_tok = torch.full((R,), -7, dtype=torch.int32, device=dev)
     rscale = torch.empty(R, dtype=torch.float32, device=dev)
     bad = torch.zeros(1, dtype=torch.int32, device=dev)
     o_d, s_d = torch.from_numpy(owner).to(dev), torch.from_numpy(slot).to(dev)
-    _lib.check(L.fgg_moe_expand_plan(view, o_d.data_ptr(), s_d.data_ptr(), Ex, rank, loc, R,
-                                     offsets.data_ptr(), route_row.data_ptr(), src_tok.data_ptr(),
-                                     rscale.data_ptr(), bad.data_ptr(), st), "plan")
     a = torch.empty((R, kh), dtype=torch.uint8, device=dev)
     a_sf = torch.empty((R, ks), dtype=torch.uint8, device=dev)
-    _lib.check(L.fgg_moe_expand_rows(view, src_tok.data_ptr(), offsets[loc:].data_ptr(), R,
-                                     a.data_ptr(), a_sf.data_ptr(), bad.data_ptr(), st), "rows")
+    _lib.check(L.fgg_moe_expand(view, o_d.data_ptr(), s_d.data_ptr(), Ex, rank, loc, R,
+                                counts.data_ptr(), offsets.data_ptr(), route_row.data_ptr(),
+                                src_tok.data_ptr(), rscale.data_ptr(), a.data_ptr(),
+                                a_sf.data_ptr(), bad.data_ptr(), st), "expand")
     torch.cuda.synchronize()
     assert int(bad.item()) == 0
     flat = ids_np.reshape(-1)
