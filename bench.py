@@ -873,11 +873,12 @@ def run_moe(args, wl):
     The 4096 tokens are split evenly over the ranks (each rank routes its own
     share); the 64 experts are placed by expected load (LPT, equal counts).
     A step = pack + all-gather dispatch + expand + grouped GEMM + weighted
-    reduce + all-to-all combine + partial sum, with no host synchronisation.
-    Total work is fixed, so the scaling is strong; value = all FLOPs / the
-    slowest rank's step time.  The line carries a per-phase breakdown (CUDA
-    events between the phases on the compute stream, mean over the timed
-    steps, max over ranks)."""
+    reduce + all-to-all combine + partial sum, with no host synchronisation,
+    replayed from one CUDA graph.  Total work is fixed, so the scaling is
+    strong; value = all FLOPs / the slowest rank's step time.  The line also
+    carries a per-phase breakdown of the same forward issued eagerly (CUDA
+    events between the phases on the compute stream, mean over the steps,
+    max over ranks)."""
     from ratchet_b200 import moe
 
     ws, rank, local = dist_init()
@@ -895,21 +896,43 @@ def run_moe(args, wl):
     torch.cuda.synchronize()
     fl = 2.0 * T * topk * n * k
 
-    def step(ev=None):
-        return layer.forward(xc, xs, xg, ids, wts, events=ev)
-
+    # 1. eager forwards with CUDA events between the phases: the per-phase
+    #    breakdown and the host's enqueue time per forward (not the value)
     for _ in range(args.warmup):
-        step()
+        layer.forward(xc, xs, xg, ids, wts)
+    torch.cuda.synchronize()
+    barrier(ws)
+    evs = [dict() for _ in range(args.steps)]
+    h0 = time.perf_counter()
+    for i in range(args.steps):
+        layer.forward(xc, xs, xg, ids, wts, events=evs[i])
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
+    torch.cuda.synchronize()
+    barrier(ws)
+    layer.check()
+    names = list(moe.PHASES) + ["end"]
+    phases = {}
+    for a, b in zip(names[:-1], names[1:]):
+        mean = sum(ev[a].elapsed_time(ev[b]) for ev in evs) / args.steps
+        phases[a] = max_over_ranks(mean, ws, dev)
+    eager_steps = [ev["pack"].elapsed_time(ev["end"]) for ev in evs]
+    eager_ms = max_over_ranks(statistics.median(eager_steps), ws, dev)
+    host_ms = max_over_ranks(host_ms, ws, dev)
+
+    # 2. the timed steps: the whole layer (kernels and collectives) replayed
+    #    from one CUDA graph per step
+    replay, out_g = layer.capture(xc, xs, xg, ids, wts)
+    for _ in range(args.warmup):
+        replay()
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    evs = [dict() for _ in range(args.steps)]
     e0.record()
     for i in range(args.steps):
-        step(evs[i])
+        replay()
     e1.record()
     torch.cuda.synchronize()
     barrier(ws)
@@ -918,11 +941,6 @@ def run_moe(args, wl):
     layer.check()
     rb.last_status()
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws, dev)
-    names = list(moe.PHASES) + ["end"]
-    phases = {}
-    for a, b in zip(names[:-1], names[1:]):
-        mean = sum(ev[a].elapsed_time(ev[b]) for ev in evs) / args.steps
-        phases[a] = max_over_ranks(mean, ws, dev)
     g_ms = phases["gemm"]
     # GEMM rows on this rank (the kernel's FLOPs): the routes of its experts from every rank
     counts = np.bincount(ids_all.ravel(), minlength=E)
@@ -935,20 +953,21 @@ def run_moe(args, wl):
             "frac": achieved / peak, "traffic": traffic_from_profiles("moe"),
             "peak_basis": f"4 x {pk['src']} dense bf16 ({pk['bf16']:.0f} TF/s)",
             "kernel_ms": g_ms, "kernel": "grouped GEMM inside the layer (device-offset prepare + "
-                                        "fgg_gemm_pair_kernel), slowest rank"}
+                                        "fgg_gemm_pair_kernel), slowest rank, eager pass"}
 
-    # end to end: this rank's activations from pinned host memory, the output back
+    # 3. end to end: this rank's activations from pinned host memory into the
+    #    graph's input tensors, the replay, the output back to pinned memory
     h_xc = xc.cpu().pin_memory()
     h_xs = xs.view(torch.uint8).cpu().pin_memory()
-    d_xc, d_xs = torch.empty_like(xc), torch.empty_like(xs.view(torch.uint8))
     h_out = torch.empty((tl, n), dtype=torch.bfloat16).pin_memory()
+    xs_u8 = xs.view(torch.uint8)
     e2e_steps = args.steps
 
     def e2e_step():
-        d_xc.copy_(h_xc, non_blocking=True)
-        d_xs.copy_(h_xs, non_blocking=True)
-        out = layer.forward(d_xc, d_xs.view(torch.float8_e4m3fn), xg, ids, wts)
-        h_out.copy_(out, non_blocking=True)
+        xc.copy_(h_xc, non_blocking=True)
+        xs_u8.copy_(h_xs, non_blocking=True)
+        replay()
+        h_out.copy_(out_g, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -963,6 +982,8 @@ def run_moe(args, wl):
     barrier(ws)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, ws, dev)
+    del replay
+    layer.release()
 
     if rank == 0:
         line = {
@@ -982,6 +1003,9 @@ def run_moe(args, wl):
                        "l2": f"expert weights {E * n * k * 0.5625 / ws / 1e6:.0f} MB per rank "
                              "read every step"},
             "phases_ms": phases,
+            "eager": {"ms_per_step_median": eager_ms, "host_enqueue_ms": host_ms,
+                      "note": "the same forward issued kernel by kernel (phases_ms come from it); "
+                              "the timed steps replay it from one CUDA graph"},
             "clocks": clocks,
             "e2e": {"value": fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": int(h_xc.numel() + h_xs.numel()) * ws,

@@ -165,6 +165,7 @@ class ExpertParallelMoE:
         self.bufs = None
         self.pack = None
         self.bad = None
+        self._graph = None
         if gemm_fn is None:
             # the product path: weights packed once and reused by every
             # forward; the kernels raise this flag on a bad id or index
@@ -313,6 +314,37 @@ class ExpertParallelMoE:
                        "fgg_moe_sum_partials")
         mark("end")
         return out
+
+    def capture(self, x_codes: torch.Tensor, x_sf: torch.Tensor, x_scale, topk_ids: torch.Tensor,
+                topk_weights: torch.Tensor | None = None, warmup: int = 2):
+        """Capture forward() on these input tensors into a CUDA graph and return
+        (replay, out): replay() re-runs the whole layer -- every kernel and both
+        collectives -- from one graph launch, reading whatever the input tensors
+        hold at that moment, and leaves the result in `out` (the same tensor on
+        every replay).  The host then issues one launch per forward instead of
+        a dozen kernels and two collectives, so the device never waits for it.
+        The warm-up forwards (outside the capture) set up the buffers and the
+        collectives' communicators first."""
+        if self.gemm_fn is not None:
+            raise ValueError("capture needs the device path")
+        for _ in range(warmup):
+            self.forward(x_codes, x_sf, x_scale, topk_ids, topk_weights)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                out = self.forward(x_codes, x_sf, x_scale, topk_ids, topk_weights)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        self._graph = g  # released with the layer (before any process-group teardown)
+        return g.replay, out
+
+    def release(self) -> None:
+        """Drop a captured graph (it holds the collectives' captured work): call
+        before destroying the process group."""
+        self._graph = None
 
     # ------------------------------------------------ host emulation (tests)
     def _forward_host(self, x_u8, s_u8, x_scale, topk_ids, topk_weights):
