@@ -117,7 +117,7 @@ while not select.select([sys.stdin], [], [], 0)[0]:
     except Exception as e:
         err = str(e)
         break
-    time.sleep(0.0002)
+    time.sleep(0.005)
 print(json.dumps({"samples": out, "err": err}), flush=True)
 """
 
@@ -187,7 +187,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm),
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons), "samples": len(sm),
                 "power_w_max": max(p for _, _, p in samples) / 1000.0,
-                "source": "NVML in a child process, ~1 ms polling during the timed region"}
+                "source": "NVML in a child process, ~5 ms polling during the timed region"}
 
 
 def dist_init():
