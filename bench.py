@@ -1,28 +1,34 @@
 #!/usr/bin/env python
-"""Grouped NVFP4 GEMM benchmark on B200.
+"""Block-scaled FP4 grouped GEMM benchmark on B200.
 
-Default workload = the headline config (8 groups, M_g ~ U[64, 1024] seeded,
-N=4096, K=7168, NVFP4 x NVFP4 -> bf16).  Other configs: --config dense
-(8192^3) and --config decode (256 groups, M_g ~ U[1, 16], N=7168, K=2048).
+Default workload = BASELINE config 3, the expert-parallel MoE layer (4096
+tokens, top-8 of 64 experts with Zipf(1.1) routing, N=4096, K=7168, NVFP4),
+the one workload that runs at every GPU count: experts sharded over the
+ranks, tokens dispatched and combined with NCCL collectives (strong
+scaling).  Other configs: --config grouped (config 2: 8 groups,
+M_g ~ U[64, 1024], N=4096, K=7168; replicas under torchrun), dense (config 4,
+8192^3; N split over the ranks), decode (config 5, 256 groups,
+M_g ~ U[1, 16], N=7168, K=2048; groups sharded by LPT), mlp (the gated
+expert MLP), mx (the reference operator fp4_grouped_gemm at its campaign
+point).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C]
+                    [--impl ours|reference|reference-gpu]
 
-Prints ONE JSON line on rank 0.  Under torchrun every rank runs its own
-instance of the workload (weak scaling; no collective on the data path),
-timed between barriers, max over ranks.
+Prints ONE JSON line on rank 0: barrier + synchronize around exactly K timed
+steps after W warm-up steps, max over ranks.
 
-  value       TFLOP/s of the public operator call (prepare + GEMM kernels)
-              with inputs resident in HBM, K steps back to back; R rotating
-              input sets whose total exceeds the 126 MB L2 (config.l2)
-  e2e         the same call fed from pinned host buffers: per step one H2D of
-              the activation codes + scales, the call, one D2H of the output,
-              pipelined over three streams (copy-in / compute / copy-out)
-  roofline    the GEMM kernel alone (CUDA events around K launches on the
-              launching stream) against 4 x the measured dense bf16 peak
+  value       TFLOP/s of the public call with inputs resident in HBM
+  e2e         the same call fed from pinned host buffers (H2D of the inputs
+              and D2H of the output inside the timed region)
+  roofline    the GEMM kernel against 4 x the measured dense bf16 peak
               (B200's dense FP4 rate is 4x its bf16 rate), or against the
               measured HBM copy bandwidth for the decode config
   cpu_baseline  the CPU oracle (dequantise + fp32 matmul, all host threads)
               on a bounded sample of the same workload, rank 0, N=1
+  --impl reference      that CPU oracle alone on the same config
+  --impl reference-gpu  the reference's own kernel (baseline/_ref) beside
+              fp4_grouped_gemm on one B200 (config mx)
 """
 from __future__ import annotations
 
@@ -222,36 +228,106 @@ def barrier(ws: int):
 
 
 # ------------------------------------------------------------------ inputs
+def shard(wl, ws: int, rank: int) -> dict:
+    """This rank's part of the workload.  grouped / mlp / mx: every rank runs
+    the whole workload (independent replicas, weak scaling).  dense: the
+    weight rows (output columns) split evenly, the activations replicated
+    (strong scaling).  decode: whole groups placed by longest-processing-time
+    on their weight bytes (strong scaling)."""
+    sub = dict(wl)
+    sub["groups"] = list(range(len(wl["m"])))
+    sub["w_rows"] = (0, wl["n"])
+    if ws == 1:
+        sub["split"] = "none"
+        return sub
+    if wl["name"] == "dense":
+        if wl["n"] % (256 * ws):
+            raise SystemExit(f"N={wl['n']} does not split into {ws} slices of 256-row tiles")
+        per = wl["n"] // ws
+        sub["n"] = per
+        sub["w_rows"] = (rank * per, (rank + 1) * per)
+        sub["split"] = f"N split: weight rows [{rank * per}, {(rank + 1) * per}) of {wl['n']}"
+        return sub
+    if wl["name"] == "decode":
+        wbytes = wl["n"] * (wl["k"] // 2 + wl["k"] // 16)   # every group's weights
+        load = [0] * ws
+        owner = []
+        for g in sorted(range(len(wl["m"])), key=lambda g: (-wbytes, g)):
+            r = min(range(ws), key=lambda r: (load[r], r))
+            owner.append((g, r))
+            load[r] += wbytes
+        sub["groups"] = sorted(g for g, r in owner if r == rank)
+        sub["m"] = [wl["m"][g] for g in sub["groups"]]
+        sub["split"] = f"groups by LPT on weight bytes: {len(sub['groups'])} of {len(wl['m'])}"
+        return sub
+    sub["split"] = "replica"
+    return sub
+
+
 def make_set(wl, seed: int, dev):
     """One input set on the device: N(0,1) activations and N(0, w_std) weights,
-    each quantised to NVFP4 with its own global scale by the device quantiser."""
+    each quantised to NVFP4 with its own global scale by the device quantiser.
+    Every group draws from its own seeded stream, so a group's data does not
+    depend on how the groups are sharded; the dense split takes its rows of
+    one seeded weight tensor.  The activation codes and scales of all groups
+    live in one contiguous buffer (the per-group tensors are row views of it)."""
     import ratchet_b200 as rb
 
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(seed)
     n, k = wl["n"], wl["k"]
-    A, ASF, B, BSF, alpha = [], [], [], [], []
-    for m in wl["m"]:
+    groups = wl.get("groups", list(range(len(wl["m"]))))
+    r0, r1 = wl.get("w_rows", (0, n))
+    ms = list(wl["m"])
+    rows = sum(ms)
+    a_all = torch.empty((rows, k // 2), dtype=torch.uint8, device=dev)
+    sf_all = torch.empty((rows, k // 16), dtype=torch.uint8, device=dev)
+    B, BSF, alpha = [], [], []
+    at = 0
+    for g, m in zip(groups, ms):
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed * 100003 + 2 * g)
         x = torch.randn((m, k), generator=gen, device=dev, dtype=torch.float32)
-        w = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32) * wl["w_std"]
         qa, sa, ga = rb.quantize_nvfp4(x)
-        qb, sb, gb = rb.quantize_nvfp4(w)
+        a_all[at:at + m].copy_(qa)
+        sf_all[at:at + m].copy_(sa.view(torch.uint8))
+        at += m
+        gen.manual_seed(seed * 100003 + 2 * g + 1)
+        w = torch.randn((r1 if wl["name"] == "dense" else n, k), generator=gen, device=dev,
+                        dtype=torch.float32)[r0:r1 if wl["name"] == "dense" else n]
+        w = w * wl["w_std"]
+        qb, sb, gb = rb.quantize_nvfp4(w.contiguous())
         del x, w
-        A.append(qa)
-        ASF.append(sa)
         B.append(qb)
         BSF.append(sb)
         alpha.append(ga * gb)
-    return dict(a=A, a_sf=ASF, b=B, b_sf=BSF, alpha=torch.stack(alpha).float(),
-                sizes=[(m, n, k) for m in wl["m"]])
+    off = torch.zeros(len(ms) + 1, dtype=torch.int32)
+    off[1:] = torch.cumsum(torch.tensor(ms, dtype=torch.int64), 0).to(torch.int32)
+    return dict(a=list(a_all.split(ms)), a_sf=[t.view(torch.float8_e4m3fn) for t in sf_all.split(ms)],
+                a_all=a_all, sf_all=sf_all.view(torch.float8_e4m3fn), offsets=off.to(dev),
+                b=B, b_sf=BSF, alpha=torch.stack(alpha).float(), sizes=[(m, n, k) for m in ms],
+                max_m=max(ms) if ms else 0)
+
+
+def public_call(s, out=None):
+    """The public operator call a step makes: the per-group-list operator
+    (the reference operator's NVFP4 drop-in), or for decode-shaped sets (every
+    M_g <= 16) the contiguous-rows form with device offsets, whose host work
+    does not grow with the group count."""
+    import ratchet_b200 as rb
+
+    if s["max_m"] <= 16:
+        if "pack" not in s:
+            s["pack"] = rb.pack_weights(s["b"], s["b_sf"])
+        return rb.nvfp4_grouped_gemm_rows(s["a_all"], s["sf_all"], s["offsets"], pack=s["pack"],
+                                          alpha=s["alpha"], out=out, max_group_rows=16)
+    return rb.nvfp4_grouped_gemm(s["a"], s["a_sf"], s["b"], s["b_sf"], s["sizes"], s["alpha"],
+                                 out=out)
 
 
 def time_value(sets, steps, warmup, dev, ws):
     import ratchet_b200 as rb
 
     R = len(sets)
-    call = lambda s: rb.nvfp4_grouped_gemm(s["a"], s["a_sf"], s["b"], s["b_sf"], s["sizes"],
-                                           s["alpha"])
+    call = lambda s: public_call(s)
     for i in range(warmup):
         call(sets[i % R])
     torch.cuda.synchronize()
@@ -327,18 +403,14 @@ def time_e2e(sets, steps, warmup, dev, ws):
     k = sets[0]["sizes"][0][2]
     bufs = []
     for s in sets:
-        ms = [int(t.shape[0]) for t in s["a"]]
-        rows = sum(ms)
-        codes = torch.cat([t.view(torch.uint8) for t in s["a"]]).cpu().pin_memory()
-        scales = torch.cat([t.view(torch.uint8) for t in s["a_sf"]]).cpu().pin_memory()
-        d_codes, d_scales = codes.to(dev), scales.to(dev)
-        # per-group views into the device staging buffers, made once
-        a_views = list(d_codes.split(ms))
-        sf_views = [v.view(torch.float8_e4m3fn) for v in d_scales.split(ms)]
+        rows = int(s["a_all"].shape[0])
+        codes = s["a_all"].cpu().pin_memory()
+        scales = s["sf_all"].view(torch.uint8).cpu().pin_memory()
         out = torch.empty((rows, n), dtype=torch.bfloat16, device=dev)
         hout = torch.empty((rows, n), dtype=torch.bfloat16).pin_memory()
-        bufs.append(dict(codes=codes, scales=scales, d_codes=d_codes, d_scales=d_scales,
-                         a=a_views, sf=sf_views, out=out, hout=hout))
+        # the step's H2D lands in the set's own contiguous activation buffers
+        bufs.append(dict(codes=codes, scales=scales, d_codes=s["a_all"],
+                         d_scales=s["sf_all"].view(torch.uint8), out=out, hout=hout))
     h2d = bufs[0]["codes"].numel() + bufs[0]["scales"].numel()
     d2h = bufs[0]["hout"].numel() * 2
     s_in, s_run, s_back = (torch.cuda.Stream(dev) for _ in range(3))
@@ -361,8 +433,7 @@ def time_e2e(sets, steps, warmup, dev, ws):
             s_run.wait_event(ready[b])
             if used[b]:
                 s_run.wait_event(drained[b])  # the previous read-back of set b's output
-            rb.nvfp4_grouped_gemm(B["a"], B["sf"], s["b"], s["b_sf"], s["sizes"], s["alpha"],
-                                  out=B["out"])
+            public_call(s, out=B["out"])
             computed[b].record(s_run)
         with torch.cuda.stream(s_back):
             s_back.wait_event(computed[b])
@@ -711,11 +782,11 @@ def run_mx(args, wl):
     call = lambda: rb.fp4_grouped_gemm(a, a_sf, b, b_sf, mi)
     for _ in range(args.warmup):
         call()
+    sampler = ClockSampler(local)  # started before the barrier (see run_moe)
+    sampler.start()
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
@@ -770,10 +841,13 @@ def run_ours(args, wl):
     dev = torch.device("cuda", local)
     import ratchet_b200 as rb  # noqa: F401  (fails loudly without the native library)
 
-    seed0 = 1000 * rank
-    per_set = set_bytes(wl)
+    sub = shard(wl, ws, rank)
+    strong = sub["split"] not in ("none", "replica")
+    # replicas draw their own data; a split workload draws the same problem on every rank
+    seed0 = 0 if strong else 1000 * rank
+    per_set = set_bytes(sub)
     R = max(1, min(8, int(np.ceil(2.0 * L2_BYTES / per_set)) + (1 if per_set < L2_BYTES else 0)))
-    sets = [make_set(wl, seed0 + s, dev) for s in range(R)]
+    sets = [make_set(sub, seed0 + s, dev) for s in range(R)]
     torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
@@ -781,26 +855,29 @@ def run_ours(args, wl):
     ms = time_value(sets, args.steps, args.warmup, dev, ws)
     clocks = sampler.stop()
     ms = max_over_ranks(ms, ws, dev)
-    fl = flops(wl)
-    value = fl * ws / (ms * 1e-3) / 1e12
+    fl_rank = flops(sub)
+    fl = flops(wl) if strong else fl_rank * ws     # work of the whole job
+    value = fl / (ms * 1e-3) / 1e12
 
     k_ms = time_kernel_only(sets, args.steps, dev)
-    k_ms = max_over_ranks(k_ms, ws, dev)
     pk = peaks()
+    # the roofline of the slowest rank's GEMM kernel against its own work
     if wl["bound"] == "tensor":
-        achieved = fl / (k_ms * 1e-3) / 1e12
-        peak = 4.0 * pk["bf16"]
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": traffic_from_profiles(wl["name"]),
+        achieved = fl_rank / (k_ms * 1e-3) / 1e12
+        frac = max_over_ranks(-achieved / (4.0 * pk["bf16"]), ws, dev) * -1.0
+        k_ms = max_over_ranks(k_ms, ws, dev)
+        roof = {"bound": "tensor", "achieved": frac * 4.0 * pk["bf16"], "peak": 4.0 * pk["bf16"],
+                "unit": "TFLOP/s", "frac": frac, "traffic": traffic_from_profiles(wl["name"]),
                 "peak_basis": f"4 x {pk['src']} dense bf16 ({pk['bf16']:.0f} TF/s)",
-                "kernel_ms": k_ms, "alg_bytes": alg_bytes(wl)}
+                "kernel_ms": k_ms, "alg_bytes": alg_bytes(sub)}
     else:
-        achieved = alg_bytes(wl) / (k_ms * 1e-3) / 1e9
-        peak = pk["hbm"]
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "traffic": traffic_from_profiles(wl["name"]),
+        achieved = alg_bytes(sub) / (k_ms * 1e-3) / 1e9
+        frac = max_over_ranks(-achieved / pk["hbm"], ws, dev) * -1.0
+        k_ms = max_over_ranks(k_ms, ws, dev)
+        roof = {"bound": "hbm", "achieved": frac * pk["hbm"], "peak": pk["hbm"], "unit": "GB/s",
+                "frac": frac, "traffic": traffic_from_profiles(wl["name"]),
                 "peak_basis": f"{pk['src']} HBM copy", "kernel_ms": k_ms,
-                "alg_bytes": alg_bytes(wl)}
+                "alg_bytes": alg_bytes(sub)}
 
     if args.no_e2e:
         e2e_ms, h2d, d2h = float("nan"), 0, 0
@@ -816,16 +893,25 @@ def run_ours(args, wl):
         line = {
             "metric": "grouped-GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "vs_baseline": None,
             "dtype": "nvfp4 (e2m1 x e2m1, e4m3/16 scales, fp32 acc, bf16 out)",
             "data": "synthetic (seeded N(0,1) activations, N(0,w_std) weights, NVFP4-quantised)",
             "config": {"workload": wl["desc"], "groups": len(wl["m"]), "sum_m": sum(wl["m"]),
-                       "n": wl["n"], "k": wl["k"], "parallelism": f"replicas x{ws}",
-                       "l2": f"{R} rotating input sets of {per_set / 1e6:.0f} MB (> L2 in total)"},
+                       "n": wl["n"], "k": wl["k"],
+                       "parallelism": (f"replicas x{ws}" if not strong else
+                                       ("N split" if wl["name"] == "dense" else "groups sharded")
+                                       + f" over {ws}"),
+                       "rank0_part": sub["split"],
+                       "call": "nvfp4_grouped_gemm_rows (device offsets)" if sets[0]["max_m"] <= 16
+                               else "nvfp4_grouped_gemm (per-group lists)",
+                       "l2": f"{R} rotating input sets of {per_set / 1e6:.0f} MB per rank "
+                             "(> L2 in total)"},
             "clocks": clocks,
             "e2e": None if args.no_e2e else {
-                "value": fl * ws / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "value": fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d * ws, "d2h_bytes_per_step": d2h * ws,
+                "ms_per_step": e2e_ms},
             "gpu_launches": 2 * args.steps,
             "roofline": roof,
             "cpu_baseline": cpu,
@@ -836,6 +922,7 @@ def run_ours(args, wl):
 
         dist.destroy_process_group()
     return 0
+
 
 def moe_setup(wl, ws: int, rank: int, dev) -> dict:
     """Config 3's seeded inputs for one rank of an ws-way expert-parallel run:
@@ -924,11 +1011,13 @@ def run_moe(args, wl):
     replay, out_g = layer.capture(xc, xs, xg, ids, wts)
     for _ in range(args.warmup):
         replay()
+    # the sampler starts before the barrier: a rank still spawning it would
+    # hold the others' first collective
+    sampler = ClockSampler(local)
+    sampler.start()
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(args.steps):
@@ -1054,11 +1143,11 @@ def run_mlp(args, wl):
     call = lambda: rb.nvfp4_expert_mlp(A, ASF, alpha13, W13, W13SF, W2, W2SF, w2s)
     for _ in range(args.warmup):
         call()
+    sampler = ClockSampler(local)  # started before the barrier (see run_moe)
+    sampler.start()
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
@@ -1122,7 +1211,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours")
     ap.add_argument("--config", choices=["grouped", "dense", "decode", "moe", "mlp", "mx"],
-                    default="grouped")
+                    default="moe")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     args = ap.parse_args()

@@ -7,10 +7,11 @@ kernel behind the C ABI in include/fgg_api.h.
 """
 from ._lib import FggError
 from .ops import (WeightPack, clear_caches, fp4_grouped_gemm, interleave_gate_up, last_status,
-                  nvfp4_expert_mlp, nvfp4_grouped_gemm, nvfp4_grouped_gemm_silu_mul, pack_weights,
-                  quantize_nvfp4)
+                  nvfp4_expert_mlp, nvfp4_grouped_gemm, nvfp4_grouped_gemm_rows,
+                  nvfp4_grouped_gemm_silu_mul, pack_weights, quantize_nvfp4)
 
-__all__ = ["fp4_grouped_gemm", "nvfp4_grouped_gemm", "nvfp4_grouped_gemm_silu_mul",
+__all__ = ["fp4_grouped_gemm", "nvfp4_grouped_gemm", "nvfp4_grouped_gemm_rows",
+           "nvfp4_grouped_gemm_silu_mul",
            "interleave_gate_up", "nvfp4_expert_mlp", "pack_weights", "WeightPack",
            "quantize_nvfp4", "last_status", "clear_caches", "FggError"]
-__version__ = "0.1.0"
+__version__ = "0.2.0"

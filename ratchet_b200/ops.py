@@ -354,6 +354,106 @@ def _nvfp4_grouped(a_list, a_sf_list, b_list, b_sf_list, problem_sizes, alpha, p
     return list(out.split_with_sizes(ms))
 
 
+# Problem structs and workspaces of the contiguous-rows entry, per geometry:
+# a repeated call only patches pointers (no per-group host work at all).
+_ROWS: OrderedDict = OrderedDict()
+
+
+def nvfp4_grouped_gemm_rows(a: torch.Tensor, a_sf: torch.Tensor, offsets: torch.Tensor,
+                            b_list=None, b_sf_list=None, alpha=None, *,
+                            pack: WeightPack | None = None, out: torch.Tensor | None = None,
+                            row_scale: torch.Tensor | None = None,
+                            b_index: torch.Tensor | None = None,
+                            max_group_rows: int = 0) -> torch.Tensor:
+    """Grouped GEMM over contiguous token rows, group sizes on the device.
+
+    The reference operator's own M-grouped layout (one concatenated activation
+    tensor, kernels/gemm/fp4_grouped_gemm/b200/kernel.py:10-37) in NVFP4: group
+    g owns rows [offsets[g], offsets[g+1]) of
+      a      [R, K/2] packed E2M1 codes (uint8 / float4_e2m1fn_x2)
+      a_sf   [R, K/16] E4M3 scales
+      out    [R, N] bf16 (allocated when not given; rows outside every group
+             are left as they are)
+    offsets: int32 CUDA tensor [G + 1] (nondecreasing, offsets[G] <= R); it may
+    be written by an earlier kernel on the stream -- the host never reads it.
+    Weights come from `pack` (or b_list / b_sf_list, packed and cached);
+    alpha: fp32 CUDA tensor [G]; row_scale: optional fp32 CUDA tensor [R]
+    (out = alpha_g * row_scale_r * acc); b_index: optional int32 CUDA tensor
+    [G] naming each group's packed weight group; max_group_rows: a host bound
+    on every group's rows (<= 16 selects the decode tiles).  Host work per
+    call does not depend on G: no per-group Python."""
+    global _last_ws
+    if pack is None:
+        if b_list is None or b_sf_list is None:
+            raise ValueError("give pack= or b_list / b_sf_list")
+        pack = pack_weights(b_list, b_sf_list)
+    n, k, dev = pack.n, pack.k, pack.device
+    a_u8 = _as_u8(a, "a")
+    s_u8 = _as_u8(a_sf, "a_sf")
+    if a_u8.dim() != 2 or a_u8.shape[1] != k // 2 or s_u8.shape != (a_u8.shape[0], k // 16):
+        raise ValueError(f"a {tuple(a_u8.shape)} / a_sf {tuple(s_u8.shape)} do not match "
+                         f"[R, {k // 2}] / [R, {k // 16}] for K={k}")
+    if not (a_u8.is_contiguous() and s_u8.is_contiguous() and a_u8.device == dev
+            and s_u8.device == dev):
+        raise ValueError(f"a and a_sf must be contiguous tensors on {dev}")
+    if (offsets.dtype != torch.int32 or offsets.dim() != 1 or offsets.device != dev
+            or not offsets.is_contiguous()):
+        raise ValueError(f"offsets must be a contiguous int32 tensor on {dev}")
+    G = int(offsets.shape[0]) - 1
+    R = int(a_u8.shape[0])
+    if alpha is None:
+        alpha = torch.ones(G, dtype=torch.float32, device=dev)
+    if (alpha.dtype != torch.float32 or alpha.numel() != G or alpha.device != dev
+            or not alpha.is_contiguous()):
+        raise ValueError(f"alpha must be a contiguous fp32 tensor of {G} values on {dev}")
+    if out is None:
+        out = torch.empty((R, n), dtype=torch.bfloat16, device=dev)
+    elif (out.dtype != torch.bfloat16 or out.shape != (R, n) or not out.is_contiguous()
+          or out.device != dev):
+        raise ValueError(f"out must be a contiguous bf16 [{R}, {n}] tensor on {dev}")
+    for name, t, dt, cnt in (("row_scale", row_scale, torch.float32, R),
+                             ("b_index", b_index, torch.int32, G)):
+        if t is not None and (t.dtype != dt or t.numel() != cnt or t.device != dev
+                              or not t.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous {dt} tensor of {cnt} values on {dev}")
+    L = _lib.lib()
+    key = (dev.index, G, n, k, R, int(max_group_rows), b_index is not None, pack.G)
+    hit = _ROWS.get(key)
+    if hit is None:
+        prob = _lib.FggNvfp4RowsProblem(G, n, k, R, 0, 0, 0, 0, 0, 0, 0, pack.G,
+                                        int(max_group_rows))
+        nbytes = int(L.fgg_nvfp4_rows_workspace_bytes(prob))
+        if nbytes == 0:
+            _lib.check(L.fgg_nvfp4_grouped_gemm_rows(prob, None, None, 0, None), "grouped GEMM rows")
+        hit = [prob, nbytes]
+        _ROWS[key] = hit
+        while len(_ROWS) > _CACHE_MAX:
+            _ROWS.popitem(last=False)
+    else:
+        _ROWS.move_to_end(key)
+    prob, nbytes = hit
+    prob.offsets = offsets.data_ptr()
+    prob.a = a_u8.data_ptr()
+    prob.a_sf = s_u8.data_ptr()
+    prob.alpha = alpha.data_ptr()
+    prob.out = out.data_ptr()
+    prob.row_scale = row_scale.data_ptr() if row_scale is not None else None
+    prob.b_index = b_index.data_ptr() if b_index is not None else None
+    if _is_current(dev):
+        stream = _stream_ptr(dev)
+        ws = _workspace(dev, stream, nbytes)
+        rc = L.fgg_nvfp4_grouped_gemm_rows(prob, pack.buf.data_ptr(), ws.data_ptr(), nbytes, stream)
+    else:
+        with torch.cuda.device(dev):
+            stream = _stream_ptr(dev)
+            ws = _workspace(dev, stream, nbytes)
+            rc = L.fgg_nvfp4_grouped_gemm_rows(prob, pack.buf.data_ptr(), ws.data_ptr(), nbytes,
+                                               stream)
+    _lib.check(rc, "nvfp4_grouped_gemm_rows")
+    _last_ws = ws
+    return out
+
+
 class _MxPrepared:
     def __init__(self, ws: torch.Tensor, sources):
         self.ws = ws
@@ -474,3 +574,4 @@ def last_status() -> int:
 def clear_caches() -> None:
     _PACKS.clear()
     _MX_PREP.clear()
+    _ROWS.clear()
