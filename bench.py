@@ -123,7 +123,7 @@ while not select.select([sys.stdin], [], [], 0)[0]:
     except Exception as e:
         err = str(e)
         break
-    time.sleep(0.005)
+    time.sleep(0.0005)
 print(json.dumps({"samples": out, "err": err}), flush=True)
 """
 
@@ -193,7 +193,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm),
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons), "samples": len(sm),
                 "power_w_max": max(p for _, _, p in samples) / 1000.0,
-                "source": "NVML in a child process, ~5 ms polling during the timed region"}
+                "source": "NVML in a child process, ~0.5 ms polling during the timed region"}
 
 
 def dist_init():
@@ -842,7 +842,8 @@ def run_ours(args, wl):
     import ratchet_b200 as rb  # noqa: F401  (fails loudly without the native library)
 
     sub = shard(wl, ws, rank)
-    strong = sub["split"] not in ("none", "replica")
+    # dense and decode split one problem over the ranks (at every N, 1 included)
+    strong = wl["name"] in ("dense", "decode")
     # replicas draw their own data; a split workload draws the same problem on every rank
     seed0 = 0 if strong else 1000 * rank
     per_set = set_bytes(sub)
