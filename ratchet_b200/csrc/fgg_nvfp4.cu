@@ -15,7 +15,6 @@
 
 #include "fgg_engine.cuh"
 #include "fgg_host.cuh"
-#include "fgg_macro.cuh"
 
 namespace fgg {
 
@@ -33,8 +32,6 @@ struct PrepParams {
   const uint8_t* a_sf[CAP];
   int32_t m[CAP];
   int32_t xtile_begin[CAP + 1];
-  // tile units per group: token tiles, or pairs of them (macro tiles)
-  int32_t unit_begin[CAP + 1];
   int32_t tile_begin[CAP + 1];
   int32_t out_row[CAP];
   int32_t wgroup[CAP];  // weight group of each problem group
@@ -43,11 +40,10 @@ struct PrepParams {
   uint32_t* tiles_out;
   uint8_t* sfx_out;
   int* status;
-  int32_t g, k, bn, ch, nk64p, nt, num_tiles, xt_total, units_total;
+  int32_t g, k, bn, ch, nk64p, nt, num_tiles, xt_total;
   int32_t blocks_tmap, blocks_tiles;
-  int32_t across_groups;  // tile order: 1 weight-tile-major over all groups, 0 group-major
-  int32_t sf_vec;  // 1: K % 256 == 0 and every a_sf[g] 16-byte aligned (vector repack)
-  int32_t macro;   // 1: a tile unit is two consecutive token tiles (the macro kernel)
+  int32_t across_groups;
+  int32_t sf_vec;  // 1: K % 256 == 0 and every a_sf[g] 16-byte aligned (vector repack)  // tile order: 1 weight-tile-major over all groups, 0 group-major
 };
 
 // Group whose tiles (its token tiles x nt weight tiles, group-major) hold tile t.
@@ -115,34 +111,31 @@ __global__ void __launch_bounds__(256)
   }
   blk -= p.blocks_tmap;
   if (blk < p.blocks_tiles) {
-    // A tile unit is a token tile, or (macro) two consecutive token tiles of
-    // a group, named by the first: unit u of a group starts at token tile
-    // u << macro.
     if (p.across_groups) {
       // Weight-tile-major over all groups: tile t pairs weight tile
-      // t / units_total with unit t % units_total of the groups' concatenated
-      // units.  The tiles running at any moment span every group, so the
-      // groups whose weights serve one unit (read from DRAM for it alone)
-      // spread over the whole kernel instead of gathering at its end.
-      for (int i = threadIdx.x; i <= p.g; i += blockDim.x) sbegin[i] = p.unit_begin[i];
+      // t / xt_total with token tile t % xt_total of the groups' concatenated
+      // token tiles.  The tiles running at any moment span every group, so
+      // the groups whose weights serve one token tile (read from DRAM for it
+      // alone) spread over the whole kernel instead of gathering at its end.
+      for (int i = threadIdx.x; i <= p.g; i += blockDim.x) sbegin[i] = p.xtile_begin[i];
       __syncthreads();
       const int t = blk * blockDim.x + threadIdx.x;
       if (t < p.num_tiles) {
-        const int nti = t / p.units_total;
-        const int X = t - nti * p.units_total;
+        const int nti = t / p.xt_total;
+        const int X = t - nti * p.xt_total;
         const int g = find_group(sbegin, p.g, X);
-        p.tiles_out[t] = pack_tile(g, nti, (X - sbegin[g]) << p.macro);
+        p.tiles_out[t] = pack_tile(g, nti, X - sbegin[g]);
       }
     } else {
-      // group-major: each group's weight tiles in turn, its units fastest
+      // group-major: each group's weight tiles in turn, its token tiles fastest
       for (int i = threadIdx.x; i <= p.g; i += blockDim.x) sbegin[i] = p.tile_begin[i];
       __syncthreads();
       const int t = blk * blockDim.x + threadIdx.x;
       if (t < p.num_tiles) {
         const int g = find_group(sbegin, p.g, t);
         const int local = t - sbegin[g];
-        const int us = p.unit_begin[g + 1] - p.unit_begin[g];
-        p.tiles_out[t] = pack_tile(g, local / us, (local % us) << p.macro);
+        const int xts = p.xtile_begin[g + 1] - p.xtile_begin[g];
+        p.tiles_out[t] = pack_tile(g, local / xts, local % xts);
       }
     }
     return;
@@ -232,14 +225,11 @@ struct RowsPrepParams {
   int32_t blocks_tiles;
   int32_t sf_vec;     // K % 256 == 0 and a_sf 16-byte aligned
   int32_t decode;     // decode tiles: never the across-groups order
-  int32_t macro;      // 1: a tile unit is two consecutive token tiles
 };
 
-// Shared-memory prefixes per group: begin[g] of the token tiles and
-// ubegin[g] of the tile units (token tiles, or pairs of them), g <= G.
-// Returns the token-tile total, or -1 when the offsets are malformed.
-__device__ int rows_tile_prefix(const RowsPrepParams& p, int32_t* begin, int32_t* ubegin,
-                                int32_t* off) {
+// Shared-memory prefix of the token tiles per group: begin[g] for g <= G.
+// Returns the total, or -1 when the offsets are malformed.
+__device__ int rows_tile_prefix(const RowsPrepParams& p, int32_t* begin, int32_t* off) {
   __shared__ int s_bad;
   __shared__ int32_t s_warp[8];
   if (threadIdx.x == 0) s_bad = 0;
@@ -248,20 +238,13 @@ __device__ int rows_tile_prefix(const RowsPrepParams& p, int32_t* begin, int32_t
   // each thread sums the tiles of a contiguous run of groups
   const int per = (p.g + blockDim.x - 1) / blockDim.x;
   const int g0 = threadIdx.x * per, g1 = min(p.g, g0 + per);
-  auto tiles_of = [&](int g) {
-    const int m = off[g + 1] - off[g];
-    return m > 0 ? (m + p.bn - 1) / p.bn : 0;
-  };
-  // both runs packed in one word: token tiles (low 16 bits), units (high)
   int run = 0;
   for (int g = g0; g < g1; ++g) {
     const int m = off[g + 1] - off[g];
     if (m < 0 || off[g] < 0 || off[g + 1] > p.max_rows) s_bad = 1;
-    const int xt = tiles_of(g);
-    run += xt + (((xt + p.macro) >> p.macro) << 16);
+    run += m > 0 ? (m + p.bn - 1) / p.bn : 0;
   }
-  // block-wide exclusive scan of the runs (both totals stay below 2^15: the
-  // host caps the token tiles of a call)
+  // block-wide exclusive scan of the runs
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int incl = run;
 #pragma unroll
@@ -275,15 +258,11 @@ __device__ int rows_tile_prefix(const RowsPrepParams& p, int32_t* begin, int32_t
   for (int w = 0; w < warp; ++w) wbase += s_warp[w];
   int acc = wbase + incl - run;
   for (int g = g0; g < g1; ++g) {
-    begin[g] = acc & 0xFFFF;
-    ubegin[g] = acc >> 16;
-    const int xt = tiles_of(g);
-    acc += xt + (((xt + p.macro) >> p.macro) << 16);
+    begin[g] = acc;
+    const int m = off[g + 1] - off[g];
+    acc += m > 0 ? (m + p.bn - 1) / p.bn : 0;
   }
-  if (threadIdx.x == blockDim.x - 1) {
-    begin[p.g] = (wbase + incl) & 0xFFFF;
-    ubegin[p.g] = (wbase + incl) >> 16;
-  }
+  if (threadIdx.x == blockDim.x - 1) begin[p.g] = wbase + incl;
   __syncthreads();
   if (s_bad) return -1;
   return begin[p.g];
@@ -294,12 +273,10 @@ __global__ void __launch_bounds__(256)
   griddep_launch_dependents();
   griddep_wait();
   __shared__ int32_t sbegin[FGG_MAX_GROUPS + 1];
-  __shared__ int32_t subegin[FGG_MAX_GROUPS + 1];
   __shared__ int32_t soff[FGG_MAX_GROUPS + 1];
-  const int xt_total = rows_tile_prefix(p, sbegin, subegin, soff);
+  const int xt_total = rows_tile_prefix(p, sbegin, soff);
   const bool bad = xt_total < 0 || xt_total > p.xt_cap;
-  const int units_total = bad ? 0 : subegin[p.g];
-  const int num_tiles = bad ? 0 : units_total * p.nt;
+  const int num_tiles = bad ? 0 : xt_total * p.nt;
   int blk = blockIdx.x;
   if (blk == 0) {
     if (threadIdx.x == 0) {
@@ -327,16 +304,17 @@ __global__ void __launch_bounds__(256)
     const bool across = !p.decode && p.g > 1 &&
                         int64_t(soff[p.g]) * (p.k / 2 + p.k / 16) <= kAcrossGroupsMaxBytes;
     if (across) {
-      const int nti = t / units_total;
-      const int X = t - nti * units_total;
-      const int g = find_group(subegin, p.g, X);
-      p.tiles_out[t] = pack_tile(g, nti, (X - subegin[g]) << p.macro);
+      const int nti = t / xt_total;
+      const int X = t - nti * xt_total;
+      const int g = find_group(sbegin, p.g, X);
+      p.tiles_out[t] = pack_tile(g, nti, X - sbegin[g]);
     } else {
-      // group-major: a group's tiles are its units x NT weight tiles
-      const int g = find_group_tiles(subegin, p.g, t, p.nt);
-      const int local = t - subegin[g] * p.nt;
-      const int us = subegin[g + 1] - subegin[g];
-      p.tiles_out[t] = pack_tile(g, local / us, (local % us) << p.macro);
+      // group-major: a group's tiles are its token tiles x NT weight tiles
+      const int X0 = find_group_tiles(sbegin, p.g, t, p.nt);
+      const int g = X0;
+      const int local = t - sbegin[g] * p.nt;
+      const int xts = sbegin[g + 1] - sbegin[g];
+      p.tiles_out[t] = pack_tile(g, local / xts, local % xts);
     }
     return;
   }
@@ -459,19 +437,6 @@ __global__ void __launch_bounds__(256) nvfp4_pack_weights_kernel(const __grid_co
 using CfgPrefill = EngineCfg<false, 224, 4>;   // one CTA per tile (N % 256 != 0)
 using CfgDecode = EngineCfg<false, 16, 4, 2>;  // every group has M <= 16; 2 K steps per stage
 using CfgPair = PairCfg<false, 6>;             // CTA pairs, 256 x 224 tiles
-using CfgMacro = MacroCfg<false, 4>;           // CTA pairs, 256 x (224 + 224) macro tiles
-
-// The CTA-pair shapes run as macro tiles (two token tiles per weight tile,
-// fgg_macro.cuh); 0 selects the one-token-tile pair kernel instead.
-#ifndef FGG_PAIR_MACRO
-#define FGG_PAIR_MACRO 1
-#endif
-constexpr bool kPairMacro = FGG_PAIR_MACRO != 0;
-static_assert(CfgMacro::SFW_ROW_U64 == CfgPair::SFW_ROW_U64 &&
-                  CfgMacro::SFW_BOX_ROWS == CfgPair::SFW_BOX_ROWS &&
-                  CfgMacro::SFX_ROW_U64 == CfgPair::SFX_ROW_U64 &&
-                  CfgMacro::SFX_BOX_ROWS == CfgPair::SFX_BOX_ROWS,
-              "both pair kernels read the same scale-atom boxes");
 
 struct PackLayout {
   size_t header, tmaps, sfw, total;
@@ -493,11 +458,9 @@ struct WsLayout {
   bool pair = false;
   int box_rows = 0;  // token rows per TMA box (a pair CTA loads half a tile)
   int nk64p = 0, nk256 = 0, nt = 0, nt128 = 0;
-  int num_tiles = 0, xt_total = 0, units_total = 0;
-  bool macro = false;  // pair tiles as macro tiles (two token tiles per unit)
+  int num_tiles = 0, xt_total = 0;
   // per-group bookkeeping in fixed arrays: planning a call touches no host heap
   int32_t xtile_begin[FGG_MAX_GROUPS + 1];
-  int32_t unit_begin[FGG_MAX_GROUPS + 1];
   int32_t tile_begin[FGG_MAX_GROUPS + 1];
   int32_t out_row[FGG_MAX_GROUPS];
   int wg = 0;  // weight groups the problem groups index into
@@ -550,25 +513,19 @@ static int plan(const FggNvfp4Problem* p, WsLayout* L) {
   L->nk64p = 4 * L->nk256;
   L->nt128 = p->n / 128;
   L->nt = L->pair ? p->n / 256 : L->nt128;
-  L->macro = L->pair && kPairMacro;
-  int64_t rows = 0, xts = 0, units = 0, tiles = 0;
+  int64_t rows = 0, xts = 0, tiles = 0;
   for (int g = 0; g < G; ++g) {
     L->out_row[g] = int32_t(rows);
     L->xtile_begin[g] = int32_t(xts);
-    L->unit_begin[g] = int32_t(units);
     L->tile_begin[g] = int32_t(tiles);
     const int64_t xt = (p->m[g] + L->bn - 1) / L->bn;
     if (xt > 2047) return set_error(FGG_EBADSHAPE, "m[%d]=%d too large", g, p->m[g]);
-    const int64_t u = L->macro ? (xt + 1) / 2 : xt;
     rows += p->m[g];
     xts += xt;
-    units += u;
-    tiles += u * L->nt;
+    tiles += xt * L->nt;
   }
   if (rows > INT32_MAX || tiles > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
   L->xtile_begin[G] = int32_t(xts);
-  L->unit_begin[G] = int32_t(units);
-  L->units_total = int(units);
   L->across_groups = !decode && G > 1 &&
                      rows * (p->k / 2 + p->k / 16) <= int64_t(kAcrossGroupsMaxBytes);
   L->tile_begin[G] = int32_t(tiles);
@@ -699,11 +656,8 @@ int prepare_launch(const FggNvfp4Problem* p, const WsLayout& L, int first, uint8
   }
   for (int g = 0; g <= G; ++g) {
     pp.xtile_begin[g] = L.xtile_begin[g];
-    pp.unit_begin[g] = L.unit_begin[g];
     pp.tile_begin[g] = L.tile_begin[g];
   }
-  pp.units_total = L.units_total;
-  pp.macro = L.macro ? 1 : 0;
   pp.tmap_out = reinterpret_cast<CUtensorMap*>(ws + L.tmaps);
   pp.ginfo_out = reinterpret_cast<GroupInfo*>(ws + L.ginfo);
   pp.tiles_out = reinterpret_cast<uint32_t*>(ws + L.tiles);
@@ -788,8 +742,7 @@ int gemm_impl(const FggNvfp4Problem* p, const WsLayout& L, const void* pack, uin
                                  uint64_t(L.xt_total) * L.nk256 * CfgPair::SFX_BOX_ROWS,
                                  CfgPair::SFX_ROW_U64, CfgPair::SFX_BOX_ROWS))
       return rc;
-    e = L.macro ? launch_macro<CfgMacro>(gp, dev.sm_count, s)
-                : launch_pair<CfgPair>(gp, dev.sm_count, s);
+    e = launch_pair<CfgPair>(gp, dev.sm_count, s);
   } else if (L.bn == CfgDecode::BN) {
     e = launch_engine<CfgDecode>(gp, dev.sm_count, s);
   } else {
@@ -866,7 +819,7 @@ namespace {
 
 struct RowsLayout {
   int bn = 0, ch = 0, nk64p = 0, nk256 = 0, nt = 0, nt128 = 0, xt_cap = 0, tile_cap = 0;
-  bool pair = false, decode = false, macro = false;
+  bool pair = false, decode = false;
   int box_rows = 0;
   size_t status = 0, ginfo = 0, tiles = 0, sfx = 0, total = 0;
 };
@@ -896,13 +849,10 @@ int plan_rows(const FggNvfp4RowsProblem* p, RowsLayout* L) {
   L->nk64p = 4 * L->nk256;
   L->nt128 = p->n / 128;
   L->nt = L->pair ? p->n / 256 : L->nt128;
-  L->macro = L->pair && kPairMacro;
-  // token tiles: sum_g ceil(M_g / BN) <= max_rows / BN + G; the device-side
-  // prefix packs token tiles and units into 16-bit halves
+  // token tiles: sum_g ceil(M_g / BN) <= max_rows / BN + G
   const int64_t xt_cap = (int64_t(p->max_rows) + L->bn - 1) / L->bn + G;
   const int64_t tile_cap = xt_cap * L->nt;
-  if (xt_cap >= (1 << 15) || tile_cap > INT32_MAX)
-    return set_error(FGG_EBADSHAPE, "max_rows=%d gives more than 32767 token tiles", p->max_rows);
+  if (xt_cap > INT32_MAX / 2 || tile_cap > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
   if (int64_t(maxg + L->bn - 1) / L->bn > 2047)
     return set_error(FGG_EBADSHAPE, "groups of up to %d rows are too large", maxg);
   L->xt_cap = int(xt_cap);
@@ -978,7 +928,6 @@ int fgg_nvfp4_grouped_gemm_rows(const FggNvfp4RowsProblem* p, const void* pack, 
   pp.blocks_tiles = (L.tile_cap + 255) / 256;
   pp.sf_vec = (p->k % 256 == 0 && aligned16(p->a_sf)) ? 1 : 0;
   pp.decode = L.decode ? 1 : 0;
-  pp.macro = L.macro ? 1 : 0;
   const int64_t sf_lines = int64_t(L.xt_cap) * L.nk64p * L.ch * 32 / (pp.sf_vec ? 4 : 1);
   const int64_t blocks = 1 + int64_t(pp.blocks_tiles) + (sf_lines + 255) / 256;
   if (blocks > INT32_MAX) return set_error(FGG_EBADSHAPE, "problem too large");
@@ -1024,8 +973,7 @@ int fgg_nvfp4_grouped_gemm_rows(const FggNvfp4RowsProblem* p, const void* pack, 
                                  uint64_t(L.xt_cap) * L.nk256 * CfgPair::SFX_BOX_ROWS,
                                  CfgPair::SFX_ROW_U64, CfgPair::SFX_BOX_ROWS))
       return rc;
-    e = L.macro ? launch_macro<CfgMacro>(gp, dev.sm_count, s)
-                : launch_pair<CfgPair>(gp, dev.sm_count, s);
+    e = launch_pair<CfgPair>(gp, dev.sm_count, s);
   } else if (L.decode) {
     e = launch_engine<CfgDecode>(gp, dev.sm_count, s);
   } else {

@@ -82,9 +82,7 @@ def _ws_bytes_py(ms, n, k):
     nk64p = 4 * nk256
     xts = sum((m + bn - 1) // bn for m in ms)
     pair = bn == 224 and n % 256 == 0   # CTA pairs cover 256 weight rows per tile
-    # pair tiles are macro tiles: two consecutive token tiles of a group per tile
-    units = sum(((m + bn - 1) // bn + 1) // 2 for m in ms) if pair else xts
-    tiles = units * (n // (256 if pair else 128))
+    tiles = xts * (n // (256 if pair else 128))
     off = 0
     def take(nbytes, align):
         nonlocal off
