@@ -980,7 +980,8 @@ def run_moe(args, wl):
     d = moe_setup(wl, ws, rank, dev)
     tl, ids_all, mine = d["tl"], d["ids_all"], d["mine"]
     xc, xs, xg, ids, wts = d["xc"], d["xs"], d["xg"], d["ids"], d["wts"]
-    layer = moe.ExpertParallelMoE(d["wc"], d["wsf"], d["wg"], d["owner"], d["slot"], max_tokens=tl)
+    layer = moe.ExpertParallelMoE(d["wc"], d["wsf"], d["wg"], d["owner"], d["slot"], max_tokens=tl,
+                                  combine=args.combine)
     torch.cuda.synchronize()
     fl = 2.0 * T * topk * n * k
 
@@ -1088,7 +1089,9 @@ def run_moe(args, wl):
                        "placement": "LPT on expected expert load, equal expert counts",
                        "dispatch": "NCCL all-gather of token records (capacity = tokens per rank)"
                                    if ws > 1 else "none (one rank)",
-                       "combine": "NCCL all-to-all of router-weighted partial rows, fp32 sum"
+                       "combine": ("NCCL reduce-scatter of router-weighted partial rows"
+                                   if args.combine == "reduce_scatter" else
+                                   "NCCL all-to-all of router-weighted partial rows, fp32 sum")
                                   if ws > 1 else "router-weighted sum on the rank",
                        "l2": f"expert weights {E * n * k * 0.5625 / ws / 1e6:.0f} MB per rank "
                              "read every step"},
@@ -1215,6 +1218,8 @@ def main():
                     default="moe")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--combine", choices=["a2a", "reduce_scatter"], default="a2a",
+                    help="the MoE layer's combine collective (--config moe)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = workload(args.config)

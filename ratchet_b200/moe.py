@@ -128,12 +128,16 @@ class ExpertParallelMoE:
     max_tokens: the dispatch capacity, the most tokens any rank passes to one
     forward (every rank must use the same value); default: the first
     forward's token count.  topk: routes per token (default: the first
-    forward's).
+    forward's).  combine: "a2a" returns the partial rows with an equal-split
+    all-to-all and sums them in fp32 on the token's rank; "reduce_scatter"
+    lets NCCL sum them on the way (bf16 additions, one rounding per step of
+    its reduction).
     """
 
     def __init__(self, w_codes: Sequence[torch.Tensor], w_sf: Sequence[torch.Tensor],
                  w_scale: Sequence, owner: np.ndarray, slot: np.ndarray, group=None,
-                 gemm_fn: GemmFn | None = None, max_tokens: int | None = None):
+                 gemm_fn: GemmFn | None = None, max_tokens: int | None = None,
+                 combine: str = "a2a"):
         import torch.distributed as dist
 
         self.group = group
@@ -161,6 +165,9 @@ class ExpertParallelMoE:
         self.owner_np, self.slot_np = owner, slot
         self.gemm_fn = gemm_fn
         self.max_tokens = max_tokens
+        if combine not in ("a2a", "reduce_scatter"):
+            raise ValueError(f"combine={combine!r}: 'a2a' or 'reduce_scatter'")
+        self.combine = combine
         self.topk = None
         self.bufs = None
         self.pack = None
@@ -306,6 +313,14 @@ class ExpertParallelMoE:
         _lib.check(L.fgg_moe_reduce(b["y"].data_ptr(), b["R"], b["route_row"].data_ptr(), toks, n,
                                     target.data_ptr(), self.bad.data_ptr(), stream), "fgg_moe_reduce")
         mark("combine")
+        if W > 1 and self.combine == "reduce_scatter":
+            import torch.distributed as dist
+
+            summed = torch.empty((C, n), dtype=torch.bfloat16, device=dev)
+            dist.reduce_scatter_tensor(summed, b["partial"], group=self.group)
+            mark("sum")
+            mark("end")
+            return summed[:T]
         if W > 1:
             self._a2a(b["recv"], b["partial"])
         mark("sum")

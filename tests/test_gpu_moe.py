@@ -185,8 +185,11 @@ def _nccl_worker(rank, world, port, result_dir):
         owner, slot = moe.place_experts(moe.expert_popularity(E, seed=2), world)
         layer = _layer(w_all, owner, slot, rank, dev, max_tokens=300)
         ok, st = _check(layer, rank, 200 + 57 * rank, dev, w_all)
+        # the same forward with the partial rows summed by NCCL's reduce-scatter
+        layer.combine = "reduce_scatter"
+        ok2, st2 = _check(layer, rank, 200 + 57 * rank, dev, w_all)
         with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
-            f.write(f"{int(ok)} {st}\n")
+            f.write(f"{int(ok and ok2)} {st} {st2}\n")
     finally:
         dist.destroy_process_group()
 
