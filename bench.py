@@ -981,7 +981,7 @@ def run_moe(args, wl):
     tl, ids_all, mine = d["tl"], d["ids_all"], d["mine"]
     xc, xs, xg, ids, wts = d["xc"], d["xs"], d["xg"], d["ids"], d["wts"]
     layer = moe.ExpertParallelMoE(d["wc"], d["wsf"], d["wg"], d["owner"], d["slot"], max_tokens=tl,
-                                  combine=args.combine)
+                                  combine=args.combine, transport=args.transport)
     torch.cuda.synchronize()
     fl = 2.0 * T * topk * n * k
 
@@ -1075,6 +1075,21 @@ def run_moe(args, wl):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, ws, dev)
     del replay
     layer.release()
+    if args.transport == "p2p":
+        # pack+store, wait, expand (2), GEMM (2), reduce+store, wait, sum
+        launches = 9
+        dispatch_desc = ("peer stores of token records into every rank's buffer by the "
+                         "library's dispatch kernel (CUDA IPC, no multicast), bounded flag wait")
+        combine_desc = ("peer stores of router-weighted partial rows by the reduce kernel, "
+                        "bounded flag wait, fp32 sum")
+    else:
+        launches = 7 if ws > 1 else 5
+        dispatch_desc = ("NCCL all-gather of token records (capacity = tokens per rank)"
+                         if ws > 1 else "none (one rank)")
+        combine_desc = (("NCCL reduce-scatter of router-weighted partial rows"
+                         if args.combine == "reduce_scatter" else
+                         "NCCL all-to-all of router-weighted partial rows, fp32 sum")
+                        if ws > 1 else "router-weighted sum on the rank")
 
     if rank == 0:
         line = {
@@ -1087,12 +1102,8 @@ def run_moe(args, wl):
             "config": {"workload": wl["desc"], "tokens": T, "experts": E, "topk": topk,
                        "n": n, "k": k, "parallelism": f"ep{ws}",
                        "placement": "LPT on expected expert load, equal expert counts",
-                       "dispatch": "NCCL all-gather of token records (capacity = tokens per rank)"
-                                   if ws > 1 else "none (one rank)",
-                       "combine": ("NCCL reduce-scatter of router-weighted partial rows"
-                                   if args.combine == "reduce_scatter" else
-                                   "NCCL all-to-all of router-weighted partial rows, fp32 sum")
-                                  if ws > 1 else "router-weighted sum on the rank",
+                       "dispatch": dispatch_desc,
+                       "combine": combine_desc,
                        "l2": f"expert weights {E * n * k * 0.5625 / ws / 1e6:.0f} MB per rank "
                              "read every step"},
             "phases_ms": phases,
@@ -1103,7 +1114,7 @@ def run_moe(args, wl):
             "e2e": {"value": fl / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": int(h_xc.numel() + h_xs.numel()) * ws,
                     "d2h_bytes_per_step": int(h_out.numel() * 2) * ws, "ms_per_step": e2e_ms},
-            "gpu_launches": (7 if ws > 1 else 5) * args.steps,
+            "gpu_launches": launches * args.steps,
             "roofline": roof,
             "cpu_baseline": cpu_sample(wl) if (ws == 1 and not args.no_cpu) else None,
         }
@@ -1220,6 +1231,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--combine", choices=["a2a", "reduce_scatter"], default="a2a",
                     help="the MoE layer's combine collective (--config moe)")
+    ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
+                    help="the MoE layer's exchange: NCCL collectives or the library's "
+                         "peer-store kernels (--config moe)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = workload(args.config)

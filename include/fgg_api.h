@@ -312,6 +312,11 @@ typedef struct FggMoeTokens {
   const int32_t* ids;        int64_t ids_stride;      /* topk expert ids per token  */
   const float* weights;      int64_t weights_stride;  /* topk router weights; NULL = 1 */
   const float* scale;        int64_t scale_stride;    /* decode scale; stride 0 = one */
+  /* Double-buffered views (the peer exchange below): when epoch is non-NULL
+   * every pointer above is advanced by ((*epoch + 1) & 1) * parity_bytes on
+   * the device, so a view captured in a CUDA graph follows the forward's
+   * buffer half.  NULL / 0 for a plain view. */
+  const int64_t* epoch;      int64_t parity_bytes;
 } FggMoeTokens;
 
 /* Bytes of one token record: codes, scales, ids, weights, decode scale,
@@ -350,6 +355,62 @@ FGG_API int fgg_moe_reduce(const void* rows, int32_t num_rows, const int32_t* ro
  * the dispatch capacity per rank). */
 FGG_API int fgg_moe_sum_partials(const void* parts, int32_t world, int32_t per_source,
                                  int32_t tokens, int32_t n, void* out, void* stream);
+
+/* The same exchange without NCCL: kernels that store straight into the
+ * other ranks' buffers over NVLink (peer memory shared through CUDA IPC, no
+ * multicast), fused with the byte work on either side of the exchange.
+ * Arrival is signalled by epoch-tagged flags in each destination's memory,
+ * written with release semantics after the data; every wait for them is
+ * bounded (about one second), after which the waiter sets *status = 0x301
+ * and returns (its data is then incomplete).  The data buffers are double
+ * buffered on the forward's epoch parity, so one forward's stores never
+ * touch the half a slower peer still reads.  No counterpart in the reference
+ * (it has no distributed code).
+ *
+ * Buffers (every rank allocates its own with fgg_peer_alloc and maps the
+ * others' with fgg_peer_export / fgg_peer_import):
+ *   gathered  [2][world * capacity][record bytes]   dispatch destination
+ *   recv      [2][world * capacity][n] bf16          combine destination
+ *   flags     [2][8] uint64 (arrivals: [0] dispatch, [1] combine, by source)
+ * epoch (int64), counters (3 x int32) and status (int32) are this rank's own.
+ * world <= 8. */
+#define FGG_PEERS_MAX 8
+typedef struct FggMoePeers {
+  int32_t world;
+  int32_t rank;
+  int32_t capacity;          /* token slots per rank (the same on every rank) */
+  int32_t n;                 /* output columns */
+  int64_t* epoch;
+  int32_t* counters;
+  int* status;
+  void* gathered[FGG_PEERS_MAX];  /* each rank's buffer, as mapped in this process */
+  void* recv[FGG_PEERS_MAX];
+  void* flags[FGG_PEERS_MAX];
+} FggMoePeers;
+
+FGG_API int fgg_peer_alloc(size_t bytes, void** ptr);
+FGG_API int fgg_peer_free(void* ptr);
+FGG_API size_t fgg_peer_handle_bytes(void);
+FGG_API int fgg_peer_export(const void* ptr, void* handle);
+FGG_API int fgg_peer_import(const void* handle, void** ptr);
+FGG_API int fgg_peer_close(void* ptr);
+/* Dispatch: this rank's tokens (num_tokens <= capacity) become records in
+ * slots [rank * capacity, ...) of EVERY rank's gathered buffer (slots past
+ * num_tokens get expert ids -1), then the arrival flags. */
+FGG_API int fgg_moe_dispatch_peers(const FggMoeTokens* tokens, const FggMoePeers* peers,
+                                   void* stream);
+/* Wait (bounded) until every rank's arrival flag of `kind` (0 dispatch,
+ * 1 combine) carries this forward's epoch. */
+FGG_API int fgg_moe_wait_peers(const FggMoePeers* peers, int32_t kind, void* stream);
+/* fgg_moe_reduce whose output row of token slot t (of world * capacity) goes
+ * to row rank * capacity + t % capacity of rank t / capacity's recv buffer,
+ * followed by the combine arrival flags. */
+FGG_API int fgg_moe_reduce_peers(const void* rows, int32_t num_rows, const int32_t* route_row,
+                                 const FggMoeTokens* tokens, const FggMoePeers* peers, int* bad,
+                                 void* stream);
+/* out[t, :] = bf16(sum_s recv[s * capacity + t, :]) in fp32 for t < tokens,
+ * from this rank's recv half of this forward; then the epoch advances. */
+FGG_API int fgg_moe_sum_peers(const FggMoePeers* peers, int32_t tokens, void* out, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* NVFP4 quantisation (activations and weights)                              */

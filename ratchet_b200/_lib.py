@@ -58,7 +58,18 @@ class FggMoeTokens(ctypes.Structure):
                 ("sf", _VOIDP), ("sf_stride", ctypes.c_int64),
                 ("ids", _VOIDP), ("ids_stride", ctypes.c_int64),
                 ("weights", _VOIDP), ("weights_stride", ctypes.c_int64),
-                ("scale", _VOIDP), ("scale_stride", ctypes.c_int64)]
+                ("scale", _VOIDP), ("scale_stride", ctypes.c_int64),
+                ("epoch", _VOIDP), ("parity_bytes", ctypes.c_int64)]
+
+
+FGG_PEERS_MAX = 8
+
+
+class FggMoePeers(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("capacity", ctypes.c_int32),
+                ("n", ctypes.c_int32), ("epoch", _VOIDP), ("counters", _VOIDP), ("status", _VOIDP),
+                ("gathered", _VOIDP * FGG_PEERS_MAX), ("recv", _VOIDP * FGG_PEERS_MAX),
+                ("flags", _VOIDP * FGG_PEERS_MAX)]
 
 
 class FggError(RuntimeError):
@@ -98,6 +109,17 @@ _SIGS = {
                                       ctypes.c_int32, _VOIDP, _VOIDP, _VOIDP]),
     "fgg_moe_sum_partials": (ctypes.c_int, [_VOIDP, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                             ctypes.c_int32, _VOIDP, _VOIDP]),
+    "fgg_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_VOIDP)]),
+    "fgg_peer_free": (ctypes.c_int, [_VOIDP]),
+    "fgg_peer_handle_bytes": (ctypes.c_size_t, []),
+    "fgg_peer_export": (ctypes.c_int, [_VOIDP, _VOIDP]),
+    "fgg_peer_import": (ctypes.c_int, [_VOIDP, ctypes.POINTER(_VOIDP)]),
+    "fgg_peer_close": (ctypes.c_int, [_VOIDP]),
+    "fgg_moe_dispatch_peers": (ctypes.c_int, [ctypes.POINTER(FggMoeTokens), ctypes.POINTER(FggMoePeers), _VOIDP]),
+    "fgg_moe_wait_peers": (ctypes.c_int, [ctypes.POINTER(FggMoePeers), ctypes.c_int32, _VOIDP]),
+    "fgg_moe_reduce_peers": (ctypes.c_int, [_VOIDP, ctypes.c_int32, _VOIDP, ctypes.POINTER(FggMoeTokens),
+                                            ctypes.POINTER(FggMoePeers), _VOIDP, _VOIDP]),
+    "fgg_moe_sum_peers": (ctypes.c_int, [ctypes.POINTER(FggMoePeers), ctypes.c_int32, _VOIDP, _VOIDP]),
     "fgg_nvfp4_grouped_gemm_silu_mul": (ctypes.c_int, [ctypes.POINTER(FggNvfp4Problem), _VOIDP, _VOIDP, ctypes.c_size_t, _VOIDP]),
     "fgg_mx_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(FggMxProblem)]),
     "fgg_mx_grouped_gemm": (ctypes.c_int, [ctypes.POINTER(FggMxProblem), _VOIDP, ctypes.c_size_t, _VOIDP]),

@@ -23,7 +23,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "_fgg.so"
 SOURCES = ["fgg_common.cu", "fgg_nvfp4.cu", "fgg_mx.cu", "fgg_quant.cu", "fgg_scratch.cu",
-           "fgg_moe.cu"]
+           "fgg_moe.cu", "fgg_peer.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -11,6 +11,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "fgg_host.cuh"
 #include "fgg_ptx.cuh"
@@ -214,7 +215,23 @@ struct MoeTok {
   const uint8_t* scale;
   int64_t codes_stride, sf_stride, ids_stride, weights_stride, scale_stride;
   int32_t num_tokens, topk, k;
+  const int64_t* epoch;  // double-buffered view: pointers advance by the epoch parity
+  int64_t parity_bytes;
 };
+
+// The view of this forward's buffer half (a plain view is returned as it is).
+__device__ __forceinline__ MoeTok resolved(MoeTok t) {
+  if (t.epoch != nullptr) {
+    const int64_t off = ((*t.epoch + 1) & 1) * t.parity_bytes;
+    t.codes += off;
+    t.sf += off;
+    t.ids += off;
+    if (t.weights != nullptr) t.weights += off;
+    if (t.scale != nullptr) t.scale += off;
+    t.epoch = nullptr;
+  }
+  return t;
+}
 
 __device__ __forceinline__ int32_t tok_id(const MoeTok& t, int64_t i, int k) {
   return __ldg(reinterpret_cast<const int32_t*>(t.ids + i * t.ids_stride) + k);
@@ -309,6 +326,7 @@ __global__ void __launch_bounds__(256)
                             const int32_t* __restrict__ slot, int32_t num_experts, int32_t rank,
                             int32_t local, int32_t* __restrict__ counts, int* __restrict__ bad) {
   griddep_wait();
+  t = resolved(t);
   __shared__ int32_t hist[kExpandMaxLocal];
   for (int i = threadIdx.x; i < local; i += blockDim.x) hist[i] = 0;
   __syncthreads();
@@ -334,6 +352,7 @@ __global__ void __launch_bounds__(256)
                             float* __restrict__ row_scale, uint8_t* __restrict__ out_codes,
                             uint8_t* __restrict__ out_sf, int* __restrict__ bad) {
   griddep_wait();
+  t = resolved(t);
   __shared__ int32_t base[kExpandMaxLocal + 1];
   if (threadIdx.x == 0) {  // local <= 1024: a serial scan of the counts
     int run = 0;
@@ -381,45 +400,217 @@ __global__ void __launch_bounds__(256)
   griddep_launch_dependents();
 }
 
+// ---- peer exchange (see fgg_api.h): buffers mapped from the other ranks ----
+constexpr int kPeersMax = FGG_PEERS_MAX;
+constexpr int kStatusPeerTimeout = 0x301;
+
+struct PeerDev {
+  int32_t world, rank, capacity, n;
+  int64_t* epoch;
+  int32_t* counters;  // [0] dispatch, [1] combine, [2] sum: blocks done
+  int* status;
+  uint8_t* gathered[kPeersMax];
+  uint8_t* recv[kPeersMax];
+  unsigned long long* flags[kPeersMax];  // [2][kPeersMax] per rank
+  int64_t rb;                            // record bytes
+  int64_t gathered_half, recv_half;      // bytes of one buffer half
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Called by every thread of every block once its stores are issued: the last
+// block to finish raises this forward's flag of `kind` in every rank.
+__device__ __forceinline__ void signal_peers(const PeerDev& x, int kind, unsigned long long e) {
+  __threadfence_system();  // this thread's stores, to every rank, before the count
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned nblocks = gridDim.x * gridDim.y;
+    const int prev = atomicAdd(x.counters + kind, 1);
+    if (unsigned(prev) == nblocks - 1) {
+      x.counters[kind] = 0;  // the next forward's count starts from zero (stream order)
+      __threadfence_system();
+      for (int s = 0; s < x.world; ++s) st_release_sys(x.flags[s] + kind * kPeersMax + x.rank, e);
+    }
+  }
+}
+
 // Router-weighted sum of a token's local routes: out[i, :] =
 // bf16(sum_k w[i, k] * rows[route_row[i * topk + k], :]) over the routes with
 // a row (>= 0); a token with none gets a zero row.  fp32 accumulation, each
-// thread 8 consecutive columns.
+// thread 8 consecutive columns.  kPeers: token slot i's row goes to row
+// rank * capacity + i % capacity of rank i / capacity's recv buffer half,
+// and the combine flags follow.
+template <bool kPeers>
 __global__ void __launch_bounds__(256) moe_reduce_kernel(MoeTok t,
                                                          const __nv_bfloat16* __restrict__ rows,
                                                          int32_t num_rows,
                                                          const int32_t* __restrict__ route_row,
                                                          int32_t n, __nv_bfloat16* __restrict__ out,
-                                                         int* __restrict__ bad) {
+                                                         int* __restrict__ bad, PeerDev x) {
   griddep_wait();
+  t = resolved(t);
   const int64_t i = blockIdx.x;
   const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
-  if (i >= t.num_tokens || col >= n) return;
-  float acc[8];
+  if (i < t.num_tokens && col < n) {
+    float acc[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-  for (int k = 0; k < t.topk; ++k) {
-    const int r = route_row[i * t.topk + k];
-    if (r < 0) continue;
-    if (r >= num_rows) {
-      atomicExch(bad, 1);
-      continue;
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    for (int k = 0; k < t.topk; ++k) {
+      const int r = route_row[i * t.topk + k];
+      if (r < 0) continue;
+      if (r >= num_rows) {
+        atomicExch(bad, 1);
+        continue;
+      }
+      const float wk = tok_weight(t, i, k);
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(rows + int64_t(r) * n + col));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] = fmaf(wk, f.x, acc[2 * j]);
+        acc[2 * j + 1] = fmaf(wk, f.y, acc[2 * j + 1]);
+      }
     }
-    const float wk = tok_weight(t, i, k);
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(rows + int64_t(r) * n + col));
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(h[j]);
-      acc[2 * j] = fmaf(wk, f.x, acc[2 * j]);
-      acc[2 * j + 1] = fmaf(wk, f.y, acc[2 * j + 1]);
+    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    __nv_bfloat16* dst;
+    if constexpr (kPeers) {
+      const int64_t par = (*x.epoch + 1) & 1;
+      const int src = int(i / x.capacity);
+      const int64_t slot = int64_t(x.rank) * x.capacity + i % x.capacity;
+      dst = reinterpret_cast<__nv_bfloat16*>(x.recv[src] + par * x.recv_half) + slot * n + col;
+    } else {
+      dst = out + i * n + col;
+    }
+    *reinterpret_cast<uint4*>(dst) = o;
+  }
+  if constexpr (kPeers) signal_peers(x, 1, (unsigned long long)(*x.epoch + 1));
+}
+
+// Dispatch over peer memory: one warp per token slot of this rank writes the
+// slot's record into every rank's gathered buffer half (one read of the
+// token, `world` stores of each 16 bytes); slots past the rank's tokens get
+// expert ids -1 only.  The dispatch flags follow.
+template <bool kVec>
+__global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerDev x) {
+  const unsigned long long e = (unsigned long long)(*x.epoch + 1);
+  const int64_t par = int64_t(e & 1ull);
+  const int lane = threadIdx.x & 31;
+  const int kh = t.k / 2, ks = t.k / 16;
+  const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t j = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; j < x.capacity;
+       j += warps) {
+    const int64_t off = par * x.gathered_half + (int64_t(x.rank) * x.capacity + j) * x.rb;
+    int32_t* ids_at[kPeersMax];
+    for (int s = 0; s < x.world; ++s)
+      ids_at[s] = reinterpret_cast<int32_t*>(x.gathered[s] + off + kh + ks);
+    if (j < t.num_tokens) {
+      // codes then scales: 16-byte (or 4-byte) pieces, each read once
+      const uint8_t* src[2] = {t.codes + j * t.codes_stride, t.sf + j * t.sf_stride};
+      const int len[2] = {kh, ks};
+      const int at[2] = {0, kh};
+      for (int part = 0; part < 2; ++part) {
+        if (kVec) {
+          for (int q = lane; q < len[part] / 16; q += 32) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src[part]) + q);
+            for (int s = 0; s < x.world; ++s)
+              reinterpret_cast<uint4*>(x.gathered[s] + off + at[part])[q] = v;
+          }
+        } else {
+          for (int q = lane; q < len[part] / 4; q += 32) {
+            const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(src[part]) + q);
+            for (int s = 0; s < x.world; ++s)
+              reinterpret_cast<uint32_t*>(x.gathered[s] + off + at[part])[q] = v;
+          }
+        }
+      }
+      for (int k = lane; k < t.topk; k += 32) {
+        const int32_t id = tok_id(t, j, k);
+        const float w = tok_weight(t, j, k);
+        for (int s = 0; s < x.world; ++s) {
+          ids_at[s][k] = id;
+          reinterpret_cast<float*>(ids_at[s] + t.topk)[k] = w;
+        }
+      }
+      if (lane == 0) {
+        const float sc = tok_scale(t, j);
+        for (int s = 0; s < x.world; ++s) reinterpret_cast<float*>(ids_at[s] + 2 * t.topk)[0] = sc;
+      }
+    } else {
+      for (int k = lane; k < t.topk; k += 32)
+        for (int s = 0; s < x.world; ++s) ids_at[s][k] = -1;
     }
   }
-  uint4 o;
-  __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+  signal_peers(x, 0, e);
+}
+
+// Bounded wait (one thread) until every rank's flag of `kind` in this rank's
+// memory carries this forward's epoch; gives up after about one second with
+// status 0x301.
+__global__ void moe_wait_peers_kernel(PeerDev x, int kind) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long e = (unsigned long long)(*x.epoch + 1);
+  const unsigned long long* f = x.flags[x.rank] + kind * kPeersMax;
+  const uint64_t t0 = globaltimer();
+  for (int s = 0; s < x.world; ++s) {
+    while (ld_acquire_sys(f + s) < e) {
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        atomicCAS(x.status, 0, kStatusPeerTimeout);
+        return;
+      }
+    }
+  }
+}
+
+// out[i, :] = bf16(sum_s recv[s * capacity + i, :]) over this rank's half of
+// this forward; the last block to finish advances the epoch.
+__global__ void __launch_bounds__(256) moe_sum_peers_kernel(PeerDev x, int32_t tokens,
+                                                            __nv_bfloat16* __restrict__ out) {
+  griddep_wait();
+  const int64_t par = (*x.epoch + 1) & 1;
+  const __nv_bfloat16* parts =
+      reinterpret_cast<const __nv_bfloat16*>(x.recv[x.rank] + par * x.recv_half);
+  const int64_t i = blockIdx.x;
+  const int n = x.n;
+  const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (i < tokens && col < n) {
+    float acc[8];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
-  *reinterpret_cast<uint4*>(out + i * n + col) = o;
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    for (int s = 0; s < x.world; ++s) {
+      const uint4 v = *reinterpret_cast<const uint4*>(parts + (int64_t(s) * x.capacity + i) * n + col);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    *reinterpret_cast<uint4*>(out + i * n + col) = o;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned nblocks = gridDim.x * gridDim.y;
+    if (unsigned(atomicAdd(x.counters + 2, 1)) == nblocks - 1) {
+      x.counters[2] = 0;
+      *x.epoch = *x.epoch + 1;  // every block of this forward has read it
+    }
+  }
 }
 
 // out[i, :] = bf16(sum_s parts[s * per_source + i, :]) in fp32 (the partial
@@ -472,6 +663,8 @@ int to_dev(const FggMoeTokens* t, MoeTok* d) {
   d->num_tokens = t->num_tokens;
   d->topk = t->topk;
   d->k = t->k;
+  d->epoch = t->epoch;
+  d->parity_bytes = t->parity_bytes;
   if ((t->ids_stride & 3) || (t->weights_stride & 3) || (t->scale_stride & 3) ||
       !aligned4(t->ids) || !aligned4(t->weights) || !aligned4(t->scale))
     return set_error(FGG_EALIGN, "ids, weights and scale (and their strides) must be 4-byte aligned");
@@ -537,6 +730,122 @@ int fgg_moe_records_view(const void* records, int32_t num_tokens, int32_t k, int
   out->scale = reinterpret_cast<const float*>(r + kh + ks + 8 * size_t(topk));
   out->codes_stride = out->sf_stride = out->ids_stride = out->weights_stride =
       out->scale_stride = int64_t(rb);
+  out->epoch = nullptr;
+  out->parity_bytes = 0;
+  return FGG_OK;
+}
+
+}  // extern "C"
+
+namespace fgg {
+namespace {
+
+int to_peers(const FggMoePeers* p, int64_t rb, PeerDev* x) {
+  if (p == nullptr) return set_error(FGG_EINVAL, "peers is null");
+  if (p->world < 1 || p->world > kPeersMax || p->rank < 0 || p->rank >= p->world ||
+      p->capacity < 1 || p->n <= 0 || p->n % 8 != 0)
+    return set_error(FGG_EBADSHAPE, "need 1 <= world <= %d, 0 <= rank < world, capacity >= 1, "
+                                    "n a positive multiple of 8", kPeersMax);
+  if (p->epoch == nullptr || p->counters == nullptr || p->status == nullptr)
+    return set_error(FGG_EINVAL, "epoch / counters / status is null");
+  memset(x, 0, sizeof(*x));
+  x->world = p->world;
+  x->rank = p->rank;
+  x->capacity = p->capacity;
+  x->n = p->n;
+  x->epoch = p->epoch;
+  x->counters = p->counters;
+  x->status = p->status;
+  for (int s = 0; s < p->world; ++s) {
+    if (p->gathered[s] == nullptr || p->recv[s] == nullptr || p->flags[s] == nullptr)
+      return set_error(FGG_EINVAL, "rank %d's buffers are null", s);
+    if (!aligned16(p->gathered[s]) || !aligned16(p->recv[s]) ||
+        (reinterpret_cast<uintptr_t>(p->flags[s]) & 7u))
+      return set_error(FGG_EALIGN, "rank %d's buffers are misaligned", s);
+    x->gathered[s] = static_cast<uint8_t*>(p->gathered[s]);
+    x->recv[s] = static_cast<uint8_t*>(p->recv[s]);
+    x->flags[s] = static_cast<unsigned long long*>(p->flags[s]);
+  }
+  x->rb = rb;
+  x->gathered_half = int64_t(p->world) * p->capacity * rb;
+  x->recv_half = int64_t(p->world) * p->capacity * p->n * 2;
+  return FGG_OK;
+}
+
+}  // namespace
+}  // namespace fgg
+
+extern "C" {
+
+int fgg_moe_dispatch_peers(const FggMoeTokens* tokens, const FggMoePeers* peers, void* stream) {
+  MoeTok t;
+  if (int rc = to_dev(tokens, &t)) return rc;
+  if (t.epoch != nullptr) return set_error(FGG_EINVAL, "the dispatched tokens must be a plain view");
+  const size_t rb = fgg_moe_record_bytes(t.k, t.topk);
+  PeerDev x;
+  if (int rc = to_peers(peers, int64_t(rb), &x)) return rc;
+  if (t.num_tokens > x.capacity)
+    return set_error(FGG_EBADSHAPE, "%d tokens exceed the capacity %d", t.num_tokens, x.capacity);
+  if (t.num_tokens > 0 && (t.codes == nullptr || t.sf == nullptr))
+    return set_error(FGG_EINVAL, "codes / sf is null");
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  const int grid = int(std::min<int64_t>((int64_t(x.capacity) + 7) / 8, int64_t(dev.sm_count) * 4));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (rows_vec16(t) || t.num_tokens == 0)
+    moe_dispatch_peers_kernel<true><<<grid, 256, 0, s>>>(t, x);
+  else if (rows_vec4(t))
+    moe_dispatch_peers_kernel<false><<<grid, 256, 0, s>>>(t, x);
+  else
+    return set_error(FGG_EALIGN, "token rows must start on 4-byte boundaries");
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+int fgg_moe_wait_peers(const FggMoePeers* peers, int32_t kind, void* stream) {
+  PeerDev x;
+  if (int rc = to_peers(peers, 0, &x)) return rc;
+  if (kind != 0 && kind != 1) return set_error(FGG_EINVAL, "kind must be 0 (dispatch) or 1 (combine)");
+  moe_wait_peers_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, kind);
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+int fgg_moe_reduce_peers(const void* rows, int32_t num_rows, const int32_t* route_row,
+                         const FggMoeTokens* tokens, const FggMoePeers* peers, int* bad,
+                         void* stream) {
+  MoeTok t;
+  if (int rc = to_dev(tokens, &t)) return rc;
+  PeerDev x;
+  if (int rc = to_peers(peers, 0, &x)) return rc;
+  if (int64_t(t.num_tokens) != int64_t(x.world) * x.capacity)
+    return set_error(FGG_EBADSHAPE, "the tokens must be the world * capacity gathered slots");
+  if (num_rows < 0) return set_error(FGG_EINVAL, "num_rows is negative");
+  if (route_row == nullptr || bad == nullptr || (num_rows > 0 && rows == nullptr))
+    return set_error(FGG_EINVAL, "null pointer");
+  if (!aligned16(rows)) return set_error(FGG_EALIGN, "rows must be 16-byte aligned");
+  const dim3 grid(unsigned(t.num_tokens), unsigned((x.n / 8 + 255) / 256));
+  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel<true>, grid, dim3(256), 0,
+                            reinterpret_cast<cudaStream_t>(stream), t,
+                            static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, x.n,
+                            static_cast<__nv_bfloat16*>(nullptr), bad, x));
+  FGG_CUDA_CHECK(cudaGetLastError());
+  return FGG_OK;
+}
+
+int fgg_moe_sum_peers(const FggMoePeers* peers, int32_t tokens, void* out, void* stream) {
+  PeerDev x;
+  if (int rc = to_peers(peers, 0, &x)) return rc;
+  if (tokens < 0 || tokens > x.capacity)
+    return set_error(FGG_EBADSHAPE, "tokens=%d outside [0, capacity=%d]", tokens, x.capacity);
+  if (out == nullptr && tokens > 0) return set_error(FGG_EINVAL, "out is null");
+  if (tokens > 0 && !aligned16(out)) return set_error(FGG_EALIGN, "out must be 16-byte aligned");
+  // one block row even for zero tokens: its last block advances the epoch
+  const dim3 grid(unsigned(std::max(tokens, 1)), unsigned((x.n / 8 + 255) / 256));
+  FGG_CUDA_CHECK(launch_pdl(moe_sum_peers_kernel, grid, dim3(256), 0,
+                            reinterpret_cast<cudaStream_t>(stream), x, tokens,
+                            static_cast<__nv_bfloat16*>(out)));
+  FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }
 
@@ -599,10 +908,12 @@ int fgg_moe_reduce(const void* rows, int32_t num_rows, const int32_t* route_row,
   if (!aligned16(rows) || !aligned16(out))
     return set_error(FGG_EALIGN, "rows and out must be 16-byte aligned");
   const dim3 grid(unsigned(t.num_tokens), unsigned((n / 8 + 255) / 256));
-  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel, grid, dim3(256), 0,
+  PeerDev none;
+  memset(&none, 0, sizeof(none));
+  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel<false>, grid, dim3(256), 0,
                             reinterpret_cast<cudaStream_t>(stream), t,
                             static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, n,
-                            static_cast<__nv_bfloat16*>(out), bad));
+                            static_cast<__nv_bfloat16*>(out), bad, none));
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }

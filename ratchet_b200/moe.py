@@ -131,13 +131,18 @@ class ExpertParallelMoE:
     forward's).  combine: "a2a" returns the partial rows with an equal-split
     all-to-all and sums them in fp32 on the token's rank; "reduce_scatter"
     lets NCCL sum them on the way (bf16 additions, one rounding per step of
-    its reduction).
+    its reduction).  transport: "nccl" moves the records and partial rows
+    with NCCL collectives; "p2p" with the library's own kernels, which store
+    them straight into the other ranks' buffers over NVLink (peer memory
+    mapped through CUDA IPC, epoch-tagged arrival flags, bounded waits) and
+    fuse the exchange with the packing and the weighted reduce; call
+    release() before destroying the process group.
     """
 
     def __init__(self, w_codes: Sequence[torch.Tensor], w_sf: Sequence[torch.Tensor],
                  w_scale: Sequence, owner: np.ndarray, slot: np.ndarray, group=None,
                  gemm_fn: GemmFn | None = None, max_tokens: int | None = None,
-                 combine: str = "a2a"):
+                 combine: str = "a2a", transport: str = "nccl"):
         import torch.distributed as dist
 
         self.group = group
@@ -167,7 +172,14 @@ class ExpertParallelMoE:
         self.max_tokens = max_tokens
         if combine not in ("a2a", "reduce_scatter"):
             raise ValueError(f"combine={combine!r}: 'a2a' or 'reduce_scatter'")
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport={transport!r}: 'nccl' or 'p2p'")
+        if transport == "p2p" and self.world > _lib.FGG_PEERS_MAX:
+            raise ValueError(f"the peer exchange spans at most {_lib.FGG_PEERS_MAX} ranks")
         self.combine = combine
+        self.transport = transport
+        self._peer_own = []      # buffers this rank allocated (freed by release)
+        self._peer_mapped = []   # other ranks' buffers mapped here (closed by release)
         self.topk = None
         self.bufs = None
         self.pack = None
@@ -200,7 +212,9 @@ class ExpertParallelMoE:
         NT = W * C if W > 1 else C           # tokens the expand plan walks
         R = NT * min(topk, E)                # local routes at most
         b = {"NT": NT, "R": R}
-        if W > 1:
+        if self.transport == "p2p":
+            self._peer_setup(b, C, topk)
+        elif W > 1:
             rb = int(L.fgg_moe_record_bytes(self.k, topk))
             b["rb"] = rb
             b["records"] = torch.empty((C, rb), dtype=torch.uint8, device=dev)
@@ -229,6 +243,64 @@ class ExpertParallelMoE:
         b["ws"] = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         self.bufs = b
         return b
+
+    def _peer_setup(self, b: dict, C: int, topk: int) -> None:
+        """Allocate this rank's exchange buffers, map every other rank's
+        (CUDA IPC handles swapped through the process group), and describe
+        them in an FggMoePeers struct.  Collective: every rank calls it."""
+        import ctypes
+
+        import torch.distributed as dist
+
+        L = _lib.lib()
+        W, n, dev = self.world, self.n, self.device
+        rb = int(L.fgg_moe_record_bytes(self.k, topk))
+        sizes = (2 * W * C * rb, 2 * W * C * n * 2, 2 * _lib.FGG_PEERS_MAX * 8)
+        own = []
+        hb = int(L.fgg_peer_handle_bytes())
+        handles = []
+        with torch.cuda.device(dev):
+            for nbytes in sizes:
+                p = ctypes.c_void_p()
+                _lib.check(L.fgg_peer_alloc(nbytes, ctypes.byref(p)), "fgg_peer_alloc")
+                own.append(p.value)
+                self._peer_own.append(p.value)
+                h = ctypes.create_string_buffer(hb)
+                _lib.check(L.fgg_peer_export(p.value, h), "fgg_peer_export")
+                handles.append(h.raw)
+        everyone = [handles]
+        if W > 1:
+            everyone = [None] * W
+            dist.all_gather_object(everyone, handles, group=self.group)
+        ptrs = [[0] * W for _ in sizes]
+        with torch.cuda.device(dev):
+            for r in range(W):
+                for i in range(len(sizes)):
+                    if r == self.rank:
+                        ptrs[i][r] = own[i]
+                        continue
+                    q = ctypes.c_void_p()
+                    _lib.check(L.fgg_peer_import(everyone[r][i], ctypes.byref(q)), "fgg_peer_import")
+                    self._peer_mapped.append(q.value)
+                    ptrs[i][r] = q.value
+        # this rank's own state: epoch (int64), three block counters, status
+        b["pstate"] = torch.zeros(4, dtype=torch.int64, device=dev)
+        base = b["pstate"].data_ptr()
+        peers = _lib.FggMoePeers()
+        peers.world, peers.rank, peers.capacity, peers.n = W, self.rank, C, n
+        peers.epoch, peers.counters, peers.status = base, base + 8, base + 20
+        for r in range(W):
+            peers.gathered[r] = ptrs[0][r]
+            peers.recv[r] = ptrs[1][r]
+            peers.flags[r] = ptrs[2][r]
+        b["peers"] = peers
+        b["rb"] = rb
+        toks = _lib.FggMoeTokens()
+        _lib.check(L.fgg_moe_records_view(own[0], W * C, self.k, topk, toks), "fgg_moe_records_view")
+        toks.epoch, toks.parity_bytes = base, W * C * rb   # this forward's half
+        b["gathered_view"] = toks
+        if W > 1:
+            dist.barrier(group=self.group)
 
     def _tokens_view(self, x_u8, s_u8, ids32, w32, xs):
         T, topk = int(ids32.shape[0]), int(ids32.shape[1])
@@ -283,6 +355,8 @@ class ExpertParallelMoE:
         xs = torch.as_tensor(x_scale, dtype=torch.float32, device=dev).reshape(1)
         mine = self._tokens_view(x_u8, s_u8, ids32, w32, xs)
         mark("pack")
+        if self.transport == "p2p":
+            return self._forward_peers(b, mine, T, mark, stream)
         if W > 1:
             if T < C:  # slots past this rank's tokens carry no route (expert id -1)
                 b["records"][T:, kh + ks:kh + ks + 4 * topk].view(torch.int32).fill_(-1)
@@ -330,6 +404,39 @@ class ExpertParallelMoE:
         mark("end")
         return out
 
+    def _forward_peers(self, b, mine, T, mark, stream):
+        """Steps 1-6 over peer memory: the dispatch kernel stores every
+        record in every rank, the reduce kernel stores each partial row in
+        its token's rank, bounded waits on the arrival flags between."""
+        L = _lib.lib()
+        E, n, dev = self.local, self.n, self.device
+        peers, toks = b["peers"], b["gathered_view"]
+        _lib.check(L.fgg_moe_dispatch_peers(mine, peers, stream), "fgg_moe_dispatch_peers")
+        mark("dispatch")
+        _lib.check(L.fgg_moe_wait_peers(peers, 0, stream), "fgg_moe_wait_peers")
+        mark("expand")
+        _lib.check(L.fgg_moe_expand(toks, self.owner_d.data_ptr(), self.slot_d.data_ptr(),
+                                    self.num_experts, self.rank, E, b["R"], b["counts"].data_ptr(),
+                                    b["offsets"].data_ptr(), b["route_row"].data_ptr(),
+                                    b["src_token"].data_ptr(), b["row_scale"].data_ptr(),
+                                    b["a"].data_ptr(), b["a_sf"].data_ptr(), self.bad.data_ptr(),
+                                    stream), "fgg_moe_expand")
+        mark("gemm")
+        _lib.check(L.fgg_nvfp4_grouped_gemm_rows(b["prob"], self.pack.buf.data_ptr(),
+                                                 b["ws"].data_ptr(), b["ws"].numel(), stream),
+                   "fgg_nvfp4_grouped_gemm_rows")
+        ops._set_last_ws(b["ws"])
+        mark("reduce")
+        _lib.check(L.fgg_moe_reduce_peers(b["y"].data_ptr(), b["R"], b["route_row"].data_ptr(), toks,
+                                          peers, self.bad.data_ptr(), stream), "fgg_moe_reduce_peers")
+        mark("combine")
+        _lib.check(L.fgg_moe_wait_peers(peers, 1, stream), "fgg_moe_wait_peers")
+        mark("sum")
+        out = torch.empty((T, n), dtype=torch.bfloat16, device=dev)
+        _lib.check(L.fgg_moe_sum_peers(peers, T, out.data_ptr(), stream), "fgg_moe_sum_peers")
+        mark("end")
+        return out
+
     def capture(self, x_codes: torch.Tensor, x_sf: torch.Tensor, x_scale, topk_ids: torch.Tensor,
                 topk_weights: torch.Tensor | None = None, warmup: int = 2):
         """Capture forward() on these input tensors into a CUDA graph and return
@@ -357,9 +464,27 @@ class ExpertParallelMoE:
         return g.replay, out
 
     def release(self) -> None:
-        """Drop a captured graph (it holds the collectives' captured work): call
-        before destroying the process group."""
+        """Drop a captured graph (it holds the collectives' captured work) and,
+        for the peer transport, unmap the other ranks' buffers and free this
+        rank's (collective: every rank calls it).  Call before destroying the
+        process group."""
         self._graph = None
+        if not (self._peer_own or self._peer_mapped):
+            return
+        import torch.distributed as dist
+
+        L = _lib.lib()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._peer_mapped:
+                _lib.check(L.fgg_peer_close(p), "fgg_peer_close")
+            self._peer_mapped = []
+            if self.world > 1:
+                dist.barrier(group=self.group)   # nobody maps a buffer that is freed below
+            for p in self._peer_own:
+                _lib.check(L.fgg_peer_free(p), "fgg_peer_free")
+            self._peer_own = []
+        self.bufs = None
 
     # ------------------------------------------------ host emulation (tests)
     def _forward_host(self, x_u8, s_u8, x_scale, topk_ids, topk_weights):
@@ -431,6 +556,11 @@ class ExpertParallelMoE:
     def check(self) -> None:
         """Raise if a plan, expand or combine kernel met a bad expert id or
         index, or a bounded wait in the GEMM gave up (synchronises the device)."""
+        if self.bufs is not None and "pstate" in self.bufs:
+            st = int(self.bufs["pstate"][2].item() >> 32) & 0xFFFFFFFF
+            if st != 0:
+                raise _lib.FggError(_lib.FGG_ETIMEOUT, "ExpertParallelMoE",
+                                    f"a peer exchange wait gave up (status 0x{st:x})")
         if self.bad is not None:
             v = int(self.bad.item())
             if v != 0:

@@ -170,3 +170,54 @@ def test_b_index_validated_before_device(L):
     assert L.fgg_nvfp4_grouped_gemm(p, None, None, 0, None) == _lib.FGG_EINVAL
     p.num_weight_groups = 2
     assert L.fgg_nvfp4_workspace_bytes(p) > 0
+
+
+def _peers(world=2, rank=0, capacity=4, n=64, base=0x10000, flag_off=0):
+    p = _lib.FggMoePeers()
+    p.world, p.rank, p.capacity, p.n = world, rank, capacity, n
+    p.epoch, p.counters, p.status = base, base + 8, base + 20
+    for r in range(max(world, 0)):
+        if r < _lib.FGG_PEERS_MAX:
+            p.gathered[r] = base + 0x1000 * (r + 1)
+            p.recv[r] = base + 0x100000 * (r + 1)
+            p.flags[r] = base + 0x200 + 0x100 * r + flag_off
+    return p
+
+
+def test_peer_descriptions_validated_before_device(L):
+    """The peer exchange entries check the description before any device
+    call: world, rank, n, null state words, misaligned buffers, the wait kind."""
+    import ctypes
+
+    def wait(p, kind=0):
+        return L.fgg_moe_wait_peers(ctypes.byref(p), kind, None)
+
+    assert wait(_peers(), 2) == _lib.FGG_EINVAL
+    assert wait(_peers(world=0)) == _lib.FGG_EBADSHAPE
+    assert wait(_peers(world=_lib.FGG_PEERS_MAX + 1)) == _lib.FGG_EBADSHAPE
+    assert wait(_peers(rank=2)) == _lib.FGG_EBADSHAPE
+    assert wait(_peers(n=60)) == _lib.FGG_EBADSHAPE
+    assert wait(_peers(capacity=0)) == _lib.FGG_EBADSHAPE
+    p = _peers()
+    p.status = None
+    assert wait(p) == _lib.FGG_EINVAL
+    p = _peers()
+    p.recv[1] = None
+    assert wait(p) == _lib.FGG_EINVAL
+    assert wait(_peers(flag_off=4)) == _lib.FGG_EALIGN
+    p = _peers()
+    p.gathered[0] += 8
+    assert wait(p) == _lib.FGG_EALIGN
+    assert L.fgg_moe_sum_peers(ctypes.byref(_peers()), 5, None, None) == _lib.FGG_EBADSHAPE
+    assert L.fgg_moe_sum_peers(ctypes.byref(_peers()), 3, None, None) == _lib.FGG_EINVAL
+
+
+def test_peer_handles_validated(L):
+    import ctypes
+
+    assert L.fgg_peer_handle_bytes() == 64
+    assert L.fgg_peer_alloc(0, ctypes.byref(ctypes.c_void_p())) == _lib.FGG_EINVAL
+    assert L.fgg_peer_export(None, ctypes.create_string_buffer(64)) == _lib.FGG_EINVAL
+    assert L.fgg_peer_import(None, ctypes.byref(ctypes.c_void_p())) == _lib.FGG_EINVAL
+    assert L.fgg_peer_free(None) == _lib.FGG_OK
+    assert L.fgg_peer_close(None) == _lib.FGG_OK

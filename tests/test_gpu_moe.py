@@ -1,6 +1,6 @@
 """Expert-parallel MoE layer on B200 with the tcgen05 grouped GEMM, against
-the CPU oracle: world size 1 on one GPU, and two NCCL ranks when two GPUs are
-visible; and the layer's byte-moving kernels (pack, expand plan, expand rows,
+the CPU oracle: world size 1 on one GPU, and two ranks when two GPUs are
+visible, over NCCL and over the peer transport; and the layer's byte-moving kernels (pack, expand plan, expand rows,
 router-weighted reduce, partial-row sum) against plain PyTorch, bit-exact for
 the integer and byte work.  GEMM tolerance: the operator's (max|err|/max|ref|
 <= 1e-2; per element |err| <= 2e-2 |ref| + 1e-2 max|ref|)."""
@@ -40,13 +40,13 @@ def _expected(xc, xs, xg, ids, w_all, w=None):
     return acc.to(torch.bfloat16)
 
 
-def _layer(w_all, owner, slot, rank, dev, max_tokens=None):
+def _layer(w_all, owner, slot, rank, dev, max_tokens=None, transport="nccl"):
     mine = sorted(np.flatnonzero(owner == rank).tolist(), key=lambda e: slot[e])
     return moe.ExpertParallelMoE([torch.from_numpy(w_all[e][0]).to(dev) for e in mine],
                                  [torch.from_numpy(w_all[e][1]).to(dev).view(torch.float8_e4m3fn)
                                   for e in mine],
                                  [float(w_all[e][2]) for e in mine], owner, slot,
-                                 max_tokens=max_tokens)
+                                 max_tokens=max_tokens, transport=transport)
 
 
 def _check(layer, rank, T, dev, w_all):
@@ -74,6 +74,74 @@ def test_moe_world1(cuda_device):
     assert ok, st
     rb.last_status()
     layer.check()
+
+
+def _graph_matches_eager(layer, rank, T, dev, replays=3):
+    """Capture the layer's forward, replay it `replays` times (the peer
+    transport alternates its buffer halves by epoch), and compare every
+    replay with an eager forward of the same inputs, bit for bit."""
+    rng = np.random.default_rng(500 + rank)
+    xc, xs, xg = ref.nvfp4_quantize(rng.standard_normal((T, K), dtype=np.float32))
+    ids, w = moe.zipf_routing(T, E, TOPK, seed=60 + rank)
+    args = (torch.from_numpy(xc).to(dev), torch.from_numpy(xs).to(dev).view(torch.float8_e4m3fn),
+            float(xg), torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev))
+    want = layer.forward(*args).clone()
+    replay, out = layer.capture(*args)
+    same = True
+    for _ in range(replays):
+        out.zero_()
+        replay()
+        torch.cuda.synchronize(dev)
+        same = same and torch.equal(out, want)
+    layer.check()
+    return same
+
+
+def test_moe_world1_peer_transport(cuda_device):
+    """The peer transport's kernels on one GPU (the only peer is this rank):
+    dispatch into the mapped buffer, bounded waits, expand from the epoch's
+    buffer half, reduce into the return buffer, sum; eager forwards over both
+    halves, then graph replays equal to an eager forward."""
+    w_all = _weights()
+    owner, slot = moe.place_experts(moe.expert_popularity(E, seed=2), 1)
+    layer = _layer(w_all, owner, slot, 0, cuda_device, max_tokens=400, transport="p2p")
+    for _ in range(2):  # four forwards: each buffer half twice
+        ok, st = _check(layer, 0, 333, cuda_device, w_all)
+        assert ok, st
+    assert int(layer.bufs["pstate"][0].item()) == 4   # the epoch counts the forwards
+    assert _graph_matches_eager(layer, 0, 271, cuda_device)
+    layer.release()
+
+
+def test_peer_wait_gives_up_and_reports(cuda_device):
+    """A wait on a flag that nothing sets: a two-rank description whose second
+    rank's buffers are plain local memory that no kernel signals.  The wait
+    kernel gives up after its time limit with status 0x301 in the status
+    word, returns, and the device stays usable."""
+    import ctypes
+
+    from ratchet_b200 import _lib
+
+    L = _lib.lib()
+    C, n = 4, 64
+    rb = int(L.fgg_moe_record_bytes(K, TOPK))
+    gathered = [torch.zeros(2 * 2 * C * rb, dtype=torch.uint8, device=cuda_device) for _ in range(2)]
+    recv = [torch.zeros(2 * 2 * C * n, dtype=torch.bfloat16, device=cuda_device) for _ in range(2)]
+    flags = [torch.zeros(2 * _lib.FGG_PEERS_MAX, dtype=torch.int64, device=cuda_device)
+             for _ in range(2)]
+    state = torch.zeros(4, dtype=torch.int64, device=cuda_device)
+    p = _lib.FggMoePeers()
+    p.world, p.rank, p.capacity, p.n = 2, 0, C, n
+    base = state.data_ptr()
+    p.epoch, p.counters, p.status = base, base + 8, base + 20
+    for r in range(2):
+        p.gathered[r], p.recv[r], p.flags[r] = (gathered[r].data_ptr(), recv[r].data_ptr(),
+                                                flags[r].data_ptr())
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    _lib.check(L.fgg_moe_wait_peers(ctypes.byref(p), 0, stream), "fgg_moe_wait_peers")
+    torch.cuda.synchronize(cuda_device)
+    assert (int(state[2].item()) >> 32) == 0x301
+    assert float(torch.ones(8, device=cuda_device).sum().item()) == 8.0
 
 
 @pytest.mark.parametrize("kh,ks", [(3584, 448), (36, 4)])
@@ -188,8 +256,18 @@ def _nccl_worker(rank, world, port, result_dir):
         # the same forward with the partial rows summed by NCCL's reduce-scatter
         layer.combine = "reduce_scatter"
         ok2, st2 = _check(layer, rank, 200 + 57 * rank, dev, w_all)
+        # the peer transport: records and partial rows stored into the other
+        # rank's buffers by this library's kernels; each buffer half twice,
+        # then graph replays equal to an eager forward
+        peer = _layer(w_all, owner, slot, rank, dev, max_tokens=300, transport="p2p")
+        ok3, st3 = True, []
+        for _ in range(2):
+            o, s3 = _check(peer, rank, 200 + 57 * rank, dev, w_all)
+            ok3, st3 = ok3 and o, st3 + [s3]
+        ok4 = _graph_matches_eager(peer, rank, 150 + 90 * rank, dev)
+        peer.release()
         with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
-            f.write(f"{int(ok and ok2)} {st} {st2}\n")
+            f.write(f"{int(ok and ok2 and ok3 and ok4)} {st} {st2} {st3} graph={ok4}\n")
     finally:
         dist.destroy_process_group()
 
