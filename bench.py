@@ -928,7 +928,8 @@ def run_ours(args, wl):
 def moe_setup(wl, ws: int, rank: int, dev) -> dict:
     """Config 3's seeded inputs for one rank of an ws-way expert-parallel run:
     Zipf(1.1) top-8 routing of all tokens (seed 0), LPT placement of the
-    experts, this rank's experts' weights (each drawn from its own seed, so
+    experts on their expected routed load (sampled independently of the
+    batch), this rank's experts' weights (each drawn from its own seed, so
     they do not depend on ws) and this rank's share of the tokens, quantised
     to NVFP4 on the device."""
     import ratchet_b200 as rb
@@ -937,7 +938,7 @@ def moe_setup(wl, ws: int, rank: int, dev) -> dict:
     T, E, topk, n, k = wl["tokens"], wl["experts"], wl["topk"], wl["n"], wl["k"]
     tl = T // ws
     ids_all, w_all = moe.zipf_routing(T, E, topk, s=1.1, seed=0)
-    owner, slot = moe.place_experts(moe.expert_popularity(E, s=1.1, seed=0), ws)
+    owner, slot = moe.place_experts(moe.routed_load(E, topk, s=1.1, seed=0), ws)
     mine = sorted(np.flatnonzero(owner == rank).tolist(), key=lambda e: slot[e])
     wc, wsf, wg = [], [], []
     for e in mine:
@@ -1101,7 +1102,7 @@ def run_moe(args, wl):
                     "Zipf(1.1) top-8 routing)",
             "config": {"workload": wl["desc"], "tokens": T, "experts": E, "topk": topk,
                        "n": n, "k": k, "parallelism": f"ep{ws}",
-                       "placement": "LPT on expected expert load, equal expert counts",
+                       "placement": "LPT on expected routed load (top-8 inclusion probability), equal expert counts",
                        "dispatch": dispatch_desc,
                        "combine": combine_desc,
                        "l2": f"expert weights {E * n * k * 0.5625 / ws / 1e6:.0f} MB per rank "

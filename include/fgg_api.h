@@ -372,8 +372,11 @@ FGG_API int fgg_moe_sum_partials(const void* parts, int32_t world, int32_t per_s
  *   gathered  [2][world * capacity][record bytes]   dispatch destination
  *   recv      [2][world * capacity][n] bf16          combine destination
  *   flags     [2][8] uint64 (arrivals: [0] dispatch, [1] combine, by source)
- * epoch (int64), counters (3 x int32) and status (int32) are this rank's own.
- * world <= 8. */
+ * epoch (int64), counters (3 x int32), status (int32) and routes
+ * ([capacity] int32) are this rank's own.  A token's record and partial row
+ * travel only between its rank and the ranks that own one of its experts
+ * (owner[e] of num_experts): routes[t] keeps that set of ranks, as a bit
+ * mask, from the dispatch to the sum.  world <= 8. */
 #define FGG_PEERS_MAX 8
 typedef struct FggMoePeers {
   int32_t world;
@@ -386,6 +389,9 @@ typedef struct FggMoePeers {
   void* gathered[FGG_PEERS_MAX];  /* each rank's buffer, as mapped in this process */
   void* recv[FGG_PEERS_MAX];
   void* flags[FGG_PEERS_MAX];
+  const int32_t* owner;      /* [num_experts] rank of each expert (device) */
+  int32_t num_experts;
+  int32_t* routes;           /* [capacity] destination ranks of each token, bit mask */
 } FggMoePeers;
 
 FGG_API int fgg_peer_alloc(size_t bytes, void** ptr);
@@ -395,8 +401,10 @@ FGG_API int fgg_peer_export(const void* ptr, void* handle);
 FGG_API int fgg_peer_import(const void* handle, void** ptr);
 FGG_API int fgg_peer_close(void* ptr);
 /* Dispatch: this rank's tokens (num_tokens <= capacity) become records in
- * slots [rank * capacity, ...) of EVERY rank's gathered buffer (slots past
- * num_tokens get expert ids -1), then the arrival flags. */
+ * slots [rank * capacity, ...) of the gathered buffer of every rank that owns
+ * one of the token's experts; the other ranks' slots get expert ids -1 only,
+ * as do slots past num_tokens.  routes[t] = those ranks; then the arrival
+ * flags. */
 FGG_API int fgg_moe_dispatch_peers(const FggMoeTokens* tokens, const FggMoePeers* peers,
                                    void* stream);
 /* Wait (bounded) until every rank's arrival flag of `kind` (0 dispatch,
@@ -404,12 +412,14 @@ FGG_API int fgg_moe_dispatch_peers(const FggMoeTokens* tokens, const FggMoePeers
 FGG_API int fgg_moe_wait_peers(const FggMoePeers* peers, int32_t kind, void* stream);
 /* fgg_moe_reduce whose output row of token slot t (of world * capacity) goes
  * to row rank * capacity + t % capacity of rank t / capacity's recv buffer,
- * followed by the combine arrival flags. */
+ * for the tokens with a route on this rank only, followed by the combine
+ * arrival flags. */
 FGG_API int fgg_moe_reduce_peers(const void* rows, int32_t num_rows, const int32_t* route_row,
                                  const FggMoeTokens* tokens, const FggMoePeers* peers, int* bad,
                                  void* stream);
-/* out[t, :] = bf16(sum_s recv[s * capacity + t, :]) in fp32 for t < tokens,
- * from this rank's recv half of this forward; then the epoch advances. */
+/* out[t, :] = bf16(sum_s recv[s * capacity + t, :]) in fp32 for t < tokens
+ * over the ranks s in routes[t], from this rank's recv half of this forward
+ * (zeros for a token with no route); then the epoch advances. */
 FGG_API int fgg_moe_sum_peers(const FggMoePeers* peers, int32_t tokens, void* out, void* stream);
 
 /* ------------------------------------------------------------------------ */

@@ -69,7 +69,8 @@ class FggMoePeers(ctypes.Structure):
     _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("capacity", ctypes.c_int32),
                 ("n", ctypes.c_int32), ("epoch", _VOIDP), ("counters", _VOIDP), ("status", _VOIDP),
                 ("gathered", _VOIDP * FGG_PEERS_MAX), ("recv", _VOIDP * FGG_PEERS_MAX),
-                ("flags", _VOIDP * FGG_PEERS_MAX)]
+                ("flags", _VOIDP * FGG_PEERS_MAX), ("owner", _VOIDP),
+                ("num_experts", ctypes.c_int32), ("routes", _VOIDP)]
 
 
 class FggError(RuntimeError):

@@ -412,6 +412,9 @@ struct PeerDev {
   uint8_t* gathered[kPeersMax];
   uint8_t* recv[kPeersMax];
   unsigned long long* flags[kPeersMax];  // [2][kPeersMax] per rank
+  const int32_t* owner;                  // [num_experts] rank of each expert
+  int32_t num_experts;
+  int32_t* routes;                       // [capacity] destination ranks per token slot
   int64_t rb;                            // record bytes
   int64_t gathered_half, recv_half;      // bytes of one buffer half
 };
@@ -443,12 +446,16 @@ __device__ __forceinline__ void signal_peers(const PeerDev& x, int kind, unsigne
 
 // Router-weighted sum of a token's local routes: out[i, :] =
 // bf16(sum_k w[i, k] * rows[route_row[i * topk + k], :]) over the routes with
-// a row (>= 0); a token with none gets a zero row.  fp32 accumulation, each
-// thread 8 consecutive columns.  kPeers: token slot i's row goes to row
+// a row (>= 0); a token with none gets a zero row.  fp32 accumulation in
+// route order; a thread takes 8 consecutive columns of one token per item
+// and strides over the items (a grid of a few blocks per SM, so that the
+// peer variant's fence before its signal is paid once per thread, not once
+// per token).  kPeers: token slot i's row goes to row
 // rank * capacity + i % capacity of rank i / capacity's recv buffer half,
-// and the combine flags follow.
+// only for a token with a route here (the sum on the token's rank skips the
+// others), and the combine flags follow.
 template <bool kPeers>
-__global__ void __launch_bounds__(256) moe_reduce_kernel(MoeTok t,
+__global__ void __launch_bounds__(256, 4) moe_reduce_kernel(MoeTok t,
                                                          const __nv_bfloat16* __restrict__ rows,
                                                          int32_t num_rows,
                                                          const int32_t* __restrict__ route_row,
@@ -456,19 +463,26 @@ __global__ void __launch_bounds__(256) moe_reduce_kernel(MoeTok t,
                                                          int* __restrict__ bad, PeerDev x) {
   griddep_wait();
   t = resolved(t);
-  const int64_t i = blockIdx.x;
-  const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
-  if (i < t.num_tokens && col < n) {
+  const int chunks = n / 8;
+  const int64_t items = int64_t(t.num_tokens) * chunks;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  int64_t par = 0;
+  if constexpr (kPeers) par = (*x.epoch + 1) & 1;
+  for (int64_t it = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; it < items; it += stride) {
+    const int64_t i = it / chunks;
+    const int col = int(it - i * chunks) * 8;
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    bool any = false;
     for (int k = 0; k < t.topk; ++k) {
-      const int r = route_row[i * t.topk + k];
+      const int r = __ldg(route_row + i * t.topk + k);
       if (r < 0) continue;
       if (r >= num_rows) {
         atomicExch(bad, 1);
         continue;
       }
+      any = true;
       const float wk = tok_weight(t, i, k);
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(rows + int64_t(r) * n + col));
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
@@ -483,24 +497,31 @@ __global__ void __launch_bounds__(256) moe_reduce_kernel(MoeTok t,
     __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
     for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
-    __nv_bfloat16* dst;
     if constexpr (kPeers) {
-      const int64_t par = (*x.epoch + 1) & 1;
-      const int src = int(i / x.capacity);
-      const int64_t slot = int64_t(x.rank) * x.capacity + i % x.capacity;
-      dst = reinterpret_cast<__nv_bfloat16*>(x.recv[src] + par * x.recv_half) + slot * n + col;
+      if (any) {
+        const int src = int(i / x.capacity);
+        const int64_t slot = int64_t(x.rank) * x.capacity + i % x.capacity;
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(x.recv[src] + par * x.recv_half) +
+                                  slot * n + col) = o;
+      }
     } else {
-      dst = out + i * n + col;
+      *reinterpret_cast<uint4*>(out + i * n + col) = o;
     }
-    *reinterpret_cast<uint4*>(dst) = o;
   }
   if constexpr (kPeers) signal_peers(x, 1, (unsigned long long)(*x.epoch + 1));
 }
 
-// Dispatch over peer memory: one warp per token slot of this rank writes the
-// slot's record into every rank's gathered buffer half (one read of the
-// token, `world` stores of each 16 bytes); slots past the rank's tokens get
-// expert ids -1 only.  The dispatch flags follow.
+// Dispatch over peer memory: one warp per token slot of this rank.  The
+// warp finds the ranks that own one of the token's experts (routes[j], a bit
+// mask) and writes the slot's record into those ranks' gathered buffer
+// halves; every other rank's slot gets expert ids -1 only, as do slots past
+// the rank's tokens.  The codes and scales are contiguous in a record, so
+// 16-byte piece q of the record comes from the codes (q < K/32) or the
+// scales; a lane loads up to kDispatchBatch pieces before it stores any, so
+// that many stores are in flight per warp (one read of the token, one store
+// of each piece per destination).  The dispatch flags follow.
+constexpr int kDispatchBatch = 8;
+
 template <bool kVec>
 __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerDev x) {
   const unsigned long long e = (unsigned long long)(*x.epoch + 1);
@@ -509,28 +530,63 @@ __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerD
   const int kh = t.k / 2, ks = t.k / 16;
   const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   for (int64_t j = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; j < x.capacity;
-       j += warps) {
+       j += warps) {  // warp-uniform
     const int64_t off = par * x.gathered_half + (int64_t(x.rank) * x.capacity + j) * x.rb;
-    int32_t* ids_at[kPeersMax];
-    for (int s = 0; s < x.world; ++s)
-      ids_at[s] = reinterpret_cast<int32_t*>(x.gathered[s] + off + kh + ks);
+    unsigned bit = 0;
     if (j < t.num_tokens) {
-      // codes then scales: 16-byte (or 4-byte) pieces, each read once
-      const uint8_t* src[2] = {t.codes + j * t.codes_stride, t.sf + j * t.sf_stride};
-      const int len[2] = {kh, ks};
-      const int at[2] = {0, kh};
-      for (int part = 0; part < 2; ++part) {
-        if (kVec) {
-          for (int q = lane; q < len[part] / 16; q += 32) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src[part]) + q);
-            for (int s = 0; s < x.world; ++s)
-              reinterpret_cast<uint4*>(x.gathered[s] + off + at[part])[q] = v;
+      for (int k = lane; k < t.topk; k += 32) {
+        const int32_t id = tok_id(t, j, k);
+        if (id >= 0 && id < x.num_experts) {
+          const int o = __ldg(x.owner + id);
+          if (o >= 0 && o < x.world) bit |= 1u << o;
+        }
+      }
+    }
+    const unsigned mask = __reduce_or_sync(0xffffffffu, bit);
+    if (lane == 0) x.routes[j] = int32_t(mask);
+    if (mask != 0) {
+      const uint8_t* codes = t.codes + j * t.codes_stride;
+      const uint8_t* sf = t.sf + j * t.sf_stride;
+      if (kVec) {
+        const int nc = kh / 16, np = (kh + ks) / 16;
+        for (int base = 0; base < np; base += 32 * kDispatchBatch) {
+          uint4 v[kDispatchBatch];
+#pragma unroll
+          for (int u = 0; u < kDispatchBatch; ++u) {
+            const int q = base + u * 32 + lane;
+            if (q < np)
+              v[u] = q < nc ? __ldg(reinterpret_cast<const uint4*>(codes) + q)
+                            : __ldg(reinterpret_cast<const uint4*>(sf) + (q - nc));
           }
-        } else {
-          for (int q = lane; q < len[part] / 4; q += 32) {
-            const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(src[part]) + q);
-            for (int s = 0; s < x.world; ++s)
-              reinterpret_cast<uint32_t*>(x.gathered[s] + off + at[part])[q] = v;
+          for (int s = 0; s < x.world; ++s) {
+            if (!((mask >> s) & 1u)) continue;
+            uint4* dst = reinterpret_cast<uint4*>(x.gathered[s] + off);
+#pragma unroll
+            for (int u = 0; u < kDispatchBatch; ++u) {
+              const int q = base + u * 32 + lane;
+              if (q < np) dst[q] = v[u];
+            }
+          }
+        }
+      } else {
+        const int nc = kh / 4, np = (kh + ks) / 4;
+        for (int base = 0; base < np; base += 32 * kDispatchBatch) {
+          uint32_t v[kDispatchBatch];
+#pragma unroll
+          for (int u = 0; u < kDispatchBatch; ++u) {
+            const int q = base + u * 32 + lane;
+            if (q < np)
+              v[u] = q < nc ? __ldg(reinterpret_cast<const uint32_t*>(codes) + q)
+                            : __ldg(reinterpret_cast<const uint32_t*>(sf) + (q - nc));
+          }
+          for (int s = 0; s < x.world; ++s) {
+            if (!((mask >> s) & 1u)) continue;
+            uint32_t* dst = reinterpret_cast<uint32_t*>(x.gathered[s] + off);
+#pragma unroll
+            for (int u = 0; u < kDispatchBatch; ++u) {
+              const int q = base + u * 32 + lane;
+              if (q < np) dst[q] = v[u];
+            }
           }
         }
       }
@@ -538,18 +594,22 @@ __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerD
         const int32_t id = tok_id(t, j, k);
         const float w = tok_weight(t, j, k);
         for (int s = 0; s < x.world; ++s) {
-          ids_at[s][k] = id;
-          reinterpret_cast<float*>(ids_at[s] + t.topk)[k] = w;
+          if (!((mask >> s) & 1u)) continue;
+          int32_t* ids = reinterpret_cast<int32_t*>(x.gathered[s] + off + kh + ks);
+          ids[k] = id;
+          reinterpret_cast<float*>(ids + t.topk)[k] = w;
         }
       }
       if (lane == 0) {
         const float sc = tok_scale(t, j);
-        for (int s = 0; s < x.world; ++s) reinterpret_cast<float*>(ids_at[s] + 2 * t.topk)[0] = sc;
+        for (int s = 0; s < x.world; ++s)
+          if ((mask >> s) & 1u)
+            reinterpret_cast<float*>(x.gathered[s] + off + kh + ks)[2 * t.topk] = sc;
       }
-    } else {
-      for (int k = lane; k < t.topk; k += 32)
-        for (int s = 0; s < x.world; ++s) ids_at[s][k] = -1;
     }
+    for (int k = lane; k < t.topk; k += 32)
+      for (int s = 0; s < x.world; ++s)
+        if (!((mask >> s) & 1u)) reinterpret_cast<int32_t*>(x.gathered[s] + off + kh + ks)[k] = -1;
   }
   signal_peers(x, 0, e);
 }
@@ -572,24 +632,36 @@ __global__ void moe_wait_peers_kernel(PeerDev x, int kind) {
   }
 }
 
-// out[i, :] = bf16(sum_s recv[s * capacity + i, :]) over this rank's half of
-// this forward; the last block to finish advances the epoch.
-__global__ void __launch_bounds__(256) moe_sum_peers_kernel(PeerDev x, int32_t tokens,
+// out[i, :] = bf16(sum_s recv[s * capacity + i, :]) over the ranks s in
+// routes[i] (the others sent no row), from this rank's half of this
+// forward: a thread per 8 columns of a token, all its loads issued before
+// the sums, striding over the items.  The last block to finish advances the
+// epoch.
+__global__ void __launch_bounds__(256, 4) moe_sum_peers_kernel(PeerDev x, int32_t tokens,
                                                             __nv_bfloat16* __restrict__ out) {
   griddep_wait();
   const int64_t par = (*x.epoch + 1) & 1;
   const __nv_bfloat16* parts =
       reinterpret_cast<const __nv_bfloat16*>(x.recv[x.rank] + par * x.recv_half);
-  const int64_t i = blockIdx.x;
-  const int n = x.n;
-  const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
-  if (i < tokens && col < n) {
+  const int n = x.n, chunks = n / 8;
+  const int64_t items = int64_t(tokens) * chunks;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t it = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; it < items; it += stride) {
+    const int64_t i = it / chunks;
+    const int col = int(it - i * chunks) * 8;
+    const unsigned mask = unsigned(x.routes[i]);
+    uint4 v[kPeersMax];
+#pragma unroll
+    for (int s = 0; s < kPeersMax; ++s)
+      if (s < x.world && ((mask >> s) & 1u))
+        v[s] = *reinterpret_cast<const uint4*>(parts + (int64_t(s) * x.capacity + i) * n + col);
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-    for (int s = 0; s < x.world; ++s) {
-      const uint4 v = *reinterpret_cast<const uint4*>(parts + (int64_t(s) * x.capacity + i) * n + col);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int s = 0; s < kPeersMax; ++s) {
+      if (!(s < x.world && ((mask >> s) & 1u))) continue;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[s]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __bfloat1622float2(h[j]);
@@ -605,8 +677,7 @@ __global__ void __launch_bounds__(256) moe_sum_peers_kernel(PeerDev x, int32_t t
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned nblocks = gridDim.x * gridDim.y;
-    if (unsigned(atomicAdd(x.counters + 2, 1)) == nblocks - 1) {
+    if (unsigned(atomicAdd(x.counters + 2, 1)) == gridDim.x - 1) {
       x.counters[2] = 0;
       *x.epoch = *x.epoch + 1;  // every block of this forward has read it
     }
@@ -681,6 +752,13 @@ bool rows_vec4(const MoeTok& t) {
          (t.k / 16) % 4 == 0;
 }
 
+// Blocks of 256 threads for a grid-stride kernel over `items` (one thread
+// each): at most per_sm per SM, as many as the kernel's launch bounds keep
+// resident at once, at least 1.
+int stride_grid(int64_t items, int sm_count, int per_sm) {
+  return int(std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, int64_t(sm_count) * per_sm)));
+}
+
 }  // namespace
 }  // namespace fgg
 
@@ -746,8 +824,10 @@ int to_peers(const FggMoePeers* p, int64_t rb, PeerDev* x) {
       p->capacity < 1 || p->n <= 0 || p->n % 8 != 0)
     return set_error(FGG_EBADSHAPE, "need 1 <= world <= %d, 0 <= rank < world, capacity >= 1, "
                                     "n a positive multiple of 8", kPeersMax);
-  if (p->epoch == nullptr || p->counters == nullptr || p->status == nullptr)
-    return set_error(FGG_EINVAL, "epoch / counters / status is null");
+  if (p->epoch == nullptr || p->counters == nullptr || p->status == nullptr ||
+      p->owner == nullptr || p->routes == nullptr)
+    return set_error(FGG_EINVAL, "epoch / counters / status / owner / routes is null");
+  if (p->num_experts < 1) return set_error(FGG_EBADSHAPE, "num_experts must be positive");
   memset(x, 0, sizeof(*x));
   x->world = p->world;
   x->rank = p->rank;
@@ -766,6 +846,9 @@ int to_peers(const FggMoePeers* p, int64_t rb, PeerDev* x) {
     x->recv[s] = static_cast<uint8_t*>(p->recv[s]);
     x->flags[s] = static_cast<unsigned long long*>(p->flags[s]);
   }
+  x->owner = p->owner;
+  x->num_experts = p->num_experts;
+  x->routes = p->routes;
   x->rb = rb;
   x->gathered_half = int64_t(p->world) * p->capacity * rb;
   x->recv_half = int64_t(p->world) * p->capacity * p->n * 2;
@@ -824,8 +907,10 @@ int fgg_moe_reduce_peers(const void* rows, int32_t num_rows, const int32_t* rout
   if (route_row == nullptr || bad == nullptr || (num_rows > 0 && rows == nullptr))
     return set_error(FGG_EINVAL, "null pointer");
   if (!aligned16(rows)) return set_error(FGG_EALIGN, "rows must be 16-byte aligned");
-  const dim3 grid(unsigned(t.num_tokens), unsigned((x.n / 8 + 255) / 256));
-  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel<true>, grid, dim3(256), 0,
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  const int grid = stride_grid(int64_t(t.num_tokens) * (x.n / 8), dev.sm_count, 4);
+  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel<true>, dim3(grid), dim3(256), 0,
                             reinterpret_cast<cudaStream_t>(stream), t,
                             static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, x.n,
                             static_cast<__nv_bfloat16*>(nullptr), bad, x));
@@ -840,9 +925,11 @@ int fgg_moe_sum_peers(const FggMoePeers* peers, int32_t tokens, void* out, void*
     return set_error(FGG_EBADSHAPE, "tokens=%d outside [0, capacity=%d]", tokens, x.capacity);
   if (out == nullptr && tokens > 0) return set_error(FGG_EINVAL, "out is null");
   if (tokens > 0 && !aligned16(out)) return set_error(FGG_EALIGN, "out must be 16-byte aligned");
-  // one block row even for zero tokens: its last block advances the epoch
-  const dim3 grid(unsigned(std::max(tokens, 1)), unsigned((x.n / 8 + 255) / 256));
-  FGG_CUDA_CHECK(launch_pdl(moe_sum_peers_kernel, grid, dim3(256), 0,
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  // at least one block even for zero tokens: the last block advances the epoch
+  const int grid = stride_grid(int64_t(tokens) * (x.n / 8), dev.sm_count, 4);
+  FGG_CUDA_CHECK(launch_pdl(moe_sum_peers_kernel, dim3(grid), dim3(256), 0,
                             reinterpret_cast<cudaStream_t>(stream), x, tokens,
                             static_cast<__nv_bfloat16*>(out)));
   FGG_CUDA_CHECK(cudaGetLastError());
@@ -907,10 +994,12 @@ int fgg_moe_reduce(const void* rows, int32_t num_rows, const int32_t* route_row,
     return set_error(FGG_EINVAL, "null pointer");
   if (!aligned16(rows) || !aligned16(out))
     return set_error(FGG_EALIGN, "rows and out must be 16-byte aligned");
-  const dim3 grid(unsigned(t.num_tokens), unsigned((n / 8 + 255) / 256));
+  DeviceInfo dev;
+  if (int rc = current_device(&dev)) return rc;
+  const int grid = stride_grid(int64_t(t.num_tokens) * (n / 8), dev.sm_count, 4);
   PeerDev none;
   memset(&none, 0, sizeof(none));
-  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel<false>, grid, dim3(256), 0,
+  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel<false>, dim3(grid), dim3(256), 0,
                             reinterpret_cast<cudaStream_t>(stream), t,
                             static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, n,
                             static_cast<__nv_bfloat16*>(out), bad, none));

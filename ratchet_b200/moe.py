@@ -83,6 +83,26 @@ def expert_popularity(num_experts: int, s: float = 1.1, seed: int = 0) -> np.nda
     return pop / pop.sum()
 
 
+def routed_load(num_experts: int, topk: int, s: float = 1.1, seed: int = 0,
+                samples: int = 65536, sample_seed: int = 12345) -> np.ndarray:
+    """Expected rows per token of each expert under zipf_routing(seed):
+    the probability that the expert is among a token's `topk` distinct
+    draws.  Drawing without replacement flattens the popularity (an expert
+    takes at most one route per token), so this, not the popularity itself,
+    is the load a placement must balance.  Estimated from `samples` draws
+    with their own seed, independent of any batch being served."""
+    pop = expert_popularity(num_experts, s=s, seed=seed)
+    rng = np.random.default_rng(sample_seed)
+    counts = np.zeros(num_experts, dtype=np.int64)
+    chunk = 8192
+    for start in range(0, samples, chunk):
+        m = min(chunk, samples - start)
+        keys = np.log(pop)[None, :] - np.log(-np.log(rng.random((m, num_experts))))
+        sel = np.argpartition(-keys, topk - 1, axis=1)[:, :topk]
+        counts += np.bincount(sel.ravel(), minlength=num_experts)
+    return counts / float(samples)
+
+
 def place_experts(load: Sequence[float], world: int):
     """Static expert -> rank placement that spreads the expected load.
 
@@ -134,9 +154,10 @@ class ExpertParallelMoE:
     its reduction).  transport: "nccl" moves the records and partial rows
     with NCCL collectives; "p2p" with the library's own kernels, which store
     them straight into the other ranks' buffers over NVLink (peer memory
-    mapped through CUDA IPC, epoch-tagged arrival flags, bounded waits) and
-    fuse the exchange with the packing and the weighted reduce; call
-    release() before destroying the process group.
+    mapped through CUDA IPC, epoch-tagged arrival flags, bounded waits),
+    fuse the exchange with the packing and the weighted reduce, and move a
+    token's record and partial row only to and from the ranks that own one
+    of its experts; call release() before destroying the process group.
     """
 
     def __init__(self, w_codes: Sequence[torch.Tensor], w_sf: Sequence[torch.Tensor],
@@ -293,6 +314,10 @@ class ExpertParallelMoE:
             peers.gathered[r] = ptrs[0][r]
             peers.recv[r] = ptrs[1][r]
             peers.flags[r] = ptrs[2][r]
+        # each token's destination ranks, from the dispatch to the sum
+        b["routes"] = torch.zeros(C, dtype=torch.int32, device=dev)
+        peers.owner, peers.num_experts = self.owner_d.data_ptr(), self.num_experts
+        peers.routes = b["routes"].data_ptr()
         b["peers"] = peers
         b["rb"] = rb
         toks = _lib.FggMoeTokens()

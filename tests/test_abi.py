@@ -181,6 +181,7 @@ def _peers(world=2, rank=0, capacity=4, n=64, base=0x10000, flag_off=0):
             p.gathered[r] = base + 0x1000 * (r + 1)
             p.recv[r] = base + 0x100000 * (r + 1)
             p.flags[r] = base + 0x200 + 0x100 * r + flag_off
+    p.owner, p.num_experts, p.routes = base + 0x800, 8, base + 0x900
     return p
 
 
@@ -204,6 +205,12 @@ def test_peer_descriptions_validated_before_device(L):
     p = _peers()
     p.recv[1] = None
     assert wait(p) == _lib.FGG_EINVAL
+    p = _peers()
+    p.routes = None
+    assert wait(p) == _lib.FGG_EINVAL
+    p = _peers()
+    p.num_experts = 0
+    assert wait(p) == _lib.FGG_EBADSHAPE
     assert wait(_peers(flag_off=4)) == _lib.FGG_EALIGN
     p = _peers()
     p.gathered[0] += 8

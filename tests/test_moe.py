@@ -172,3 +172,21 @@ def test_forward_two_gloo_ranks(tmp_path):
     for r in range(2):
         line = (tmp_path / f"rank{r}.txt").read_text()
         assert line.startswith("1 "), f"rank {r}: {line}"
+
+
+def test_routed_load_is_topk_inclusion():
+    """Expected rows per token: sums to topk, never above 1 per expert, ranks
+    the experts like their popularity, and balances a placement of a sampled
+    batch far better than the raw popularity at two and four ranks."""
+    E, topk = 64, 8
+    load = moe.routed_load(E, topk, samples=16384)
+    assert abs(load.sum() - topk) < 1e-9 and (load <= 1.0).all()
+    pop = moe.expert_popularity(E)
+    top = np.argsort(-pop)[:8]
+    assert np.array_equal(np.argsort(-load)[:8], top)   # the popular experts, in order
+    ids, _ = moe.zipf_routing(4096, E, topk, seed=0)
+    cnt = np.bincount(ids.ravel(), minlength=E)
+    for world in (2, 4):
+        by_load = [cnt[moe.place_experts(load, world)[0] == r].sum() for r in range(world)]
+        by_pop = [cnt[moe.place_experts(pop, world)[0] == r].sum() for r in range(world)]
+        assert max(by_load) / np.mean(by_load) < 1.03 < max(by_pop) / np.mean(by_pop)
