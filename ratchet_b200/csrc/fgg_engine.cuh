@@ -649,7 +649,8 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
                 tc_cp_sf(c0, desc_sf_atom(sSFW(q)));
 #pragma unroll
                 for (int c = 0; c < C::CH; ++c)
-                  tc_cp_sf(c0 + 4 + 4 * c, desc_sf_atom(sSFX(q) + c * 512));
+                  if (c == 0 || ncols > 128 * c)
+                    tc_cp_sf(c0 + 4 + 4 * c, desc_sf_atom(sSFX(q) + c * 512));
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                   // K step of 32 one-byte elements = 32 bytes = +2 in the start field;
@@ -665,9 +666,12 @@ __global__ void __launch_bounds__(256, 1) fgg_gemm_kernel(const __grid_constant_
                 for (int j = 0; j < 4; ++j) {
                   const uint32_t c0 = col[sub * 4 + j];
                   tc_cp_sf(c0, desc_sf_atom(sSFW(q) + j * 512));
+                  // token scale atom c covers tokens [128 c, 128 c + 128): a tile
+                  // of ncols columns reads only the atoms it reaches
 #pragma unroll
                   for (int c = 0; c < C::CH; ++c)
-                    tc_cp_sf(c0 + 4 + 4 * c, desc_sf_atom(sSFX(q) + (j * C::CH + c) * 512));
+                    if (c == 0 || ncols > 128 * c)
+                      tc_cp_sf(c0 + 4 + 4 * c, desc_sf_atom(sSFX(q) + (j * C::CH + c) * 512));
                   // K step of 64 fp4 = 32 bytes = +2 in the descriptor's start field.
                   tc_mma_nvf4(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, c0, c0 + 4,
                               (ks | j) != 0 ? 1u : 0u);
@@ -1135,7 +1139,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                 const uint32_t c0 = col[sub];
                 tc_cp_sf_pair(c0, desc_sf_atom(sSFW(q)));
                 tc_cp_sf_pair(c0 + 4, desc_sf_atom(sSFX(q)));
-                tc_cp_sf_pair(c0 + 8, desc_sf_atom(sSFX(q) + 512));
+                if (ncols > 128) tc_cp_sf_pair(c0 + 8, desc_sf_atom(sSFX(q) + 512));
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                   const uint32_t idj =
@@ -1150,7 +1154,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                   const uint32_t c0 = col[sub * 4 + j];
                   tc_cp_sf_pair(c0, desc_sf_atom(sSFW(q) + j * 512));
                   tc_cp_sf_pair(c0 + 4, desc_sf_atom(sSFX(q) + (2 * j) * 512));
-                  tc_cp_sf_pair(c0 + 8, desc_sf_atom(sSFX(q) + (2 * j + 1) * 512));
+                  // tokens 128..223: only a tile wider than 128 columns reads them
+                  if (ncols > 128)
+                    tc_cp_sf_pair(c0 + 8, desc_sf_atom(sSFX(q) + (2 * j + 1) * 512));
                   tc_mma_nvf4_pair(d_tmem, adesc + 2u * j, bdesc + 2u * j, idesc, c0, c0 + 4,
                                    (ks | j) != 0 ? 1u : 0u);
                 }

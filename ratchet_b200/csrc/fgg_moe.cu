@@ -444,71 +444,93 @@ __device__ __forceinline__ void signal_peers(const PeerDev& x, int kind, unsigne
   }
 }
 
-// Router-weighted sum of a token's local routes: out[i, :] =
-// bf16(sum_k w[i, k] * rows[route_row[i * topk + k], :]) over the routes with
-// a row (>= 0); a token with none gets a zero row.  fp32 accumulation in
-// route order; a thread takes 8 consecutive columns of one token per item
-// and strides over the items (a grid of a few blocks per SM, so that the
-// peer variant's fence before its signal is paid once per thread, not once
-// per token).  kPeers: token slot i's row goes to row
-// rank * capacity + i % capacity of rank i / capacity's recv buffer half,
-// only for a token with a route here (the sum on the token's rank skips the
-// others), and the combine flags follow.
-template <bool kPeers>
-__global__ void __launch_bounds__(256, 4) moe_reduce_kernel(MoeTok t,
+// Router-weighted sum of one token's local routes over 8 columns:
+// bf16(sum_k w[i, k] * rows[route_row[i * topk + k], col:col+8]) over the
+// routes with a row (>= 0), fp32 accumulation in route order; *any tells
+// whether the token has a route here at all.
+__device__ __forceinline__ uint4 reduce_routes(const MoeTok& t, const __nv_bfloat16* rows,
+                                               int32_t num_rows, const int32_t* route_row,
+                                               int32_t n, int64_t i, int col, int* bad,
+                                               bool* any) {
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  bool seen = false;
+  for (int k = 0; k < t.topk; ++k) {
+    const int r = __ldg(route_row + i * t.topk + k);
+    if (r < 0) continue;
+    if (r >= num_rows) {
+      atomicExch(bad, 1);
+      continue;
+    }
+    seen = true;
+    const float wk = tok_weight(t, i, k);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(rows + int64_t(r) * n + col));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      acc[2 * j] = fmaf(wk, f.x, acc[2 * j]);
+      acc[2 * j + 1] = fmaf(wk, f.y, acc[2 * j + 1]);
+    }
+  }
+  uint4 o;
+  __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+  *any = seen;
+  return o;
+}
+
+// out[i, :] = the router-weighted sum of token i's local routes (a zero row
+// for a token with none): block (i, y) takes 8 columns a thread, so that many
+// blocks stay resident to hide the row loads' latency.
+__global__ void __launch_bounds__(256) moe_reduce_kernel(MoeTok t,
                                                          const __nv_bfloat16* __restrict__ rows,
                                                          int32_t num_rows,
                                                          const int32_t* __restrict__ route_row,
                                                          int32_t n, __nv_bfloat16* __restrict__ out,
-                                                         int* __restrict__ bad, PeerDev x) {
+                                                         int* __restrict__ bad) {
   griddep_wait();
   t = resolved(t);
-  const int chunks = n / 8;
+  const int64_t i = blockIdx.x;
+  const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (i < t.num_tokens && col < n) {
+    bool any;
+    const uint4 o = reduce_routes(t, rows, num_rows, route_row, n, i, col, bad, &any);
+    *reinterpret_cast<uint4*>(out + i * n + col) = o;
+  }
+}
+
+// The same sum stored into the token's rank: token slot i's row goes to row
+// rank * capacity + i % capacity of rank i / capacity's recv buffer half,
+// only for a token with a route here (the sum on the token's rank skips the
+// others); the combine flags follow.  A thread takes 8 columns of one token
+// per item and strides over the items (a grid of a few blocks per SM, so
+// that the fence before the signal is paid once per thread, not once per
+// token).
+__global__ void __launch_bounds__(256, 4) moe_reduce_peers_kernel(
+    MoeTok t, const __nv_bfloat16* __restrict__ rows, int32_t num_rows,
+    const int32_t* __restrict__ route_row, int* __restrict__ bad, PeerDev x) {
+  griddep_wait();
+  t = resolved(t);
+  const int n = x.n, chunks = n / 8;
   const int64_t items = int64_t(t.num_tokens) * chunks;
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-  int64_t par = 0;
-  if constexpr (kPeers) par = (*x.epoch + 1) & 1;
+  const int64_t par = (*x.epoch + 1) & 1;
   for (int64_t it = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; it < items; it += stride) {
     const int64_t i = it / chunks;
     const int col = int(it - i * chunks) * 8;
-    float acc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-    bool any = false;
-    for (int k = 0; k < t.topk; ++k) {
-      const int r = __ldg(route_row + i * t.topk + k);
-      if (r < 0) continue;
-      if (r >= num_rows) {
-        atomicExch(bad, 1);
-        continue;
-      }
-      any = true;
-      const float wk = tok_weight(t, i, k);
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(rows + int64_t(r) * n + col));
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        acc[2 * j] = fmaf(wk, f.x, acc[2 * j]);
-        acc[2 * j + 1] = fmaf(wk, f.y, acc[2 * j + 1]);
-      }
-    }
-    uint4 o;
-    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
-    if constexpr (kPeers) {
-      if (any) {
-        const int src = int(i / x.capacity);
-        const int64_t slot = int64_t(x.rank) * x.capacity + i % x.capacity;
-        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(x.recv[src] + par * x.recv_half) +
-                                  slot * n + col) = o;
-      }
-    } else {
-      *reinterpret_cast<uint4*>(out + i * n + col) = o;
+    bool any;
+    const uint4 o = reduce_routes(t, rows, num_rows, route_row, n, i, col, bad, &any);
+    if (any) {
+      const int src = int(i / x.capacity);
+      const int64_t slot = int64_t(x.rank) * x.capacity + i % x.capacity;
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(x.recv[src] + par * x.recv_half) +
+                                slot * n + col) = o;
     }
   }
-  if constexpr (kPeers) signal_peers(x, 1, (unsigned long long)(*x.epoch + 1));
+  signal_peers(x, 1, (unsigned long long)(*x.epoch + 1));
 }
 
 // Dispatch over peer memory: one warp per token slot of this rank.  The
@@ -910,10 +932,9 @@ int fgg_moe_reduce_peers(const void* rows, int32_t num_rows, const int32_t* rout
   DeviceInfo dev;
   if (int rc = current_device(&dev)) return rc;
   const int grid = stride_grid(int64_t(t.num_tokens) * (x.n / 8), dev.sm_count, 4);
-  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel<true>, dim3(grid), dim3(256), 0,
+  FGG_CUDA_CHECK(launch_pdl(moe_reduce_peers_kernel, dim3(grid), dim3(256), 0,
                             reinterpret_cast<cudaStream_t>(stream), t,
-                            static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, x.n,
-                            static_cast<__nv_bfloat16*>(nullptr), bad, x));
+                            static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, bad, x));
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }
@@ -994,15 +1015,11 @@ int fgg_moe_reduce(const void* rows, int32_t num_rows, const int32_t* route_row,
     return set_error(FGG_EINVAL, "null pointer");
   if (!aligned16(rows) || !aligned16(out))
     return set_error(FGG_EALIGN, "rows and out must be 16-byte aligned");
-  DeviceInfo dev;
-  if (int rc = current_device(&dev)) return rc;
-  const int grid = stride_grid(int64_t(t.num_tokens) * (n / 8), dev.sm_count, 4);
-  PeerDev none;
-  memset(&none, 0, sizeof(none));
-  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel<false>, dim3(grid), dim3(256), 0,
+  const dim3 grid(unsigned(t.num_tokens), unsigned((n / 8 + 255) / 256));
+  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel, grid, dim3(256), 0,
                             reinterpret_cast<cudaStream_t>(stream), t,
                             static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, n,
-                            static_cast<__nv_bfloat16*>(out), bad, none));
+                            static_cast<__nv_bfloat16*>(out), bad));
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }
