@@ -307,27 +307,37 @@ def make_set(wl, seed: int, dev):
                 max_m=max(ms) if ms else 0)
 
 
-def public_call(s, out=None):
-    """The public operator call a step makes: the per-group-list operator
-    (the reference operator's NVFP4 drop-in), or for decode-shaped sets (every
-    M_g <= 16) the contiguous-rows form with device offsets, whose host work
-    does not grow with the group count."""
+# The public entry a step calls: "rows" = nvfp4_grouped_gemm_rows over the
+# contiguous activations with device offsets (the reference operator's own
+# M-grouped layout; host work independent of the group count), "list" = the
+# per-group-list operator.
+CALL = "rows"
+
+
+def public_call(s, out=None, call=None):
+    """The public operator call a step makes (CALL unless `call` is given).
+    Decode-shaped sets (every M_g <= 16) pass that bound, which selects the
+    decode tiles."""
     import ratchet_b200 as rb
 
-    if s["max_m"] <= 16:
+    if (call or CALL) == "rows":
         if "pack" not in s:
             s["pack"] = rb.pack_weights(s["b"], s["b_sf"])
         return rb.nvfp4_grouped_gemm_rows(s["a_all"], s["sf_all"], s["offsets"], pack=s["pack"],
-                                          alpha=s["alpha"], out=out, max_group_rows=16)
+                                          alpha=s["alpha"], out=out,
+                                          max_group_rows=16 if s["max_m"] <= 16 else 0)
     return rb.nvfp4_grouped_gemm(s["a"], s["a_sf"], s["b"], s["b_sf"], s["sizes"], s["alpha"],
                                  out=out)
 
 
-def time_value(sets, steps, warmup, dev, ws):
+def time_value(sets, steps, warmup, dev, ws, entry=None):
+    """Device time per step (CUDA events around exactly `steps` calls) and the
+    host's time per call (wall clock of the same loop, which only enqueues
+    work: while the device is the bottleneck this is the host cost itself)."""
     import ratchet_b200 as rb
 
     R = len(sets)
-    call = lambda s: public_call(s)
+    call = lambda s: public_call(s, call=entry)
     for i in range(warmup):
         call(sets[i % R])
     torch.cuda.synchronize()
@@ -336,14 +346,16 @@ def time_value(sets, steps, warmup, dev, ws):
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
+    h0 = time.perf_counter()
     for i in range(steps):
         call(sets[i % R])
+    host_us = (time.perf_counter() - h0) * 1e6 / steps
     e1.record(st)
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
     rb.last_status()
-    return e0.elapsed_time(e1) / steps
+    return e0.elapsed_time(e1) / steps, host_us
 
 
 def time_kernel_only(sets, steps, dev):
@@ -853,9 +865,14 @@ def run_ours(args, wl):
 
     sampler = ClockSampler(local)
     sampler.start()
-    ms = time_value(sets, args.steps, args.warmup, dev, ws)
+    ms, host_us = time_value(sets, args.steps, args.warmup, dev, ws)
     clocks = sampler.stop()
     ms = max_over_ranks(ms, ws, dev)
+    host_us = max_over_ranks(host_us, ws, dev)
+    # the other public entry on the same sets, for its step and host cost
+    other = "list" if CALL == "rows" else "rows"
+    o_ms, o_host = time_value(sets, args.steps, args.warmup, dev, ws, entry=other)
+    o_ms, o_host = max_over_ranks(o_ms, ws, dev), max_over_ranks(o_host, ws, dev)
     fl_rank = flops(sub)
     fl = flops(wl) if strong else fl_rank * ws     # work of the whole job
     value = fl / (ms * 1e-3) / 1e12
@@ -870,7 +887,9 @@ def run_ours(args, wl):
         roof = {"bound": "tensor", "achieved": frac * 4.0 * pk["bf16"], "peak": 4.0 * pk["bf16"],
                 "unit": "TFLOP/s", "frac": frac, "traffic": traffic_from_profiles(wl["name"]),
                 "peak_basis": f"4 x {pk['src']} dense bf16 ({pk['bf16']:.0f} TF/s)",
-                "kernel_ms": k_ms, "alg_bytes": alg_bytes(sub)}
+                "kernel_ms": k_ms, "alg_bytes": alg_bytes(sub),
+                "kernel": "the GEMM launch alone (fgg_nvfp4_gemm after one prepare per set; "
+                          "the same tile kernel both public entries launch)"}
     else:
         achieved = alg_bytes(sub) / (k_ms * 1e-3) / 1e9
         frac = max_over_ranks(-achieved / pk["hbm"], ws, dev) * -1.0
@@ -904,8 +923,8 @@ def run_ours(args, wl):
                                        ("N split" if wl["name"] == "dense" else "groups sharded")
                                        + f" over {ws}"),
                        "rank0_part": sub["split"],
-                       "call": "nvfp4_grouped_gemm_rows (device offsets)" if sets[0]["max_m"] <= 16
-                               else "nvfp4_grouped_gemm (per-group lists)",
+                       "call": ("nvfp4_grouped_gemm_rows (contiguous rows, device offsets)"
+                                if CALL == "rows" else "nvfp4_grouped_gemm (per-group lists)"),
                        "l2": f"{R} rotating input sets of {per_set / 1e6:.0f} MB per rank "
                              "(> L2 in total)"},
             "clocks": clocks,
@@ -914,6 +933,8 @@ def run_ours(args, wl):
                 "h2d_bytes_per_step": h2d * ws, "d2h_bytes_per_step": d2h * ws,
                 "ms_per_step": e2e_ms},
             "gpu_launches": 2 * args.steps,
+            "host_us_per_call": host_us,
+            "other_entry": {"call": other, "ms_per_step": o_ms, "host_us_per_call": o_host},
             "roofline": roof,
             "cpu_baseline": cpu,
         }
@@ -1232,11 +1253,15 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--combine", choices=["a2a", "reduce_scatter"], default="a2a",
                     help="the MoE layer's combine collective (--config moe)")
+    ap.add_argument("--call", choices=["rows", "list"], default="rows",
+                    help="the public entry a GEMM step calls (configs other than moe / mx)")
     ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
                     help="the MoE layer's exchange: NCCL collectives or the library's "
                          "peer-store kernels (--config moe)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    global CALL
+    CALL = args.call
     wl = workload(args.config)
     if args.impl == "reference" and wl["name"] == "mlp":
         print(json.dumps({"impl": "reference", "unavailable": "the reference operator has no "
