@@ -11,6 +11,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <cstring>
 
 #include "fgg_host.cuh"
@@ -533,26 +534,35 @@ __global__ void __launch_bounds__(256, 4) moe_reduce_peers_kernel(
   signal_peers(x, 1, (unsigned long long)(*x.epoch + 1));
 }
 
-// Dispatch over peer memory: one warp per token slot of this rank.  The
-// warp finds the ranks that own one of the token's experts (routes[j], a bit
-// mask) and writes the slot's record into those ranks' gathered buffer
-// halves; every other rank's slot gets expert ids -1 only, as do slots past
-// the rank's tokens.  The codes and scales are contiguous in a record, so
+// Dispatch over peer memory: kDispatchParts warps per token slot of this
+// rank, each moving one part of the slot's record, so that even a few hundred
+// slots keep every SM storing.  Each warp finds the ranks that own one of
+// the token's experts (a bit mask; part 0 keeps it in routes[j]) and writes
+// its part of the record into those ranks' gathered buffer halves; part 0
+// also writes the expert ids, router weights and decode scale, and gives
+// every other rank's slot expert ids -1 only, as it does for slots past the
+// rank's tokens.  The codes and scales are contiguous in a record, so
 // 16-byte piece q of the record comes from the codes (q < K/32) or the
-// scales; a lane loads up to kDispatchBatch pieces before it stores any, so
-// that many stores are in flight per warp (one read of the token, one store
-// of each piece per destination).  The dispatch flags follow.
+// scales; a lane loads up to kDispatchBatch pieces before it stores any.
+// The dispatch flags follow.
 constexpr int kDispatchBatch = 8;
+constexpr int kDispatchParts = 4;
 
 template <bool kVec>
 __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerDev x) {
+  using V = typename std::conditional<kVec, uint4, uint32_t>::type;
+  constexpr int kB = int(sizeof(V));
   const unsigned long long e = (unsigned long long)(*x.epoch + 1);
   const int64_t par = int64_t(e & 1ull);
   const int lane = threadIdx.x & 31;
   const int kh = t.k / 2, ks = t.k / 16;
+  const int nc = kh / kB, np = (kh + ks) / kB;  // pieces: codes, then all
   const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t j = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; j < x.capacity;
-       j += warps) {  // warp-uniform
+  const int64_t items = int64_t(x.capacity) * kDispatchParts;
+  for (int64_t w = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < items;
+       w += warps) {  // warp-uniform
+    const int64_t j = w / kDispatchParts;
+    const int part = int(w - j * kDispatchParts);
     const int64_t off = par * x.gathered_half + (int64_t(x.rank) * x.capacity + j) * x.rb;
     unsigned bit = 0;
     if (j < t.num_tokens) {
@@ -565,61 +575,40 @@ __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerD
       }
     }
     const unsigned mask = __reduce_or_sync(0xffffffffu, bit);
-    if (lane == 0) x.routes[j] = int32_t(mask);
     if (mask != 0) {
-      const uint8_t* codes = t.codes + j * t.codes_stride;
-      const uint8_t* sf = t.sf + j * t.sf_stride;
-      if (kVec) {
-        const int nc = kh / 16, np = (kh + ks) / 16;
-        for (int base = 0; base < np; base += 32 * kDispatchBatch) {
-          uint4 v[kDispatchBatch];
+      const V* codes = reinterpret_cast<const V*>(t.codes + j * t.codes_stride);
+      const V* sf = reinterpret_cast<const V*>(t.sf + j * t.sf_stride);
+      const int q0 = int(int64_t(np) * part / kDispatchParts);
+      const int q1 = int(int64_t(np) * (part + 1) / kDispatchParts);
+      for (int base = q0; base < q1; base += 32 * kDispatchBatch) {
+        V v[kDispatchBatch];
 #pragma unroll
-          for (int u = 0; u < kDispatchBatch; ++u) {
-            const int q = base + u * 32 + lane;
-            if (q < np)
-              v[u] = q < nc ? __ldg(reinterpret_cast<const uint4*>(codes) + q)
-                            : __ldg(reinterpret_cast<const uint4*>(sf) + (q - nc));
-          }
-          for (int s = 0; s < x.world; ++s) {
-            if (!((mask >> s) & 1u)) continue;
-            uint4* dst = reinterpret_cast<uint4*>(x.gathered[s] + off);
-#pragma unroll
-            for (int u = 0; u < kDispatchBatch; ++u) {
-              const int q = base + u * 32 + lane;
-              if (q < np) dst[q] = v[u];
-            }
-          }
+        for (int u = 0; u < kDispatchBatch; ++u) {
+          const int q = base + u * 32 + lane;
+          if (q < q1) v[u] = q < nc ? __ldg(codes + q) : __ldg(sf + (q - nc));
         }
-      } else {
-        const int nc = kh / 4, np = (kh + ks) / 4;
-        for (int base = 0; base < np; base += 32 * kDispatchBatch) {
-          uint32_t v[kDispatchBatch];
+        for (int s = 0; s < x.world; ++s) {
+          if (!((mask >> s) & 1u)) continue;
+          V* dst = reinterpret_cast<V*>(x.gathered[s] + off);
 #pragma unroll
           for (int u = 0; u < kDispatchBatch; ++u) {
             const int q = base + u * 32 + lane;
-            if (q < np)
-              v[u] = q < nc ? __ldg(reinterpret_cast<const uint32_t*>(codes) + q)
-                            : __ldg(reinterpret_cast<const uint32_t*>(sf) + (q - nc));
-          }
-          for (int s = 0; s < x.world; ++s) {
-            if (!((mask >> s) & 1u)) continue;
-            uint32_t* dst = reinterpret_cast<uint32_t*>(x.gathered[s] + off);
-#pragma unroll
-            for (int u = 0; u < kDispatchBatch; ++u) {
-              const int q = base + u * 32 + lane;
-              if (q < np) dst[q] = v[u];
-            }
+            if (q < q1) dst[q] = v[u];
           }
         }
       }
+    }
+    if (part != 0) continue;
+    if (lane == 0) x.routes[j] = int32_t(mask);
+    if (mask != 0) {
       for (int k = lane; k < t.topk; k += 32) {
         const int32_t id = tok_id(t, j, k);
-        const float w = tok_weight(t, j, k);
+        const float wt = tok_weight(t, j, k);
         for (int s = 0; s < x.world; ++s) {
           if (!((mask >> s) & 1u)) continue;
           int32_t* ids = reinterpret_cast<int32_t*>(x.gathered[s] + off + kh + ks);
           ids[k] = id;
-          reinterpret_cast<float*>(ids + t.topk)[k] = w;
+          reinterpret_cast<float*>(ids + t.topk)[k] = wt;
         }
       }
       if (lane == 0) {
@@ -895,7 +884,9 @@ int fgg_moe_dispatch_peers(const FggMoeTokens* tokens, const FggMoePeers* peers,
     return set_error(FGG_EINVAL, "codes / sf is null");
   DeviceInfo dev;
   if (int rc = current_device(&dev)) return rc;
-  const int grid = int(std::min<int64_t>((int64_t(x.capacity) + 7) / 8, int64_t(dev.sm_count) * 4));
+  // 8 warps a block, kDispatchParts warps a token slot
+  const int grid = int(std::min<int64_t>((int64_t(x.capacity) * kDispatchParts + 7) / 8,
+                                         int64_t(dev.sm_count) * 8));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (rows_vec16(t) || t.num_tokens == 0)
     moe_dispatch_peers_kernel<true><<<grid, 256, 0, s>>>(t, x);
