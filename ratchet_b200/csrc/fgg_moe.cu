@@ -534,9 +534,9 @@ __global__ void __launch_bounds__(256, 4) moe_reduce_peers_kernel(
   signal_peers(x, 1, (unsigned long long)(*x.epoch + 1));
 }
 
-// Dispatch over peer memory: kDispatchParts warps per token slot of this
-// rank, each moving one part of the slot's record, so that even a few hundred
-// slots keep every SM storing.  Each warp finds the ranks that own one of
+// Dispatch over peer memory: `parts` warps per token slot of this rank (1 to
+// kDispatchParts, more when there are few slots), each moving one part of
+// the slot's record, so that even a few hundred slots keep every SM storing.  Each warp finds the ranks that own one of
 // the token's experts (a bit mask; part 0 keeps it in routes[j]) and writes
 // its part of the record into those ranks' gathered buffer halves; part 0
 // also writes the expert ids, router weights and decode scale, and gives
@@ -549,7 +549,7 @@ constexpr int kDispatchBatch = 8;
 constexpr int kDispatchParts = 4;
 
 template <bool kVec>
-__global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerDev x) {
+__global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerDev x, int parts) {
   using V = typename std::conditional<kVec, uint4, uint32_t>::type;
   constexpr int kB = int(sizeof(V));
   const unsigned long long e = (unsigned long long)(*x.epoch + 1);
@@ -558,11 +558,11 @@ __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerD
   const int kh = t.k / 2, ks = t.k / 16;
   const int nc = kh / kB, np = (kh + ks) / kB;  // pieces: codes, then all
   const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-  const int64_t items = int64_t(x.capacity) * kDispatchParts;
+  const int64_t items = int64_t(x.capacity) * parts;
   for (int64_t w = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < items;
        w += warps) {  // warp-uniform
-    const int64_t j = w / kDispatchParts;
-    const int part = int(w - j * kDispatchParts);
+    const int64_t j = w / parts;
+    const int part = int(w - j * parts);
     const int64_t off = par * x.gathered_half + (int64_t(x.rank) * x.capacity + j) * x.rb;
     unsigned bit = 0;
     if (j < t.num_tokens) {
@@ -578,8 +578,8 @@ __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerD
     if (mask != 0) {
       const V* codes = reinterpret_cast<const V*>(t.codes + j * t.codes_stride);
       const V* sf = reinterpret_cast<const V*>(t.sf + j * t.sf_stride);
-      const int q0 = int(int64_t(np) * part / kDispatchParts);
-      const int q1 = int(int64_t(np) * (part + 1) / kDispatchParts);
+      const int q0 = int(int64_t(np) * part / parts);
+      const int q1 = int(int64_t(np) * (part + 1) / parts);
       for (int base = q0; base < q1; base += 32 * kDispatchBatch) {
         V v[kDispatchBatch];
 #pragma unroll
@@ -884,14 +884,17 @@ int fgg_moe_dispatch_peers(const FggMoeTokens* tokens, const FggMoePeers* peers,
     return set_error(FGG_EINVAL, "codes / sf is null");
   DeviceInfo dev;
   if (int rc = current_device(&dev)) return rc;
-  // 8 warps a block, kDispatchParts warps a token slot
-  const int grid = int(std::min<int64_t>((int64_t(x.capacity) * kDispatchParts + 7) / 8,
+  // 8 warps a block; a token slot per warp down to about 2048 slots, then
+  // up to kDispatchParts warps a slot
+  const int parts = int(std::max<int64_t>(1, std::min<int64_t>(kDispatchParts,
+                                                               2048 / std::max(x.capacity, 1))));
+  const int grid = int(std::min<int64_t>((int64_t(x.capacity) * parts + 7) / 8,
                                          int64_t(dev.sm_count) * 8));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (rows_vec16(t) || t.num_tokens == 0)
-    moe_dispatch_peers_kernel<true><<<grid, 256, 0, s>>>(t, x);
+    moe_dispatch_peers_kernel<true><<<grid, 256, 0, s>>>(t, x, parts);
   else if (rows_vec4(t))
-    moe_dispatch_peers_kernel<false><<<grid, 256, 0, s>>>(t, x);
+    moe_dispatch_peers_kernel<false><<<grid, 256, 0, s>>>(t, x, parts);
   else
     return set_error(FGG_EALIGN, "token rows must start on 4-byte boundaries");
   FGG_CUDA_CHECK(cudaGetLastError());
