@@ -3,6 +3,7 @@
 #include "fgg_host.cuh"
 
 #include <atomic>
+#include <cstring>
 #include <mutex>
 
 namespace fgg {
@@ -122,9 +123,47 @@ int current_device(DeviceInfo* out) {
   return FGG_OK;
 }
 
+// The encoder's arguments, which fully determine its result: a repeated call
+// (the same buffers every step) copies the remembered map instead of
+// encoding again.  Per host thread, a few entries replaced round-robin.
+struct EncodeKey {
+  int dtype, rank, swz;
+  const void* base;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  bool operator==(const EncodeKey& o) const { return memcmp(this, &o, sizeof(*this)) == 0; }
+};
+struct EncodeMemo {
+  static constexpr int kEntries = 16;
+  EncodeKey key[kEntries];
+  CUtensorMap map[kEntries];
+  bool used[kEntries];
+  int next;
+};
+static thread_local EncodeMemo t_memo;
+
 static int encode(CUtensorMap* out, CUtensorMapDataType dtype, cuuint32_t rank, const void* base,
                   const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
                   CUtensorMapSwizzle swz) {
+  EncodeKey k;
+  memset(&k, 0, sizeof(k));  // padding too: keys compare as bytes
+  k.dtype = int(dtype);
+  k.rank = int(rank);
+  k.swz = int(swz);
+  k.base = base;
+  for (cuuint32_t i = 0; i < rank && i < 3; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+    if (i + 1 < rank) k.strides[i] = strides[i];
+  }
+  EncodeMemo& m = t_memo;
+  if (rank <= 3) {
+    for (int i = 0; i < EncodeMemo::kEntries; ++i)
+      if (m.used[i] && m.key[i] == k) {
+        *out = m.map[i];
+        return FGG_OK;
+      }
+  }
   std::call_once(g_encode_once, load_encoder);
   if (g_encode == nullptr)
     return set_error(FGG_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
@@ -135,6 +174,13 @@ static int encode(CUtensorMap* out, CUtensorMapDataType dtype, cuuint32_t rank, 
   if (r != CUDA_SUCCESS)
     return set_error(FGG_ECUDA, "cuTensorMapEncodeTiled failed (CUresult %d, rank %u)", int(r),
                      rank);
+  if (rank <= 3) {
+    const int i = m.next;
+    m.next = (m.next + 1) % EncodeMemo::kEntries;
+    m.key[i] = k;
+    m.map[i] = *out;
+    m.used[i] = true;
+  }
   return FGG_OK;
 }
 
