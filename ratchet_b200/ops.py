@@ -388,34 +388,39 @@ def nvfp4_grouped_gemm_rows(a: torch.Tensor, a_sf: torch.Tensor, offsets: torch.
             raise ValueError("give pack= or b_list / b_sf_list")
         pack = pack_weights(b_list, b_sf_list)
     n, k, dev = pack.n, pack.k, pack.device
-    a_u8 = _as_u8(a, "a")
-    s_u8 = _as_u8(a_sf, "a_sf")
+    # device checks on the index (get_device(): -1 on the host), which is
+    # cheaper than building and comparing device objects
+    di = dev.index if dev.type == "cuda" else -1
+    a_u8 = a if a.dtype is torch.uint8 else _as_u8(a, "a")
+    s_u8 = a_sf if a_sf.dtype is torch.uint8 else _as_u8(a_sf, "a_sf")
     if a_u8.dim() != 2 or a_u8.shape[1] != k // 2 or s_u8.shape != (a_u8.shape[0], k // 16):
         raise ValueError(f"a {tuple(a_u8.shape)} / a_sf {tuple(s_u8.shape)} do not match "
                          f"[R, {k // 2}] / [R, {k // 16}] for K={k}")
-    if not (a_u8.is_contiguous() and s_u8.is_contiguous() and a_u8.device == dev
-            and s_u8.device == dev):
+    if not (a_u8.is_contiguous() and s_u8.is_contiguous() and a_u8.get_device() == di
+            and s_u8.get_device() == di):
         raise ValueError(f"a and a_sf must be contiguous tensors on {dev}")
-    if (offsets.dtype != torch.int32 or offsets.dim() != 1 or offsets.device != dev
+    if (offsets.dtype is not torch.int32 or offsets.dim() != 1 or offsets.get_device() != di
             or not offsets.is_contiguous()):
         raise ValueError(f"offsets must be a contiguous int32 tensor on {dev}")
-    G = int(offsets.shape[0]) - 1
-    R = int(a_u8.shape[0])
+    G = offsets.shape[0] - 1
+    R = a_u8.shape[0]
     if alpha is None:
         alpha = torch.ones(G, dtype=torch.float32, device=dev)
-    if (alpha.dtype != torch.float32 or alpha.numel() != G or alpha.device != dev
+    if (alpha.dtype is not torch.float32 or alpha.numel() != G or alpha.get_device() != di
             or not alpha.is_contiguous()):
         raise ValueError(f"alpha must be a contiguous fp32 tensor of {G} values on {dev}")
     if out is None:
         out = torch.empty((R, n), dtype=torch.bfloat16, device=dev)
-    elif (out.dtype != torch.bfloat16 or out.shape != (R, n) or not out.is_contiguous()
-          or out.device != dev):
+    elif (out.dtype is not torch.bfloat16 or out.shape != (R, n) or not out.is_contiguous()
+          or out.get_device() != di):
         raise ValueError(f"out must be a contiguous bf16 [{R}, {n}] tensor on {dev}")
-    for name, t, dt, cnt in (("row_scale", row_scale, torch.float32, R),
-                             ("b_index", b_index, torch.int32, G)):
-        if t is not None and (t.dtype != dt or t.numel() != cnt or t.device != dev
-                              or not t.is_contiguous()):
-            raise ValueError(f"{name} must be a contiguous {dt} tensor of {cnt} values on {dev}")
+    if row_scale is not None or b_index is not None:
+        for name, t, dt, cnt in (("row_scale", row_scale, torch.float32, R),
+                                 ("b_index", b_index, torch.int32, G)):
+            if t is not None and (t.dtype is not dt or t.numel() != cnt or t.get_device() != di
+                                  or not t.is_contiguous()):
+                raise ValueError(f"{name} must be a contiguous {dt} tensor of {cnt} values "
+                                 f"on {dev}")
     L = _lib.lib()
     key = (dev.index, G, n, k, R, int(max_group_rows), b_index is not None, pack.G)
     hit = _ROWS.get(key)
