@@ -303,6 +303,8 @@ def make_set(wl, seed: int, dev):
     off[1:] = torch.cumsum(torch.tensor(ms, dtype=torch.int64), 0).to(torch.int32)
     return dict(a=list(a_all.split(ms)), a_sf=[t.view(torch.float8_e4m3fn) for t in sf_all.split(ms)],
                 a_all=a_all, sf_all=sf_all.view(torch.float8_e4m3fn), offsets=off.to(dev),
+                out=torch.empty((rows, r1 - r0 if wl["name"] == "dense" else n),
+                                dtype=torch.bfloat16, device=dev),
                 b=B, b_sf=BSF, alpha=torch.stack(alpha).float(), sizes=[(m, n, k) for m in ms],
                 max_m=max(ms) if ms else 0)
 
@@ -315,11 +317,14 @@ CALL = "rows"
 
 
 def public_call(s, out=None, call=None):
-    """The public operator call a step makes (CALL unless `call` is given).
-    Decode-shaped sets (every M_g <= 16) pass that bound, which selects the
-    decode tiles."""
+    """The public operator call a step makes (CALL unless `call` is given),
+    writing the set's own output buffer unless `out` is given (a serving loop
+    reuses its output buffers).  Decode-shaped sets (every M_g <= 16) pass
+    that bound, which selects the decode tiles."""
     import ratchet_b200 as rb
 
+    if out is None:
+        out = s["out"]
     if (call or CALL) == "rows":
         if "pack" not in s:
             s["pack"] = rb.pack_weights(s["b"], s["b_sf"])
