@@ -1103,12 +1103,12 @@ def run_moe(args, wl):
     del replay
     layer.release()
     if args.transport == "p2p":
-        # pack+store, wait, expand (2), GEMM (2), reduce+store, wait, sum
-        launches = 9
+        # dispatch (pack + peer stores), wait, expand (2), GEMM (2), reduce, signal, wait, sum
+        launches = 10
         dispatch_desc = ("peer stores of token records into every rank's buffer by the "
                          "library's dispatch kernel (CUDA IPC, no multicast), bounded flag wait")
-        combine_desc = ("peer stores of router-weighted partial rows by the reduce kernel, "
-                        "bounded flag wait, fp32 sum")
+        combine_desc = ("router-weighted partial rows kept where they are computed, "
+                        "bounded flag wait, fp32 sum reading them over NVLink")
     else:
         launches = 7 if ws > 1 else 5
         dispatch_desc = ("NCCL all-gather of token records (capacity = tokens per rank)"

@@ -362,15 +362,18 @@ FGG_API int fgg_moe_sum_partials(const void* parts, int32_t world, int32_t per_s
  * Arrival is signalled by epoch-tagged flags in each destination's memory,
  * written with release semantics after the data; every wait for them is
  * bounded (about one second), after which the waiter sets *status = 0x301
- * and returns (its data is then incomplete).  The data buffers are double
+ * and returns (its data is then incomplete).  The dispatch buffer is double
  * buffered on the forward's epoch parity, so one forward's stores never
- * touch the half a slower peer still reads.  No counterpart in the reference
- * (it has no distributed code).
+ * touch the half a slower peer still reads.  The combine pulls: each rank
+ * writes its partial rows into its own return buffer and each token's rank
+ * reads them from there over NVLink; a rank overwrites that buffer only
+ * after every rank has dispatched the next forward, i.e. finished reading
+ * it.  No counterpart in the reference (it has no distributed code).
  *
  * Buffers (every rank allocates its own with fgg_peer_alloc and maps the
  * others' with fgg_peer_export / fgg_peer_import):
  *   gathered  [2][world * capacity][record bytes]   dispatch destination
- *   recv      [2][world * capacity][n] bf16          combine destination
+ *   recv      [world * capacity][n] bf16             partial rows, read by their token's rank
  *   flags     [2][8] uint64 (arrivals: [0] dispatch, [1] combine, by source)
  * epoch (int64), counters (3 x int32), status (int32) and routes
  * ([capacity] int32) are this rank's own.  A token's record and partial row
@@ -410,15 +413,14 @@ FGG_API int fgg_moe_dispatch_peers(const FggMoeTokens* tokens, const FggMoePeers
 /* Wait (bounded) until every rank's arrival flag of `kind` (0 dispatch,
  * 1 combine) carries this forward's epoch. */
 FGG_API int fgg_moe_wait_peers(const FggMoePeers* peers, int32_t kind, void* stream);
-/* fgg_moe_reduce whose output row of token slot t (of world * capacity) goes
- * to row rank * capacity + t % capacity of rank t / capacity's recv buffer,
- * for the tokens with a route on this rank only, followed by the combine
- * arrival flags. */
+/* fgg_moe_reduce into this rank's own recv buffer: the partial row of
+ * gathered slot t (of world * capacity) in row t, for the tokens with a
+ * route on this rank only, followed by the combine arrival flags. */
 FGG_API int fgg_moe_reduce_peers(const void* rows, int32_t num_rows, const int32_t* route_row,
                                  const FggMoeTokens* tokens, const FggMoePeers* peers, int* bad,
                                  void* stream);
-/* out[t, :] = bf16(sum_s recv[s * capacity + t, :]) in fp32 for t < tokens
- * over the ranks s in routes[t], from this rank's recv half of this forward
+/* out[t, :] = bf16(sum_s recv_s[rank * capacity + t, :]) in fp32 for
+ * t < tokens over the ranks s in routes[t], read from rank s's recv buffer
  * (zeros for a token with no route); then the epoch advances. */
 FGG_API int fgg_moe_sum_peers(const FggMoePeers* peers, int32_t tokens, void* out, void* stream);
 

@@ -417,7 +417,7 @@ struct PeerDev {
   int32_t num_experts;
   int32_t* routes;                       // [capacity] destination ranks per token slot
   int64_t rb;                            // record bytes
-  int64_t gathered_half, recv_half;      // bytes of one buffer half
+  int64_t gathered_half;                 // bytes of one buffer half
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
@@ -430,11 +430,14 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 }
 
 // Called by every thread of every block once its stores are issued: the last
-// block to finish raises this forward's flag of `kind` in every rank.
+// block to finish raises this forward's flag of `kind` in every rank.  The
+// barrier orders the block's stores before thread 0's system-scope fence,
+// whose cumulativity covers them, so one fence per block releases them all
+// (the pattern of a grid-wide barrier, here at system scope).
 __device__ __forceinline__ void signal_peers(const PeerDev& x, int kind, unsigned long long e) {
-  __threadfence_system();  // this thread's stores, to every rank, before the count
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();  // the block's stores, to every rank, before the count
     const unsigned nblocks = gridDim.x * gridDim.y;
     const int prev = atomicAdd(x.counters + kind, 1);
     if (unsigned(prev) == nblocks - 1) {
@@ -483,15 +486,16 @@ __device__ __forceinline__ uint4 reduce_routes(const MoeTok& t, const __nv_bfloa
   return o;
 }
 
-// out[i, :] = the router-weighted sum of token i's local routes (a zero row
-// for a token with none): block (i, y) takes 8 columns a thread, so that many
-// blocks stay resident to hide the row loads' latency.
+// out[i, :] = the router-weighted sum of token i's local routes: block (i, y)
+// takes 8 columns a thread, so that many blocks stay resident to hide the row
+// loads' latency.  A token with no local route gets a zero row, or no row at
+// all with skip_empty (its reader knows, from the routes, not to read it).
 __global__ void __launch_bounds__(256) moe_reduce_kernel(MoeTok t,
                                                          const __nv_bfloat16* __restrict__ rows,
                                                          int32_t num_rows,
                                                          const int32_t* __restrict__ route_row,
                                                          int32_t n, __nv_bfloat16* __restrict__ out,
-                                                         int* __restrict__ bad) {
+                                                         int* __restrict__ bad, int skip_empty) {
   griddep_wait();
   t = resolved(t);
   const int64_t i = blockIdx.x;
@@ -499,39 +503,19 @@ __global__ void __launch_bounds__(256) moe_reduce_kernel(MoeTok t,
   if (i < t.num_tokens && col < n) {
     bool any;
     const uint4 o = reduce_routes(t, rows, num_rows, route_row, n, i, col, bad, &any);
-    *reinterpret_cast<uint4*>(out + i * n + col) = o;
+    if (any || !skip_empty) *reinterpret_cast<uint4*>(out + i * n + col) = o;
   }
 }
 
-// The same sum stored into the token's rank: token slot i's row goes to row
-// rank * capacity + i % capacity of rank i / capacity's recv buffer half,
-// only for a token with a route here (the sum on the token's rank skips the
-// others); the combine flags follow.  A thread takes 8 columns of one token
-// per item and strides over the items (a grid of a few blocks per SM, so
-// that the fence before the signal is paid once per thread, not once per
-// token).
-__global__ void __launch_bounds__(256, 4) moe_reduce_peers_kernel(
-    MoeTok t, const __nv_bfloat16* __restrict__ rows, int32_t num_rows,
-    const int32_t* __restrict__ route_row, int* __restrict__ bad, PeerDev x) {
-  griddep_wait();
-  t = resolved(t);
-  const int n = x.n, chunks = n / 8;
-  const int64_t items = int64_t(t.num_tokens) * chunks;
-  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-  const int64_t par = (*x.epoch + 1) & 1;
-  for (int64_t it = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; it < items; it += stride) {
-    const int64_t i = it / chunks;
-    const int col = int(it - i * chunks) * 8;
-    bool any;
-    const uint4 o = reduce_routes(t, rows, num_rows, route_row, n, i, col, bad, &any);
-    if (any) {
-      const int src = int(i / x.capacity);
-      const int64_t slot = int64_t(x.rank) * x.capacity + i % x.capacity;
-      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(x.recv[src] + par * x.recv_half) +
-                                slot * n + col) = o;
-    }
-  }
-  signal_peers(x, 1, (unsigned long long)(*x.epoch + 1));
+// One thread raises this forward's flag of `kind` in every rank, after the
+// kernels before it on the stream: their writes to this GPU's memory are
+// complete when it starts, and the fence orders them before the flags that
+// peers acquire (a peer reads this GPU's memory through this GPU's L2).
+__global__ void moe_signal_peers_kernel(PeerDev x, int kind) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long e = (unsigned long long)(*x.epoch + 1);
+  __threadfence_system();
+  for (int s = 0; s < x.world; ++s) st_release_sys(x.flags[s] + kind * kPeersMax + x.rank, e);
 }
 
 // Dispatch over peer memory: `parts` warps per token slot of this rank (1 to
@@ -643,29 +627,26 @@ __global__ void moe_wait_peers_kernel(PeerDev x, int kind) {
   }
 }
 
-// out[i, :] = bf16(sum_s recv[s * capacity + i, :]) over the ranks s in
-// routes[i] (the others sent no row), from this rank's half of this
-// forward: a thread per 8 columns of a token, all its loads issued before
-// the sums, striding over the items.  The last block to finish advances the
-// epoch.
-__global__ void __launch_bounds__(256, 4) moe_sum_peers_kernel(PeerDev x, int32_t tokens,
+// out[i, :] = bf16(sum_s recv_s[rank * capacity + i, :]) over the ranks s
+// in routes[i], in rank order (the others hold no row for the token): the
+// partial rows are read where they were computed, over NVLink for s != rank.
+// Block (i, y) takes 8 columns a thread and issues its loads from every
+// source before it sums.  The last block to finish advances the epoch.
+__global__ void __launch_bounds__(256) moe_sum_peers_kernel(PeerDev x, int32_t tokens,
                                                             __nv_bfloat16* __restrict__ out) {
   griddep_wait();
-  const int64_t par = (*x.epoch + 1) & 1;
-  const __nv_bfloat16* parts =
-      reinterpret_cast<const __nv_bfloat16*>(x.recv[x.rank] + par * x.recv_half);
-  const int n = x.n, chunks = n / 8;
-  const int64_t items = int64_t(tokens) * chunks;
-  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
-  for (int64_t it = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; it < items; it += stride) {
-    const int64_t i = it / chunks;
-    const int col = int(it - i * chunks) * 8;
+  const int n = x.n;
+  const int64_t i = blockIdx.x;
+  const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (i < tokens && col < n) {
     const unsigned mask = unsigned(x.routes[i]);
+    const int64_t row = int64_t(x.rank) * x.capacity + i;
     uint4 v[kPeersMax];
 #pragma unroll
     for (int s = 0; s < kPeersMax; ++s)
       if (s < x.world && ((mask >> s) & 1u))
-        v[s] = *reinterpret_cast<const uint4*>(parts + (int64_t(s) * x.capacity + i) * n + col);
+        v[s] = *reinterpret_cast<const uint4*>(
+            reinterpret_cast<const __nv_bfloat16*>(x.recv[s]) + row * n + col);
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
@@ -688,7 +669,7 @@ __global__ void __launch_bounds__(256, 4) moe_sum_peers_kernel(PeerDev x, int32_
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (unsigned(atomicAdd(x.counters + 2, 1)) == gridDim.x - 1) {
+    if (unsigned(atomicAdd(x.counters + 2, 1)) == gridDim.x * gridDim.y - 1) {
       x.counters[2] = 0;
       *x.epoch = *x.epoch + 1;  // every block of this forward has read it
     }
@@ -763,12 +744,6 @@ bool rows_vec4(const MoeTok& t) {
          (t.k / 16) % 4 == 0;
 }
 
-// Blocks of 256 threads for a grid-stride kernel over `items` (one thread
-// each): at most per_sm per SM, as many as the kernel's launch bounds keep
-// resident at once, at least 1.
-int stride_grid(int64_t items, int sm_count, int per_sm) {
-  return int(std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, int64_t(sm_count) * per_sm)));
-}
 
 }  // namespace
 }  // namespace fgg
@@ -862,7 +837,6 @@ int to_peers(const FggMoePeers* p, int64_t rb, PeerDev* x) {
   x->routes = p->routes;
   x->rb = rb;
   x->gathered_half = int64_t(p->world) * p->capacity * rb;
-  x->recv_half = int64_t(p->world) * p->capacity * p->n * 2;
   return FGG_OK;
 }
 
@@ -923,12 +897,13 @@ int fgg_moe_reduce_peers(const void* rows, int32_t num_rows, const int32_t* rout
   if (route_row == nullptr || bad == nullptr || (num_rows > 0 && rows == nullptr))
     return set_error(FGG_EINVAL, "null pointer");
   if (!aligned16(rows)) return set_error(FGG_EALIGN, "rows must be 16-byte aligned");
-  DeviceInfo dev;
-  if (int rc = current_device(&dev)) return rc;
-  const int grid = stride_grid(int64_t(t.num_tokens) * (x.n / 8), dev.sm_count, 4);
-  FGG_CUDA_CHECK(launch_pdl(moe_reduce_peers_kernel, dim3(grid), dim3(256), 0,
-                            reinterpret_cast<cudaStream_t>(stream), t,
-                            static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, bad, x));
+  const dim3 grid(unsigned(t.num_tokens), unsigned((x.n / 8 + 255) / 256));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // the partial rows stay in this rank's memory; their tokens' ranks read them
+  FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel, grid, dim3(256), 0, s, t,
+                            static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, x.n,
+                            reinterpret_cast<__nv_bfloat16*>(x.recv[x.rank]), bad, 1));
+  moe_signal_peers_kernel<<<1, 32, 0, s>>>(x, 1);
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }
@@ -940,11 +915,9 @@ int fgg_moe_sum_peers(const FggMoePeers* peers, int32_t tokens, void* out, void*
     return set_error(FGG_EBADSHAPE, "tokens=%d outside [0, capacity=%d]", tokens, x.capacity);
   if (out == nullptr && tokens > 0) return set_error(FGG_EINVAL, "out is null");
   if (tokens > 0 && !aligned16(out)) return set_error(FGG_EALIGN, "out must be 16-byte aligned");
-  DeviceInfo dev;
-  if (int rc = current_device(&dev)) return rc;
   // at least one block even for zero tokens: the last block advances the epoch
-  const int grid = stride_grid(int64_t(tokens) * (x.n / 8), dev.sm_count, 4);
-  FGG_CUDA_CHECK(launch_pdl(moe_sum_peers_kernel, dim3(grid), dim3(256), 0,
+  const dim3 grid(unsigned(std::max(tokens, 1)), unsigned((x.n / 8 + 255) / 256));
+  FGG_CUDA_CHECK(launch_pdl(moe_sum_peers_kernel, grid, dim3(256), 0,
                             reinterpret_cast<cudaStream_t>(stream), x, tokens,
                             static_cast<__nv_bfloat16*>(out)));
   FGG_CUDA_CHECK(cudaGetLastError());
@@ -1013,7 +986,7 @@ int fgg_moe_reduce(const void* rows, int32_t num_rows, const int32_t* route_row,
   FGG_CUDA_CHECK(launch_pdl(moe_reduce_kernel, grid, dim3(256), 0,
                             reinterpret_cast<cudaStream_t>(stream), t,
                             static_cast<const __nv_bfloat16*>(rows), num_rows, route_row, n,
-                            static_cast<__nv_bfloat16*>(out), bad));
+                            static_cast<__nv_bfloat16*>(out), bad, 0));
   FGG_CUDA_CHECK(cudaGetLastError());
   return FGG_OK;
 }

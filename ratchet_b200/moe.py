@@ -155,7 +155,7 @@ class ExpertParallelMoE:
     with NCCL collectives; "p2p" with the library's own kernels, which store
     them straight into the other ranks' buffers over NVLink (peer memory
     mapped through CUDA IPC, epoch-tagged arrival flags, bounded waits),
-    fuse the exchange with the packing and the weighted reduce, and move a
+    fuse the exchange with the packing and the final sum, and move a
     token's record and partial row only to and from the ranks that own one
     of its experts; call release() before destroying the process group.
     """
@@ -276,7 +276,8 @@ class ExpertParallelMoE:
         L = _lib.lib()
         W, n, dev = self.world, self.n, self.device
         rb = int(L.fgg_moe_record_bytes(self.k, topk))
-        sizes = (2 * W * C * rb, 2 * W * C * n * 2, 2 * _lib.FGG_PEERS_MAX * 8)
+        # records (two halves), partial rows (one), arrival flags
+        sizes = (2 * W * C * rb, W * C * n * 2, 2 * _lib.FGG_PEERS_MAX * 8)
         own = []
         hb = int(L.fgg_peer_handle_bytes())
         handles = []
@@ -430,9 +431,11 @@ class ExpertParallelMoE:
         return out
 
     def _forward_peers(self, b, mine, T, mark, stream):
-        """Steps 1-6 over peer memory: the dispatch kernel stores every
-        record in every rank, the reduce kernel stores each partial row in
-        its token's rank, bounded waits on the arrival flags between."""
+        """Steps 1-6 over peer memory: the dispatch kernel stores each record
+        in the ranks that own one of its experts, the reduce kernel writes the
+        partial rows into this rank's own return buffer and the sum kernel
+        reads a token's partial rows from the ranks that computed them, with
+        bounded waits on the arrival flags between."""
         L = _lib.lib()
         E, n, dev = self.local, self.n, self.device
         peers, toks = b["peers"], b["gathered_view"]

@@ -128,7 +128,7 @@ def test_peer_wait_gives_up_and_reports(cuda_device):
     C, n = 4, 64
     rb = int(L.fgg_moe_record_bytes(K, TOPK))
     gathered = [torch.zeros(2 * 2 * C * rb, dtype=torch.uint8, device=cuda_device) for _ in range(2)]
-    recv = [torch.zeros(2 * 2 * C * n, dtype=torch.bfloat16, device=cuda_device) for _ in range(2)]
+    recv = [torch.zeros(2 * C * n, dtype=torch.bfloat16, device=cuda_device) for _ in range(2)]
     flags = [torch.zeros(2 * _lib.FGG_PEERS_MAX, dtype=torch.int64, device=cuda_device)
              for _ in range(2)]
     state = torch.zeros(4, dtype=torch.int64, device=cuda_device)
