@@ -361,8 +361,8 @@ FGG_API int fgg_moe_sum_partials(const void* parts, int32_t world, int32_t per_s
  * multicast), fused with the byte work on either side of the exchange.
  * Arrival is signalled by epoch-tagged flags in each destination's memory,
  * written with release semantics after the data; every wait for them is
- * bounded (about one second), after which the waiter sets *status = 0x301
- * and returns (its data is then incomplete).  The dispatch buffer is double
+ * bounded (wait_ms, default 10 s), after which the waiter sets
+ * *status = 0x301 and returns (its data is then incomplete).  The dispatch buffer is double
  * buffered on the forward's epoch parity, so one forward's stores never
  * touch the half a slower peer still reads.  The combine pulls: each rank
  * writes its partial rows into its own return buffer and each token's rank
@@ -395,6 +395,8 @@ typedef struct FggMoePeers {
   const int32_t* owner;      /* [num_experts] rank of each expert (device) */
   int32_t num_experts;
   int32_t* routes;           /* [capacity] destination ranks of each token, bit mask */
+  int32_t wait_ms;           /* limit of each flag wait; 0 = 10000 (the waits span the
+                                other ranks' host work as well as their kernels) */
 } FggMoePeers;
 
 FGG_API int fgg_peer_alloc(size_t bytes, void** ptr);

@@ -70,7 +70,8 @@ class FggMoePeers(ctypes.Structure):
                 ("n", ctypes.c_int32), ("epoch", _VOIDP), ("counters", _VOIDP), ("status", _VOIDP),
                 ("gathered", _VOIDP * FGG_PEERS_MAX), ("recv", _VOIDP * FGG_PEERS_MAX),
                 ("flags", _VOIDP * FGG_PEERS_MAX), ("owner", _VOIDP),
-                ("num_experts", ctypes.c_int32), ("routes", _VOIDP)]
+                ("num_experts", ctypes.c_int32), ("routes", _VOIDP),
+                ("wait_ms", ctypes.c_int32)]
 
 
 class FggError(RuntimeError):

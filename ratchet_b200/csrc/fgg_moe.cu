@@ -404,6 +404,9 @@ __global__ void __launch_bounds__(256)
 // ---- peer exchange (see fgg_api.h): buffers mapped from the other ranks ----
 constexpr int kPeersMax = FGG_PEERS_MAX;
 constexpr int kStatusPeerTimeout = 0x301;
+// A peer's flag waits on the other ranks' hosts too (their launches of the
+// same forward), so its default limit is longer than a kernel-internal wait's.
+constexpr int32_t kPeerWaitDefaultMs = 10000;
 
 struct PeerDev {
   int32_t world, rank, capacity, n;
@@ -416,6 +419,7 @@ struct PeerDev {
   const int32_t* owner;                  // [num_experts] rank of each expert
   int32_t num_experts;
   int32_t* routes;                       // [capacity] destination ranks per token slot
+  uint64_t wait_ns;                      // limit of each wait on the peers' flags
   int64_t rb;                            // record bytes
   int64_t gathered_half;                 // bytes of one buffer half
 };
@@ -610,8 +614,8 @@ __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerD
 }
 
 // Bounded wait (one thread) until every rank's flag of `kind` in this rank's
-// memory carries this forward's epoch; gives up after about one second with
-// status 0x301.
+// memory carries this forward's epoch; gives up after wait_ns with status
+// 0x301.
 __global__ void moe_wait_peers_kernel(PeerDev x, int kind) {
   if (threadIdx.x != 0) return;
   const unsigned long long e = (unsigned long long)(*x.epoch + 1);
@@ -619,7 +623,7 @@ __global__ void moe_wait_peers_kernel(PeerDev x, int kind) {
   const uint64_t t0 = globaltimer();
   for (int s = 0; s < x.world; ++s) {
     while (ld_acquire_sys(f + s) < e) {
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > x.wait_ns) {
         atomicCAS(x.status, 0, kStatusPeerTimeout);
         return;
       }
@@ -832,6 +836,8 @@ int to_peers(const FggMoePeers* p, int64_t rb, PeerDev* x) {
     x->recv[s] = static_cast<uint8_t*>(p->recv[s]);
     x->flags[s] = static_cast<unsigned long long*>(p->flags[s]);
   }
+  if (p->wait_ms < 0) return set_error(FGG_EINVAL, "wait_ms is negative");
+  x->wait_ns = uint64_t(p->wait_ms > 0 ? p->wait_ms : kPeerWaitDefaultMs) * 1000000ull;
   x->owner = p->owner;
   x->num_experts = p->num_experts;
   x->routes = p->routes;

@@ -182,6 +182,7 @@ def _peers(world=2, rank=0, capacity=4, n=64, base=0x10000, flag_off=0):
             p.recv[r] = base + 0x100000 * (r + 1)
             p.flags[r] = base + 0x200 + 0x100 * r + flag_off
     p.owner, p.num_experts, p.routes = base + 0x800, 8, base + 0x900
+    p.wait_ms = 0
     return p
 
 
@@ -228,3 +229,11 @@ def test_peer_handles_validated(L):
     assert L.fgg_peer_import(None, ctypes.byref(ctypes.c_void_p())) == _lib.FGG_EINVAL
     assert L.fgg_peer_free(None) == _lib.FGG_OK
     assert L.fgg_peer_close(None) == _lib.FGG_OK
+
+
+def test_peer_wait_limit_validated(L):
+    import ctypes
+
+    p = _peers()
+    p.wait_ms = -1
+    assert L.fgg_moe_wait_peers(ctypes.byref(p), 0, None) == _lib.FGG_EINVAL

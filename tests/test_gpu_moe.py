@@ -56,9 +56,11 @@ def _check(layer, rank, T, dev, w_all):
     ids[3, 2] = -1  # an absent route
     args = (torch.from_numpy(xc).to(dev), torch.from_numpy(xs).to(dev).view(torch.float8_e4m3fn),
             float(xg), torch.from_numpy(ids).to(dev))
+    # both forwards before the oracle's host work, so that ranks with more
+    # tokens do not fall behind between two collective forwards
     got = layer.forward(*args)
-    ok, st = ref.check_close(got.cpu().float(), _expected(xc, xs, xg, ids, w_all).float())
     summed = layer.forward(*args, torch.from_numpy(w).to(dev))
+    ok, st = ref.check_close(got.cpu().float(), _expected(xc, xs, xg, ids, w_all).float())
     ok2, st2 = ref.check_close(summed.cpu().float(), _expected(xc, xs, xg, ids, w_all, w).float())
     layer.check()
     return ok and ok2, (st, st2)
@@ -118,8 +120,8 @@ def test_moe_world1_peer_transport(cuda_device):
 def test_peer_wait_gives_up_and_reports(cuda_device):
     """A wait on a flag that nothing sets: a two-rank description whose second
     rank's buffers are plain local memory that no kernel signals.  The wait
-    kernel gives up after its time limit with status 0x301 in the status
-    word, returns, and the device stays usable."""
+    kernel gives up after its time limit (200 ms here) with status 0x301 in
+    the status word, returns, and the device stays usable."""
     import ctypes
 
     from ratchet_b200 import _lib
@@ -136,6 +138,7 @@ def test_peer_wait_gives_up_and_reports(cuda_device):
     routes = torch.zeros(C, dtype=torch.int32, device=cuda_device)
     p = _lib.FggMoePeers()
     p.owner, p.num_experts, p.routes = owner.data_ptr(), E, routes.data_ptr()
+    p.wait_ms = 200  # a short limit: nothing will ever set the second rank's flag
     p.world, p.rank, p.capacity, p.n = 2, 0, C, n
     base = state.data_ptr()
     p.epoch, p.counters, p.status = base, base + 8, base + 20
@@ -267,6 +270,9 @@ def _nccl_worker(rank, world, port, result_dir):
         peer = _layer(w_all, owner, slot, rank, dev, max_tokens=300, transport="p2p")
         ok3, st3 = True, []
         for _ in range(2):
+            # the oracle's host work takes longer on the ranks with more tokens;
+            # line the ranks up so that no flag wait spans it
+            dist.barrier()
             o, s3 = _check(peer, rank, 120 + 23 * rank, dev, w_all)
             ok3, st3 = ok3 and o, st3 + [s3]
         ok4 = _graph_matches_eager(peer, rank, 100 + 25 * rank, dev)
