@@ -522,22 +522,20 @@ __global__ void moe_signal_peers_kernel(PeerDev x, int kind) {
   for (int s = 0; s < x.world; ++s) st_release_sys(x.flags[s] + kind * kPeersMax + x.rank, e);
 }
 
-// Dispatch over peer memory: `parts` warps per token slot of this rank (1 to
-// kDispatchParts, more when there are few slots), each moving one part of
-// the slot's record, so that even a few hundred slots keep every SM storing.  Each warp finds the ranks that own one of
-// the token's experts (a bit mask; part 0 keeps it in routes[j]) and writes
-// its part of the record into those ranks' gathered buffer halves; part 0
-// also writes the expert ids, router weights and decode scale, and gives
-// every other rank's slot expert ids -1 only, as it does for slots past the
-// rank's tokens.  The codes and scales are contiguous in a record, so
-// 16-byte piece q of the record comes from the codes (q < K/32) or the
-// scales; a lane loads up to kDispatchBatch pieces before it stores any.
-// The dispatch flags follow.
+// Dispatch over peer memory: one warp per (token slot of this rank,
+// destination rank), so the stores to different ranks proceed in parallel
+// and even a few hundred slots keep every SM storing.  Each warp finds the
+// ranks that own one of the token's experts (a bit mask; the warp of this
+// rank keeps it in routes[j]).  If its destination is among them it writes
+// the whole record there (codes, scales, expert ids, router weights, decode
+// scale), otherwise only expert ids -1, as for slots past the rank's tokens.
+// The codes and scales are contiguous in a record, so 16-byte piece q of the
+// record comes from the codes (q < K/32) or the scales; a lane loads up to
+// kDispatchBatch pieces before it stores any.  The dispatch flags follow.
 constexpr int kDispatchBatch = 8;
-constexpr int kDispatchParts = 4;
 
 template <bool kVec>
-__global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerDev x, int parts) {
+__global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerDev x) {
   using V = typename std::conditional<kVec, uint4, uint32_t>::type;
   constexpr int kB = int(sizeof(V));
   const unsigned long long e = (unsigned long long)(*x.epoch + 1);
@@ -546,12 +544,14 @@ __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerD
   const int kh = t.k / 2, ks = t.k / 16;
   const int nc = kh / kB, np = (kh + ks) / kB;  // pieces: codes, then all
   const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-  const int64_t items = int64_t(x.capacity) * parts;
+  const int64_t items = int64_t(x.capacity) * x.world;
   for (int64_t w = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < items;
        w += warps) {  // warp-uniform
-    const int64_t j = w / parts;
-    const int part = int(w - j * parts);
-    const int64_t off = par * x.gathered_half + (int64_t(x.rank) * x.capacity + j) * x.rb;
+    const int64_t j = w / x.world;
+    const int dst = int(w - j * x.world);
+    uint8_t* const rec = x.gathered[dst] + par * x.gathered_half +
+                         (int64_t(x.rank) * x.capacity + j) * x.rb;
+    int32_t* const ids = reinterpret_cast<int32_t*>(rec + kh + ks);
     unsigned bit = 0;
     if (j < t.num_tokens) {
       for (int k = lane; k < t.topk; k += 32) {
@@ -563,52 +563,32 @@ __global__ void __launch_bounds__(256) moe_dispatch_peers_kernel(MoeTok t, PeerD
       }
     }
     const unsigned mask = __reduce_or_sync(0xffffffffu, bit);
-    if (mask != 0) {
-      const V* codes = reinterpret_cast<const V*>(t.codes + j * t.codes_stride);
-      const V* sf = reinterpret_cast<const V*>(t.sf + j * t.sf_stride);
-      const int q0 = int(int64_t(np) * part / parts);
-      const int q1 = int(int64_t(np) * (part + 1) / parts);
-      for (int base = q0; base < q1; base += 32 * kDispatchBatch) {
-        V v[kDispatchBatch];
+    if (dst == x.rank && lane == 0) x.routes[j] = int32_t(mask);
+    if (!((mask >> dst) & 1u)) {
+      for (int k = lane; k < t.topk; k += 32) ids[k] = -1;
+      continue;
+    }
+    const V* codes = reinterpret_cast<const V*>(t.codes + j * t.codes_stride);
+    const V* sf = reinterpret_cast<const V*>(t.sf + j * t.sf_stride);
+    V* out = reinterpret_cast<V*>(rec);
+    for (int base = 0; base < np; base += 32 * kDispatchBatch) {
+      V v[kDispatchBatch];
 #pragma unroll
-        for (int u = 0; u < kDispatchBatch; ++u) {
-          const int q = base + u * 32 + lane;
-          if (q < q1) v[u] = q < nc ? __ldg(codes + q) : __ldg(sf + (q - nc));
-        }
-        for (int s = 0; s < x.world; ++s) {
-          if (!((mask >> s) & 1u)) continue;
-          V* dst = reinterpret_cast<V*>(x.gathered[s] + off);
+      for (int u = 0; u < kDispatchBatch; ++u) {
+        const int q = base + u * 32 + lane;
+        if (q < np) v[u] = q < nc ? __ldg(codes + q) : __ldg(sf + (q - nc));
+      }
 #pragma unroll
-          for (int u = 0; u < kDispatchBatch; ++u) {
-            const int q = base + u * 32 + lane;
-            if (q < q1) dst[q] = v[u];
-          }
-        }
+      for (int u = 0; u < kDispatchBatch; ++u) {
+        const int q = base + u * 32 + lane;
+        if (q < np) out[q] = v[u];
       }
     }
-    if (part != 0) continue;
-    if (lane == 0) x.routes[j] = int32_t(mask);
-    if (mask != 0) {
-      for (int k = lane; k < t.topk; k += 32) {
-        const int32_t id = tok_id(t, j, k);
-        const float wt = tok_weight(t, j, k);
-        for (int s = 0; s < x.world; ++s) {
-          if (!((mask >> s) & 1u)) continue;
-          int32_t* ids = reinterpret_cast<int32_t*>(x.gathered[s] + off + kh + ks);
-          ids[k] = id;
-          reinterpret_cast<float*>(ids + t.topk)[k] = wt;
-        }
-      }
-      if (lane == 0) {
-        const float sc = tok_scale(t, j);
-        for (int s = 0; s < x.world; ++s)
-          if ((mask >> s) & 1u)
-            reinterpret_cast<float*>(x.gathered[s] + off + kh + ks)[2 * t.topk] = sc;
-      }
+    for (int k = lane; k < t.topk; k += 32) {
+      ids[k] = tok_id(t, j, k);
+      reinterpret_cast<float*>(ids + t.topk)[k] = tok_weight(t, j, k);
     }
-    for (int k = lane; k < t.topk; k += 32)
-      for (int s = 0; s < x.world; ++s)
-        if (!((mask >> s) & 1u)) reinterpret_cast<int32_t*>(x.gathered[s] + off + kh + ks)[k] = -1;
+    if (lane == 0) reinterpret_cast<float*>(ids + 2 * t.topk)[0] = tok_scale(t, j);
   }
   signal_peers(x, 0, e);
 }
@@ -864,17 +844,14 @@ int fgg_moe_dispatch_peers(const FggMoeTokens* tokens, const FggMoePeers* peers,
     return set_error(FGG_EINVAL, "codes / sf is null");
   DeviceInfo dev;
   if (int rc = current_device(&dev)) return rc;
-  // 8 warps a block; a token slot per warp down to about 2048 slots, then
-  // up to kDispatchParts warps a slot
-  const int parts = int(std::max<int64_t>(1, std::min<int64_t>(kDispatchParts,
-                                                               2048 / std::max(x.capacity, 1))));
-  const int grid = int(std::min<int64_t>((int64_t(x.capacity) * parts + 7) / 8,
+  // 8 warps a block, a warp per (token slot, destination rank)
+  const int grid = int(std::min<int64_t>((int64_t(x.capacity) * x.world + 7) / 8,
                                          int64_t(dev.sm_count) * 8));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (rows_vec16(t) || t.num_tokens == 0)
-    moe_dispatch_peers_kernel<true><<<grid, 256, 0, s>>>(t, x, parts);
+    moe_dispatch_peers_kernel<true><<<grid, 256, 0, s>>>(t, x);
   else if (rows_vec4(t))
-    moe_dispatch_peers_kernel<false><<<grid, 256, 0, s>>>(t, x, parts);
+    moe_dispatch_peers_kernel<false><<<grid, 256, 0, s>>>(t, x);
   else
     return set_error(FGG_EALIGN, "token rows must start on 4-byte boundaries");
   FGG_CUDA_CHECK(cudaGetLastError());
