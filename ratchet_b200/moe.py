@@ -158,12 +158,14 @@ class ExpertParallelMoE:
     fuse the exchange with the packing and the final sum, and move a
     token's record and partial row only to and from the ranks that own one
     of its experts; call release() before destroying the process group.
+    wait_ms: the limit of each wait on the other ranks' flags (0: the
+    library's default, 10 s); a wait that runs out makes check() raise.
     """
 
     def __init__(self, w_codes: Sequence[torch.Tensor], w_sf: Sequence[torch.Tensor],
                  w_scale: Sequence, owner: np.ndarray, slot: np.ndarray, group=None,
                  gemm_fn: GemmFn | None = None, max_tokens: int | None = None,
-                 combine: str = "a2a", transport: str = "nccl"):
+                 combine: str = "a2a", transport: str = "nccl", wait_ms: int = 0):
         import torch.distributed as dist
 
         self.group = group
@@ -199,6 +201,9 @@ class ExpertParallelMoE:
             raise ValueError(f"the peer exchange spans at most {_lib.FGG_PEERS_MAX} ranks")
         self.combine = combine
         self.transport = transport
+        if wait_ms < 0:
+            raise ValueError("wait_ms must be >= 0 (0: the library's default)")
+        self.wait_ms = int(wait_ms)
         self._peer_own = []      # buffers this rank allocated (freed by release)
         self._peer_mapped = []   # other ranks' buffers mapped here (closed by release)
         self.topk = None
@@ -281,30 +286,42 @@ class ExpertParallelMoE:
         own = []
         hb = int(L.fgg_peer_handle_bytes())
         handles = []
-        with torch.cuda.device(dev):
-            for nbytes in sizes:
-                p = ctypes.c_void_p()
-                _lib.check(L.fgg_peer_alloc(nbytes, ctypes.byref(p)), "fgg_peer_alloc")
-                own.append(p.value)
-                self._peer_own.append(p.value)
-                h = ctypes.create_string_buffer(hb)
-                _lib.check(L.fgg_peer_export(p.value, h), "fgg_peer_export")
-                handles.append(h.raw)
-        everyone = [handles]
-        if W > 1:
-            everyone = [None] * W
-            dist.all_gather_object(everyone, handles, group=self.group)
-        ptrs = [[0] * W for _ in sizes]
-        with torch.cuda.device(dev):
-            for r in range(W):
-                for i in range(len(sizes)):
-                    if r == self.rank:
-                        ptrs[i][r] = own[i]
-                        continue
-                    q = ctypes.c_void_p()
-                    _lib.check(L.fgg_peer_import(everyone[r][i], ctypes.byref(q)), "fgg_peer_import")
-                    self._peer_mapped.append(q.value)
-                    ptrs[i][r] = q.value
+        try:
+            with torch.cuda.device(dev):
+                for nbytes in sizes:
+                    p = ctypes.c_void_p()
+                    _lib.check(L.fgg_peer_alloc(nbytes, ctypes.byref(p)), "fgg_peer_alloc")
+                    own.append(p.value)
+                    self._peer_own.append(p.value)
+                    h = ctypes.create_string_buffer(hb)
+                    _lib.check(L.fgg_peer_export(p.value, h), "fgg_peer_export")
+                    handles.append(h.raw)
+            everyone = [handles]
+            if W > 1:
+                everyone = [None] * W
+                dist.all_gather_object(everyone, handles, group=self.group)
+            ptrs = [[0] * W for _ in sizes]
+            with torch.cuda.device(dev):
+                for r in range(W):
+                    for i in range(len(sizes)):
+                        if r == self.rank:
+                            ptrs[i][r] = own[i]
+                            continue
+                        q = ctypes.c_void_p()
+                        _lib.check(L.fgg_peer_import(everyone[r][i], ctypes.byref(q)),
+                                   "fgg_peer_import")
+                        self._peer_mapped.append(q.value)
+                        ptrs[i][r] = q.value
+        except Exception:
+            # give back what this rank holds (no collective: the others may be
+            # failing too, and their process group ends their part)
+            with torch.cuda.device(dev):
+                for q in self._peer_mapped:
+                    L.fgg_peer_close(q)
+                for q in self._peer_own:
+                    L.fgg_peer_free(q)
+            self._peer_mapped, self._peer_own = [], []
+            raise
         # this rank's own state: epoch (int64), three block counters, status
         b["pstate"] = torch.zeros(4, dtype=torch.int64, device=dev)
         base = b["pstate"].data_ptr()
@@ -319,6 +336,7 @@ class ExpertParallelMoE:
         b["routes"] = torch.zeros(C, dtype=torch.int32, device=dev)
         peers.owner, peers.num_experts = self.owner_d.data_ptr(), self.num_experts
         peers.routes = b["routes"].data_ptr()
+        peers.wait_ms = self.wait_ms
         b["peers"] = peers
         b["rb"] = rb
         toks = _lib.FggMoeTokens()
@@ -585,6 +603,7 @@ class ExpertParallelMoE:
         """Raise if a plan, expand or combine kernel met a bad expert id or
         index, or a bounded wait in the GEMM gave up (synchronises the device)."""
         if self.bufs is not None and "pstate" in self.bufs:
+            # pstate bytes 20-23 (the high half of word 2) hold the status
             st = int(self.bufs["pstate"][2].item() >> 32) & 0xFFFFFFFF
             if st != 0:
                 raise _lib.FggError(_lib.FGG_ETIMEOUT, "ExpertParallelMoE",
