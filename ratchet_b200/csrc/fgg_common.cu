@@ -134,7 +134,7 @@ struct EncodeKey {
   bool operator==(const EncodeKey& o) const { return memcmp(this, &o, sizeof(*this)) == 0; }
 };
 struct EncodeMemo {
-  static constexpr int kEntries = 16;
+  static constexpr int kEntries = 64;
   EncodeKey key[kEntries];
   CUtensorMap map[kEntries];
   bool used[kEntries];

@@ -88,6 +88,9 @@ struct SchedSlot {
 };
 static_assert(sizeof(SchedSlot) == 32, "slot is 8 words");
 
+// Narrow token boxes of the pair kernel: 16, 32, ..., 16 * kXSmallMaps rows.
+constexpr int kXSmallMaps = 6;
+
 struct GemmParams {
   CUtensorMap mx_tmap_w;      // MX: 3-D map of the [G, N, K] weight codes
   // One 2-D map over contiguous token rows: MX [M_total, K] fp8 activations;
@@ -95,6 +98,10 @@ struct GemmParams {
   CUtensorMap tmap_x_flat;
   CUtensorMap sfw_map;        // pair kernel: the weight SF atoms as a 2-D uint64 tensor
   CUtensorMap sfx_map;        // pair kernel: the token SF atoms as a 2-D uint64 tensor
+  // pair kernel, NVFP4 with x_flat and x_small set: maps over the same token
+  // rows as tmap_x_flat with boxes of 16, 32, ..., 96 rows, so that a tile
+  // whose MMA is narrower than 224 columns loads only the rows it uses
+  CUtensorMap tmap_x_small[kXSmallMaps];
   const CUtensorMap* tmap_w;  // NVFP4: [G] per-group maps (global memory)
   const CUtensorMap* tmap_x;  // NVFP4: [G] per-group maps (global memory)
   const uint8_t* sfw;         // [G][NT128][KSTEPS][SFW_BYTES]
@@ -124,6 +131,7 @@ struct GemmParams {
   // optional device word holding the tile count (written by the prepare
   // kernel); null = num_tiles
   const int32_t* num_tiles_dev;
+  int32_t x_small;  // 1: tmap_x_small is encoded (x_flat only)
 };
 
 // Test hook: the producer arms no stage and issues no load, so the MMA role's
@@ -1005,6 +1013,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const int half = tile_ncols(rows) >> 1;
         const CUtensorMap* tw;
         const CUtensorMap* tx;
+        // bytes both CTAs' loads of one K step deliver to the leader's barrier
+        uint32_t tx_step = 2u * C::TX_CTA;
         if constexpr (C::MX) {
           tw = &p.mx_tmap_w;
           tx = &p.tmap_x_flat;
@@ -1013,6 +1023,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           tensormap_acquire(tw);  // every lane: the issuing one among them
           if (p.x_flat) {
             tx = &p.tmap_x_flat;
+            // a narrow tile (half a multiple of 16 below BNH) loads its rows only
+            if (p.x_small && half >= 16 && half < C::BNH) {
+              tx = &p.tmap_x_small[half / 16 - 1];
+              tx_step = 2u * (C::TX_CTA - C::X_BYTES + uint32_t(half) * 128u);
+            }
           } else {
             tx = p.tmap_x + g;
             tensormap_acquire(tx);
@@ -1037,10 +1052,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           if (arm && elect_one()) {
             if (leader) {
               if constexpr (C::KSUB == 1)
-                mbar_arrive_expect_tx(full_bar(stage), 2u * C::TX_CTA);
+                mbar_arrive_expect_tx(full_bar(stage), tx_step);
               else
                 mbar_arrive_expect_tx(full_bar(stage),
-                                      2u * C::TX_CTA * uint32_t(min(C::KSUB, p.ksteps - ks0)));
+                                      tx_step * uint32_t(min(C::KSUB, p.ksteps - ks0)));
             }
 #pragma unroll
             for (int sub = 0; sub < C::KSUB; ++sub) {

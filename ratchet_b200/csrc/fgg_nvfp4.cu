@@ -973,6 +973,12 @@ int fgg_nvfp4_grouped_gemm_rows(const FggNvfp4RowsProblem* p, const void* pack, 
                                  uint64_t(L.xt_cap) * L.nk256 * CfgPair::SFX_BOX_ROWS,
                                  CfgPair::SFX_ROW_U64, CfgPair::SFX_BOX_ROWS))
       return rc;
+    // the narrow token boxes (a tail tile of a group loads only its rows)
+    for (int i = 0; i < kXSmallMaps; ++i)
+      if (int rc = encode_u8_2d(&gp.tmap_x_small[i], p->a, uint64_t(p->k) / 2,
+                                uint64_t(p->max_rows), 128, uint32_t(16 * (i + 1))))
+        return rc;
+    gp.x_small = 1;
     e = launch_pair<CfgPair>(gp, dev.sm_count, s);
   } else if (L.decode) {
     e = launch_engine<CfgDecode>(gp, dev.sm_count, s);
