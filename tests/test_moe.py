@@ -190,3 +190,21 @@ def test_routed_load_is_topk_inclusion():
         by_load = [cnt[moe.place_experts(load, world)[0] == r].sum() for r in range(world)]
         by_pop = [cnt[moe.place_experts(pop, world)[0] == r].sum() for r in range(world)]
         assert max(by_load) / np.mean(by_load) < 1.03 < max(by_pop) / np.mean(by_pop)
+
+
+def test_layer_options_validated():
+    """Bad transport, combine or wait limit names are refused up front."""
+    E, n, k = 4, 16, 64
+    weights_all = _weights(E, n, k, seed=8)
+    owner, slot = moe.place_experts(np.ones(E), 1)
+    mine = [weights_all[e] for e in range(E)]
+    args = ([torch.from_numpy(c) for c, _, _ in mine], [torch.from_numpy(s) for _, s, _ in mine],
+            [float(g) for _, _, g in mine], owner, slot)
+    with pytest.raises(ValueError):
+        moe.ExpertParallelMoE(*args, gemm_fn=_oracle_gemm(mine), transport="shm")
+    with pytest.raises(ValueError):
+        moe.ExpertParallelMoE(*args, gemm_fn=_oracle_gemm(mine), combine="allreduce")
+    with pytest.raises(ValueError):
+        moe.ExpertParallelMoE(*args, gemm_fn=_oracle_gemm(mine), transport="p2p", wait_ms=-1)
+    layer = moe.ExpertParallelMoE(*args, gemm_fn=_oracle_gemm(mine), transport="p2p", wait_ms=250)
+    assert layer.wait_ms == 250 and layer.transport == "p2p"
